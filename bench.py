@@ -1,0 +1,394 @@
+"""Benchmark of the B200 KIVI decode-attention path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload config2]
+                    [--impl kivi|reference]
+
+Default workload = BASELINE config 2 (Llama-3-8B shape decode): B=64 sequences
+per GPU, Hq=32, Hkv=8, D=128, context U[1024, 8192], 16-token pages scattered
+over a shared pool, KIVI INT4 with G=R=128, bf16 q, synthetic seeded data
+(weak scaling: every rank decodes its own 64 sequences, no collective on the
+data path).  A step = one decode-attention call for all sequences of one
+layer.  metric = sequence-tokens/s (B / step time), whole job.
+
+--impl reference times the reference's CPU path for the same workload: the
+CPU restatement of the reference algorithm (oracle/, the reference has no CPU
+implementation of this path) on all host threads, over a bounded sample of the
+sequences.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "KIVI-INT4 paged decode-attn seq-tokens/s (HBM GB/s and % of peak in roofline)"
+UNIT = "seq-tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="config2", choices=["config2", "config4", "config5"])
+    ap.add_argument("--impl", default="kivi", choices=["kivi", "reference"])
+    ap.add_argument("--cpu-sample", type=int, default=8, help="sequences in the CPU sample")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def make_workload(wl, name: str, rank: int):
+    if name == "config2":
+        return wl.config2(seed=1000 + rank)
+    if name == "config4":
+        return wl.config4(seed=4000 + rank)
+    return wl.config5(seed=5000 + rank)
+
+
+# ---------------------------------------------------------------------------
+# cache construction on the GPU (through the public append API)
+# ---------------------------------------------------------------------------
+def build_gpu_cache(ops, w, dev, torch):
+    fmt = ops.KiviFormat(w.D, w.group, w.residual, w.bits, w.Hkv)
+    cache = ops.KiviPagedCache(fmt, w.num_pages, w.B, dev)
+    bt = torch.from_numpy(w.block_tables).to(dev)
+    lens = w.lengths.astype(np.int64)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(w.seed)
+    oc = torch.from_numpy(np.asarray(w.outlier_channels, np.int64)).to(dev)
+    # append in batches of sequences to bound the temporary K/V memory
+    per = max(1, int(2_000_000 // max(1, int(lens.mean()))))
+    for s0 in range(0, w.B, per):
+        s1 = min(w.B, s0 + per)
+        T = int(lens[s0:s1].sum())
+        k = torch.randn((T, w.Hkv, w.D), generator=gen, device=dev, dtype=torch.float32)
+        v = torch.randn((T, w.Hkv, w.D), generator=gen, device=dev, dtype=torch.float32)
+        if len(w.outlier_channels):
+            k[:, :, oc] *= w.outlier_scale
+        k = k.to(torch.bfloat16)
+        v = v.to(torch.bfloat16)
+        cu = torch.zeros(s1 - s0 + 1, dtype=torch.int32)
+        cu[1:] = torch.from_numpy(np.cumsum(lens[s0:s1])).to(torch.int32)
+        zero = torch.zeros(s1 - s0, dtype=torch.int32, device=dev)
+        ops.paged_append(cache, k, v, cu.to(dev), zero, bt[s0:s1].contiguous(),
+                         seq_slots=torch.arange(s0, s1, dtype=torch.int32, device=dev),
+                         max_new_tokens=int(lens[s0:s1].max()))
+        del k, v
+    torch.cuda.synchronize()
+    return cache, bt
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path("/tmp") / f"tkv_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path.exists():
+            return None
+        rows = [r.split(",") for r in self.path.read_text().strip().splitlines() if r.strip()]
+        rows = [[x.strip() for x in r] for r in rows if len(r) >= 7]
+        if not rows:
+            return None
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i] == "Active"})
+        self.path.unlink(missing_ok=True)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def ncu_traffic(workload: str):
+    """Per-launch DRAM traffic of the split kernel from the committed ncu
+    summary (profiles/decode_split_<workload>.json), or None."""
+    p = ROOT / "profiles" / f"decode_split_{workload}.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return d.get("dram_bytes_per_launch")
+
+
+# ---------------------------------------------------------------------------
+# CPU timing of the reference algorithm (oracle restatement)
+# ---------------------------------------------------------------------------
+def cpu_reference_time(O, w, pool_np, ring_np, q_f32, sample, n_threads, repeats=1):
+    st = O.PagedState(w.D, w.group, w.residual, w.bits, w.Hkv, w.num_pages, w.B)
+    st.pool = pool_np
+    st.ring = ring_np
+    idx = np.arange(sample)
+    bt = np.ascontiguousarray(w.block_tables[idx])
+    lens = np.ascontiguousarray(w.lengths[idx])
+    # the ring is indexed by batch row: use the sample's rows 0..sample-1
+    t0 = time.perf_counter()
+    for _ in range(repeats):
+        st.decode(q_f32[idx], bt, lens, 1.0 / math.sqrt(w.D), n_threads=n_threads)
+    return (time.perf_counter() - t0) / repeats
+
+
+def host_cache_for_reference(O, wl, w, sample):
+    """Builds the cache of the first `sample` sequences on the CPU with the
+    oracle append (same seeded distribution as the GPU arm)."""
+    rng = np.random.default_rng(w.seed)
+    st = O.PagedState(w.D, w.group, w.residual, w.bits, w.Hkv, w.num_pages, sample)
+    for b in range(sample):
+        L = int(w.lengths[b])
+        k, v = wl.kv_tokens(rng, L, w.Hkv, w.D, w.outlier_channels, w.outlier_scale)
+        cu = np.zeros(sample + 1, np.int32)
+        cu[b + 1:] = L
+        lens_old = np.zeros(sample, np.int32)
+        st.append(wl.to_bits(k, "bf16"), wl.to_bits(v, "bf16"), True, cu, lens_old,
+                  np.ascontiguousarray(w.block_tables[:sample]))
+    return st
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+    O.build()
+    wl = importlib.import_module("truellm-engine_b200.workloads")
+    w = make_workload(wl, args.workload, 0)
+    sample = min(args.cpu_sample, w.B)
+    st = host_cache_for_reference(O, wl, w, sample)
+    rng = np.random.default_rng(w.seed + 1)
+    q = wl.bits_to_f32(wl.f32_to_bf16_bits(rng.standard_normal((w.B, w.Hq, w.D))), "bf16")
+    threads = os.cpu_count() or 1
+    bt = np.ascontiguousarray(w.block_tables[:sample])
+    lens = np.ascontiguousarray(w.lengths[:sample])
+    for _ in range(max(1, min(args.warmup, 2))):
+        st.decode(q[:sample], bt, lens, 1 / math.sqrt(w.D), n_threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        st.decode(q[:sample], bt, lens, 1 / math.sqrt(w.D), n_threads=threads)
+        times.append(time.perf_counter() - t0)
+    t = float(np.mean(times))
+    value = sample / t
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: sample of {sample} sequences",
+                   "mean_context": float(lens.mean())},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{sample} sequences of {args.workload} (mean context "
+                                   f"{lens.mean():.0f}), fp64 attention over the "
+                                   "dequantised pages, all host threads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_kivi(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    ops = importlib.import_module("truellm-engine_b200.ops")
+    wl = importlib.import_module("truellm-engine_b200.workloads")
+    w = make_workload(wl, args.workload, rank)
+    cache, bt = build_gpu_cache(ops, w, dev, torch)
+    lens = torch.from_numpy(w.lengths).to(dev)
+    rng = np.random.default_rng(w.seed + 1)
+    q_np = wl.f32_to_bf16_bits(rng.standard_normal((w.B, w.Hq, w.D)))
+    q = torch.from_numpy(q_np.view(np.int16)).view(torch.bfloat16).to(dev)
+    out = torch.empty_like(q)
+    max_ctx = int(w.lengths.max())
+    scale = 1.0 / math.sqrt(w.D)
+    S = ops.decode_num_splits(max_ctx)
+    part_ml = torch.empty((S, w.B, w.Hq, 2), dtype=torch.float32, device=dev)
+    part_o = torch.empty((S, w.B, w.Hq, w.D), dtype=torch.float32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(ev=None):
+        # one decode step = split kernel + merge kernel (2 launches)
+        if ev is not None:
+            ev[0].record(stream)
+        ops.paged_decode_partials(cache, q, bt, lens, 0, S - 1, True, part_ml, part_o,
+                                  scale=scale, err=err, stream=stream)
+        if ev is not None:
+            ev[1].record(stream)
+        ops.merge_partials(part_ml, part_o, out, stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            step(evs[i])
+        stop.record(stream)
+        torch.cuda.synchronize()
+    clocks = clk.summary()
+    t_total = start.elapsed_time(stop) / 1e3
+    t_split = float(np.mean([a.elapsed_time(b) for a, b in evs])) / 1e3
+    if int(err.item()) != 0:
+        raise RuntimeError(f"device error flag {int(err.item()):#x}")
+    t_step = t_total / args.steps
+    times = torch.tensor([t_step, t_split], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    t_step, t_split = float(times[0]), float(times[1])
+
+    # ---- end to end through the public API with host buffers ----
+    q_host = torch.from_numpy(q_np.view(np.int16)).view(torch.bfloat16).pin_memory()
+    lens_host = torch.from_numpy(w.lengths.copy()).pin_memory()
+    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    q_dev = torch.empty_like(q)
+    lens_dev = torch.empty_like(lens)
+    ws = torch.empty(ops.decode_workspace_bytes(w.B, w.Hq, w.D, max_ctx), dtype=torch.uint8,
+                     device=dev)
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        lens_dev.copy_(lens_host, non_blocking=True)
+        ops.paged_decode(cache, q_dev, bt, lens_dev, max_ctx, scale=scale, out=out,
+                         workspace=ws, err=err, stream=stream)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_e2e = torch.tensor([e0.elapsed_time(e1) / 1e3 / args.steps], dtype=torch.float64,
+                         device=dev)
+    if world > 1:
+        dist.all_reduce(t_e2e, op=dist.ReduceOp.MAX)
+    t_e2e = float(t_e2e[0])
+    h2d = q_host.numel() * 2 + lens_host.numel() * 4
+    d2h = out_host.numel() * 2
+
+    alg_bytes = wl.decode_algorithmic_bytes(w)  # per launch of the split kernel (+ q/out)
+    peak, peak_kind = peaks()
+    achieved = alg_bytes / t_split / 1e9
+    traffic = ncu_traffic(args.workload)
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1:
+            try:
+                from oracle import oracle as O
+                O.build()
+                sample = min(args.cpu_sample, w.B)
+                pool_np = cache.pool.cpu().numpy()
+                ring_np = cache.ring.cpu().numpy().view(np.uint16)
+                qf = q.float().cpu().numpy()
+                threads = os.cpu_count() or 1
+                tc = cpu_reference_time(O, w, pool_np, ring_np, qf, sample, threads)
+                cpu = {"value": sample / tc, "unit": UNIT, "cores": threads, "kind": "port",
+                       "sample": f"{sample} of the {w.B} sequences (mean context "
+                                 f"{w.lengths[:sample].mean():.0f}), CPU restatement of the "
+                                 "reference algorithm (fp64), all host threads"}
+            except Exception as e:  # the baseline is reported, never required
+                cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                       "sample": f"failed: {e!r}"[:200]}
+        line = {
+            "metric": METRIC, "value": world * w.B / t_step, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4/bf16",
+            "data": "synthetic (seeded N(0,1) K/V, 2% key outlier channels x8)",
+            "config": {"workload": f"{args.workload}: B={w.B}/GPU Hq={w.Hq} Hkv={w.Hkv} D={w.D} "
+                                   f"L~U[1024,8192] G={w.group} R={w.residual} INT{w.bits}",
+                       "global_batch": world * w.B, "mean_context": float(w.lengths.mean()),
+                       "parallelism": f"sequence-sharded x{world}",
+                       "l2": "inputs larger than L2 (cache %.0f MB)" % (alg_bytes / 1e6)},
+            "gpu_launches": 2 * args.steps,
+            "e2e": {"value": world * w.B / t_e2e, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": traffic, "kernel": "decode_split_kernel<128,4,1>",
+                         "alg_bytes_per_launch": alg_bytes,
+                         "kernel_ms": t_split * 1e3},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_kivi(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

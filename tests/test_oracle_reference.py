@@ -1,0 +1,155 @@
+"""CPU oracle of the reference-format KIVI quantizer, pinned against the
+reference's own tests (tests/unit/inference/cuda/test_kivi_bounds.cpp,
+test_kivi_roundtrip.cpp), hand-computed known answers, and golden vectors
+produced by the reference kernel itself (tests/golden/, see make_golden.py).
+"""
+import numpy as np
+import pytest
+
+from pathlib import Path
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def f16(x):
+    return np.asarray(x, dtype=np.float32).astype(np.float16).view(np.uint16)
+
+
+def h2f(b):
+    return np.asarray(b, dtype=np.uint16).view(np.float16).astype(np.float32)
+
+
+# ---- test_kivi_bounds.cpp:25-30 ----
+def test_compressed_bytes_matches_layout(O, ops):
+    for mod in (O, ops):
+        assert mod.kivi_compressed_bytes(128, 8, 16) == 24 + 8 * 12
+        assert mod.kivi_compressed_bytes(64, 0, 16) == 4 * 12
+        assert mod.kivi_compressed_bytes(64, 64, 16) == 64 * 3
+
+
+# ---- test_kivi_bounds.cpp:35-57 ----
+def test_params_supported_grid(O, ops):
+    for mod in (O, ops):
+        assert mod.kivi_params_supported(128, 8, 16)
+        assert mod.kivi_params_supported(64, 4, 16)
+        assert mod.kivi_params_supported(128, 64, 16)
+        assert not mod.kivi_params_supported(129, 8, 16)
+        assert not mod.kivi_params_supported(128, 65, 16)
+        assert not mod.kivi_params_supported(16, 32, 16)
+        assert not mod.kivi_params_supported(128, 8, 0)
+        assert not mod.kivi_params_supported(128, 8, -4)
+        assert not mod.kivi_params_supported(0, 0, 16)
+        assert not mod.kivi_params_supported(-1, 0, 16)
+
+
+# ---- test_kivi_bounds.cpp:65-69 ----
+def test_constants(ops):
+    assert ops.KIVI_MAX_HEAD_DIM == 128
+    assert ops.KIVI_MAX_OUTLIERS == 64
+
+
+# ---- hand-computed known answers ----
+def test_known_answer_single_group(O):
+    # [0,1,2,3], G=4: range 3, scale 15/3 = 5, codes 0,5,10,15;
+    # step = 1/5 -> fp16 0x3266, zero = 0 -> 0x0000
+    rec = O.kivi_compress(f16([[0, 1, 2, 3]]), 0, 4)
+    assert rec.tolist() == [[0x50, 0xFA, 0x66, 0x32, 0x00, 0x00]]
+
+
+def test_known_answer_outlier_slot_order(O):
+    # |x| = 1 5 3 7 2 9 4 6 with 2 slots: ch0->s0, ch1->s1, ch2->s0, ch3->s0,
+    # ch5->s1  => slots [3, 5] (slot order is not channel order for 7 vs 9)
+    x = f16([[1, -5, 3, 7, -2, 9, 4, 6]])
+    rec = O.kivi_compress(x, 2, 6)
+    assert rec[0, 0] == 3 and rec[0, 3] == 5
+    assert rec[0, 1:3].view(np.uint16)[0] == x[0, 3]
+    assert rec[0, 4:6].view(np.uint16)[0] == x[0, 5]
+    # residual channels 0,1,2,4,6,7 -> values 1,-5,3,-2,4,6: min -5, max 6
+    codes = rec[0, 6:9]
+    q = np.array([codes[0] & 15, codes[0] >> 4, codes[1] & 15, codes[1] >> 4, codes[2] & 15,
+                  codes[2] >> 4])
+    scale = np.float32(15) / np.float32(11)
+    vals = np.array([1, -5, 3, -2, 4, 6], dtype=np.float32)
+    expect = np.clip(np.rint((vals + np.float32(5)) * scale), 0, 15)
+    assert q.tolist() == expect.astype(int).tolist()
+
+
+def test_known_answer_round_half_even(O):
+    # range 15 -> scale 1: (x - min) = 0.5, 1.5, 2.5 round to 0, 2, 2 (half to even)
+    rec = O.kivi_compress(f16([[0, 0.5, 1.5, 2.5, 15, 15]]), 0, 6)
+    q = [rec[0, 0] & 15, rec[0, 0] >> 4, rec[0, 1] & 15, rec[0, 1] >> 4, rec[0, 2] & 15,
+         rec[0, 2] >> 4]
+    assert q == [0, 0, 2, 2, 15, 15]
+
+
+def test_degenerate_and_nonfinite_groups(O):
+    rec = O.kivi_compress(f16([[2.5] * 4]), 0, 4)
+    assert rec[0, :2].tolist() == [0, 0]                       # codes 0
+    assert rec[0, 2:4].view(np.uint16)[0] == 0                 # step 0
+    assert rec[0, 4:6].view(np.uint16)[0] == f16([2.5])[0]     # zero = gmin
+    # -inf minimum: not degenerate, scale 0 -> step inf, zero sanitised to 0
+    rec = O.kivi_compress(np.array([[0xFC00, 0, 0x3C00, 0x4000]], np.uint16), 0, 4)
+    assert rec[0, 2:4].view(np.uint16)[0] == 0x7C00
+    assert rec[0, 4:6].view(np.uint16)[0] == 0
+
+
+# ---- test_kivi_roundtrip.cpp:83-113 ----
+def test_roundtrip_no_outliers(O):
+    x = np.array([[0.1 * d + 0.5 * v for d in range(64)] for v in range(3)], np.float32)
+    got = h2f(O.kivi_decompress(O.kivi_compress(f16(x), 0, 16), 64, 0, 16))
+    assert np.max(np.abs(got - x)) <= 0.15
+
+
+# ---- test_kivi_roundtrip.cpp:121-170 ----
+def test_roundtrip_with_outliers(O):
+    x = np.array([[0.01 * (i % 64) for i in range(64)] for _ in range(2)], np.float32)
+    chans = [3, 17, 33, 55]
+    for v in range(2):
+        for k, ch in enumerate(chans):
+            x[v, ch] = 50.0 + k + v
+    got = h2f(O.kivi_decompress(O.kivi_compress(f16(x), 4, 16), 64, 4, 16))
+    assert np.max(np.abs(got - x)) <= 0.1
+
+
+# ---- test_kivi_roundtrip.cpp:178-200 ----
+def test_roundtrip_degenerate(O):
+    x = np.full((1, 32), 2.5, np.float32)
+    got = h2f(O.kivi_decompress(O.kivi_compress(f16(x), 0, 16), 32, 0, 16))
+    assert np.max(np.abs(got - 2.5)) <= 1e-2
+
+
+# ---- test_kivi_roundtrip.cpp:207-229 ----
+def test_unsupported_params_are_a_noop(O):
+    x = f16(np.ones((1, 256), np.float32))
+    rec = O.kivi_compress(x, 0, 16, fill=0xAB)
+    assert (rec == 0xAB).all()
+
+
+def test_slack_bytes_untouched(O):
+    # 128 dims, 8 outliers, G=16 -> 120 residuals = 7 full groups + one of 8:
+    # the last record writes 4+4 bytes of its 12-byte slot.
+    rng = np.random.default_rng(0)
+    x = f16(rng.standard_normal((5, 128)))
+    rec = O.kivi_compress(x, 8, 16, fill=0xCD)
+    mask = O.written_mask(128, 8, 16)
+    assert (rec[:, ~mask] == 0xCD).all()
+    assert (~mask).sum() == 4
+
+
+@pytest.mark.parametrize("name", sorted(p.name for p in GOLDEN.glob("refkivi_*.npz")))
+def test_oracle_matches_reference_golden(O, name):
+    """Byte records and decompressed vectors produced by the reference's own
+    kivi_cache.cu kernels on a B200 (tests/golden/make_golden.py)."""
+    g = np.load(GOLDEN / name)
+    n_out, G = int(g["n_outliers"]), int(g["group_size"])
+    x = g["x"]
+    D = x.shape[1]
+    rec = O.kivi_compress(x, n_out, G)
+    mask = O.written_mask(D, n_out, G)
+    assert np.array_equal(rec[:, mask], g["packed"][:, mask])
+    out = O.kivi_decompress(g["packed"], D, n_out, G)
+    assert np.array_equal(out, g["unpacked"])
+
+
+def test_golden_fixtures_present():
+    assert len(list(GOLDEN.glob("refkivi_*.npz"))) > 0, "reference golden vectors missing"

@@ -1,0 +1,78 @@
+"""Build the sm_100a C-ABI library libtruellm_kivi.so in-tree with nvcc.
+
+Each csrc/*.cu file is compiled to an object for sm_100a (-lineinfo, -O3,
+IEEE division and square root, no fast-math) in parallel and linked into one
+shared library with the CUDA runtime linked statically, so the library only
+needs the driver on the GPU box.  Objects go to _build/ (not committed).
+"""
+from __future__ import annotations
+
+import concurrent.futures as cf
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+CSRC = PKG / "csrc"
+BUILD = PKG / "_build"
+LIB = PKG / "libtruellm_kivi.so"
+INCLUDE = PKG.parent / "include"
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + [
+    "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+    "-prec-div=true", "-prec-sqrt=true", "-ftz=false", "--expt-relaxed-constexpr",
+    f"-I{INCLUDE}",
+]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", "nvcc"):
+        if cand and (os.path.sep not in cand or os.path.exists(cand)):
+            return cand
+    return "nvcc"
+
+
+def _sources() -> list[Path]:
+    return sorted(CSRC.glob("*.cu"))
+
+
+def _deps() -> list[Path]:
+    return sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+
+
+def _compile(src: Path, extra: list[str]) -> Path:
+    obj = BUILD / (src.stem + ".o")
+    newest_dep = max([src.stat().st_mtime] + [d.stat().st_mtime for d in _deps()])
+    if obj.exists() and obj.stat().st_mtime >= newest_dep:
+        return obj
+    cmd = [nvcc(), *NVCC_FLAGS, *extra, "-c", str(src), "-o", str(obj)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {src.name}:\n{res.stdout}\n{res.stderr}")
+    if res.stderr.strip():
+        sys.stderr.write(res.stderr)
+    return obj
+
+
+def build(verbose_ptxas: bool = False, force: bool = False) -> Path:
+    """Compile every CUDA source and link libtruellm_kivi.so; returns its path."""
+    BUILD.mkdir(exist_ok=True)
+    if force:
+        for o in BUILD.glob("*.o"):
+            o.unlink()
+    extra = ["-Xptxas", "-v"] if verbose_ptxas else []
+    with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
+        objs = list(ex.map(lambda s: _compile(s, extra), _sources()))
+    newest = max(o.stat().st_mtime for o in objs)
+    if force or not LIB.exists() or LIB.stat().st_mtime < newest:
+        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(LIB), *map(str, objs)]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(verbose_ptxas="-v" in sys.argv, force="--force" in sys.argv))

@@ -1,0 +1,206 @@
+// tkv_common.cuh -- shared device helpers for the sm_100a KIVI kernels:
+// bulk (TMA 1-D) copies completed on mbarriers with bounded waits, the
+// mma.m16n8k16 tensor-core op, code extraction and the reference quantizer's
+// arithmetic.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <float.h>
+#include <stdint.h>
+
+#include "../../include/truellm_kivi.h"
+
+namespace tkv {
+
+constexpr int kPage = TKV_PAGE_SIZE;
+constexpr int kSplitTokens = TKV_SPLIT_TOKENS;
+constexpr int kSplitPages = kSplitTokens / kPage;  // 32
+// A bounded mbarrier wait gives up after this many try_wait polls (each poll
+// may itself suspend the thread for a hardware-chosen time), then reports
+// TKV_ERR_TIMEOUT instead of spinning forever.
+constexpr uint32_t kMaxPolls = 1u << 22;
+
+__device__ __forceinline__ void set_err(int* err, int bit) {
+  if (err) atomicOr(err, bit);
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier + bulk copy (cp.async.bulk, no multicast)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Returns true when the phase with the given parity has completed.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait; on timeout sets TKV_ERR_TIMEOUT and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  for (uint32_t i = 0; i < kMaxPolls; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  set_err(err, TKV_ERR_TIMEOUT);
+  return false;
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (bytes % 16 == 0,
+// both addresses 16-byte aligned).
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          smem_u32(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tensor core: D = A(16x16 f16) * B(16x8 f16) + C (f32), mma.sync m16n8k16
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float2 unpack_h2(uint32_t u) {
+  __half2 h = *reinterpret_cast<__half2*>(&u);
+  return __half22float2(h);
+}
+
+// Codes -> f16 pairs holding 1 + code/16 (exact).  For 4-bit codes the pair is
+// the nibbles at bits [s0, s0+4) and [s0+16, s0+20) of w; for 2-bit codes the
+// 2-bit fields at the same positions.  SHIFT moves bit s0 to bit 6.
+template <int SHIFT>
+__device__ __forceinline__ uint32_t ext4(uint32_t w) {
+  uint32_t x = SHIFT >= 0 ? (w << SHIFT) : (w >> (-SHIFT));
+  return (x & 0x03C003C0u) | 0x3C003C00u;
+}
+template <int SHIFT>
+__device__ __forceinline__ uint32_t ext2(uint32_t w) {
+  uint32_t x = SHIFT >= 0 ? (w << SHIFT) : (w >> (-SHIFT));
+  return (x & 0x00C000C0u) | 0x3C003C00u;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
+
+// ---------------------------------------------------------------------------
+// reference quantizer arithmetic (kivi_cache.cu:92-124), IEEE ops spelled out
+// so no contraction or fast-math can change a bit.
+// ---------------------------------------------------------------------------
+struct QParams {
+  float gmin;
+  float scale;  // qmax / range, or 0 when degenerate
+  uint16_t hstep, hzero;
+};
+
+__device__ __forceinline__ QParams quant_params(float gmin, float gmax, int qmax) {
+  QParams p;
+  float range = __fsub_rn(gmax, gmin);
+  bool degenerate = !(range > 1e-6f);
+  p.scale = degenerate ? 0.f : __fdiv_rn(static_cast<float>(qmax), range);
+  float step = degenerate ? 0.f : __fdiv_rn(1.f, p.scale);
+  bool gmin_ok = (gmin == gmin) && (gmin > -FLT_MAX) && (gmin < FLT_MAX);
+  p.gmin = gmin;
+  __half hs = __float2half_rn(step);
+  __half hz = __float2half_rn(gmin_ok ? gmin : 0.f);
+  p.hstep = *reinterpret_cast<uint16_t*>(&hs);
+  p.hzero = *reinterpret_cast<uint16_t*>(&hz);
+  return p;
+}
+
+__device__ __forceinline__ int quant_code(float x, const QParams& p, int qmax) {
+  int q = __float2int_rn(__fmul_rn(__fsub_rn(x, p.gmin), p.scale));
+  q = q < 0 ? 0 : q;
+  return q > qmax ? qmax : q;
+}
+
+// ---------------------------------------------------------------------------
+// kernel argument blocks (filled by tkv_api.cu)
+// ---------------------------------------------------------------------------
+struct AppendArgs {
+  uint8_t* pool;
+  uint16_t* ring;
+  int num_pages, max_seqs, n_kv_heads, head_dim, group, residual, bits, ring_cap, n_vgroups;
+  int k_codes_off, v_codes_off, v_meta_off, k_meta_off, k_meta_slice;
+  int64_t page_bytes;
+  const void* k_new;
+  const void* v_new;
+  bool in_bf16;
+  const int32_t* cu_new;
+  const int32_t* lens_old;
+  const int32_t* block_tables;
+  int max_blocks;
+  const int32_t* seq_slots;
+  int max_new;
+  int* err;
+};
+
+struct DecodeArgs {
+  const uint8_t* pool;
+  const uint16_t* ring;
+  int num_pages, max_seqs, n_kv_heads, group, residual, ring_cap;
+  int k_codes_off, v_codes_off, v_meta_off, k_meta_off, k_meta_slice;
+  int64_t page_bytes;
+  int warp_smem;  // bytes of shared memory per warp
+  const void* q;
+  bool q_bf16;
+  const int32_t* block_tables;
+  int max_blocks;
+  const int32_t* seq_lens;
+  const int32_t* seq_slots;
+  int num_seqs, num_q_heads, grp;
+  float alpha;  // scale * log2(e)
+  int split_lo, split_hi, include_residual, n_slots;
+  float* part_ml;
+  float* part_o;
+  int* err;
+};
+
+int launch_ref_kivi(int mode, const void* in, void* out, int n_vecs, int head_dim, int n_outliers,
+                    int group_size, cudaStream_t stream);
+int launch_append(const AppendArgs& a, int num_seqs, cudaStream_t stream);
+int launch_decode_splits(DecodeArgs a, int head_dim, int bits, int n_vgroups, cudaStream_t stream);
+int launch_merge(const float* part_ml, const float* part_o, int n_slots, int num_seqs,
+                 int num_q_heads, int head_dim, void* out, int out_dtype, cudaStream_t stream);
+
+}  // namespace tkv

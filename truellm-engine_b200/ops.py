@@ -1,0 +1,243 @@
+"""Torch-facing wrappers of the C ABI: the reference's kernel entry points.
+
+Mirrors, with the same argument meaning:
+  kivi_compressed_bytes / kivi_params_supported / kivi_compress / kivi_decompress
+      src/inference/backends/cuda/compression/kivi_cache.cuh:32-84
+  reshape_and_cache  -> paged_append    (cuda_engine.cpp:48-50, cache_kernels.cu:202-232)
+  paged_attention_v1/v2 -> paged_decode (cuda_engine.cpp:51-62)
+Every call goes to the sm_100a library; tensors must be CUDA tensors.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib as L
+
+_DT = {torch.float16: L.TKV_F16, torch.bfloat16: L.TKV_BF16, torch.float32: L.TKV_F32}
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    if t is None:
+        return None
+    return C.c_void_p(t.data_ptr())
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("KIVI kernels take CUDA tensors")
+
+
+# ---------------------------------------------------------------------------
+# reference-format KIVI (kivi_cache.cuh)
+# ---------------------------------------------------------------------------
+KIVI_MAX_HEAD_DIM = 128  # kivi_cache.cuh:27
+KIVI_MAX_OUTLIERS = 64  # kivi_cache.cuh:28
+
+
+def kivi_compressed_bytes(head_dim: int, n_outliers: int, group_size: int) -> int:
+    """Bytes of one compressed vector (kivi_cache.cuh:32-43)."""
+    return int(L.lib().tkv_kivi_compressed_bytes(head_dim, n_outliers, group_size))
+
+
+def kivi_params_supported(head_dim: int, n_outliers: int, group_size: int) -> bool:
+    """kivi_cache.cu:205-211."""
+    return bool(L.lib().tkv_kivi_params_supported(head_dim, n_outliers, group_size))
+
+
+def kivi_compress(d_kv_in: torch.Tensor, d_out: torch.Tensor, n_vecs: int, head_dim: int,
+                  n_outliers: int, group_size: int, stream=None) -> None:
+    """truellm::kivi_compress: a no-op when kivi_params_supported() is false or
+    n_vecs <= 0, as in the reference wrapper (kivi_cache.cu:213-225)."""
+    if n_vecs <= 0 or not kivi_params_supported(head_dim, n_outliers, group_size):
+        return
+    _need_cuda(d_kv_in, d_out)
+    L.check("tkv_kivi_compress", L.lib().tkv_kivi_compress(
+        _ptr(d_kv_in), _ptr(d_out), n_vecs, head_dim, n_outliers, group_size,
+        C.c_void_p(_stream(stream))))
+
+
+def kivi_decompress(d_in: torch.Tensor, d_kv_out: torch.Tensor, n_vecs: int, head_dim: int,
+                    n_outliers: int, group_size: int, stream=None) -> None:
+    """truellm::kivi_decompress (kivi_cache.cu:227-239)."""
+    if n_vecs <= 0 or not kivi_params_supported(head_dim, n_outliers, group_size):
+        return
+    _need_cuda(d_in, d_kv_out)
+    L.check("tkv_kivi_decompress", L.lib().tkv_kivi_decompress(
+        _ptr(d_in), _ptr(d_kv_out), n_vecs, head_dim, n_outliers, group_size,
+        C.c_void_p(_stream(stream))))
+
+
+def kivi_roundtrip_inplace(d_kv: torch.Tensor, n_vecs: int, head_dim: int, n_outliers: int,
+                           group_size: int, stream=None) -> None:
+    """compress + decompress in place in one launch (KvCompressionPass::run_kivi)."""
+    if n_vecs <= 0 or not kivi_params_supported(head_dim, n_outliers, group_size):
+        return
+    _need_cuda(d_kv)
+    L.check("tkv_kivi_roundtrip_inplace", L.lib().tkv_kivi_roundtrip_inplace(
+        _ptr(d_kv), n_vecs, head_dim, n_outliers, group_size, C.c_void_p(_stream(stream))))
+
+
+# ---------------------------------------------------------------------------
+# paged KIVI cache
+# ---------------------------------------------------------------------------
+@dataclass(frozen=True)
+class KiviFormat:
+    head_dim: int
+    group_size: int
+    residual: int
+    bits: int
+    n_kv_heads: int
+
+    def c_struct(self) -> L.TkvFormat:
+        f = L.TkvFormat()
+        L.check("tkv_format_init", L.lib().tkv_format_init(
+            C.byref(f), self.head_dim, self.group_size, self.residual, self.bits,
+            self.n_kv_heads))
+        return f
+
+    @property
+    def page_bytes(self) -> int:
+        return int(self.c_struct().page_bytes)
+
+    @property
+    def ring_cap(self) -> int:
+        return int(self.c_struct().ring_cap)
+
+    def quantized_len(self, length: int) -> int:
+        x = length - self.residual
+        return self.group_size * (x // self.group_size) if x > 0 else 0
+
+
+class KiviPagedCache:
+    """Device buffers of one layer's paged KIVI cache.
+
+    pool: [num_pages, n_kv_heads, page_bytes] uint8 (block-major like the
+    reference pool, cuda_allocator.h:9-12); ring: [max_seqs, n_kv_heads,
+    ring_cap/16, 2, 16*D] fp16 residual window.  Both zero-initialised.
+    """
+
+    def __init__(self, fmt: KiviFormat, num_pages: int, max_seqs: int, device="cuda"):
+        self.fmt = fmt
+        cf = fmt.c_struct()
+        self.num_pages = int(num_pages)
+        self.max_seqs = int(max_seqs)
+        self.pool = torch.zeros((num_pages, fmt.n_kv_heads, int(cf.page_bytes)),
+                                dtype=torch.uint8, device=device)
+        self.ring = torch.zeros((max_seqs, fmt.n_kv_heads, int(cf.ring_cap) // 16, 2,
+                                 16 * fmt.head_dim), dtype=torch.float16, device=device)
+
+    def c_struct(self) -> L.TkvCache:
+        c = L.TkvCache()
+        c.pool = self.pool.data_ptr()
+        c.ring = self.ring.data_ptr()
+        c.num_pages = self.num_pages
+        c.max_seqs = self.max_seqs
+        c.fmt = self.fmt.c_struct()
+        return c
+
+
+def paged_append(cache: KiviPagedCache, k_new: torch.Tensor, v_new: torch.Tensor,
+                 cu_new: torch.Tensor, seq_lens_old: torch.Tensor, block_tables: torch.Tensor,
+                 seq_slots: Optional[torch.Tensor] = None, max_new_tokens: Optional[int] = None,
+                 err: Optional[torch.Tensor] = None, stream=None) -> None:
+    """Quantize-on-append (the KIVI reshape_and_cache).
+
+    k_new, v_new: [T_total, n_kv_heads, D] fp16/bf16; cu_new: [B+1] int32 token
+    offsets; seq_lens_old: [B] int32; block_tables: [B, max_blocks] int32.
+    max_new_tokens bounds the per-sequence token count (defaults to T_total).
+    """
+    _need_cuda(k_new, v_new, cu_new, seq_lens_old, block_tables)
+    if k_new.dtype not in (torch.float16, torch.bfloat16) or v_new.dtype != k_new.dtype:
+        raise ValueError("k_new/v_new must both be fp16 or bf16")
+    B = int(seq_lens_old.numel())
+    mnt = int(k_new.shape[0]) if max_new_tokens is None else int(max_new_tokens)
+    c = cache.c_struct()
+    L.check("tkv_paged_append", L.lib().tkv_paged_append(
+        C.byref(c), _ptr(k_new.contiguous()), _ptr(v_new.contiguous()), _DT[k_new.dtype],
+        _ptr(cu_new), _ptr(seq_lens_old), _ptr(block_tables), int(block_tables.shape[1]),
+        _ptr(seq_slots), B, mnt, _ptr(err), C.c_void_p(_stream(stream))))
+
+
+def decode_workspace_bytes(num_seqs: int, num_q_heads: int, head_dim: int,
+                           max_context_len: int) -> int:
+    return int(L.lib().tkv_decode_workspace_bytes(num_seqs, num_q_heads, head_dim,
+                                                  max_context_len))
+
+
+def decode_num_splits(max_context_len: int) -> int:
+    return int(L.lib().tkv_decode_num_splits(max_context_len))
+
+
+def paged_decode(cache: KiviPagedCache, q: torch.Tensor, block_tables: torch.Tensor,
+                 seq_lens: torch.Tensor, max_context_len: int, scale: Optional[float] = None,
+                 out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                 workspace: Optional[torch.Tensor] = None,
+                 seq_slots: Optional[torch.Tensor] = None, err: Optional[torch.Tensor] = None,
+                 stream=None) -> torch.Tensor:
+    """Decode attention over the KIVI cache (the paged_attention_v1/v2 slot).
+
+    q: [B, Hq, D] fp16/bf16.  Returns out [B, Hq, D] (dtype of q unless
+    out/out_dtype say otherwise).  scale defaults to 1/sqrt(D) (cuda_engine.cpp:1140).
+    """
+    _need_cuda(q, block_tables, seq_lens)
+    B, Hq, D = q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=out_dtype or q.dtype, device=q.device)
+    ws_bytes = decode_workspace_bytes(B, Hq, D, max_context_len)
+    if workspace is None:
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    c = cache.c_struct()
+    L.check("tkv_paged_decode", L.lib().tkv_paged_decode(
+        C.byref(c), _ptr(q.contiguous()), _DT[q.dtype], _ptr(out), _DT[out.dtype],
+        _ptr(block_tables), int(block_tables.shape[1]), _ptr(seq_lens), _ptr(seq_slots), B, Hq,
+        float(scale), int(max_context_len), _ptr(workspace), int(workspace.numel()),
+        _ptr(err), C.c_void_p(_stream(stream))))
+    return out
+
+
+def paged_decode_partials(cache: KiviPagedCache, q: torch.Tensor, block_tables: torch.Tensor,
+                          seq_lens: torch.Tensor, split_lo: int, split_hi: int,
+                          include_residual: bool, part_ml: torch.Tensor, part_o: torch.Tensor,
+                          scale: Optional[float] = None,
+                          seq_slots: Optional[torch.Tensor] = None,
+                          err: Optional[torch.Tensor] = None, stream=None) -> None:
+    """Split-KV partials (m, l, o) of quantised splits [split_lo, split_hi)
+    (+ the residual split) for sequences split across GPUs."""
+    _need_cuda(q, block_tables, seq_lens, part_ml, part_o)
+    B, Hq, D = q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    c = cache.c_struct()
+    L.check("tkv_paged_decode_partials", L.lib().tkv_paged_decode_partials(
+        C.byref(c), _ptr(q.contiguous()), _DT[q.dtype], _ptr(block_tables),
+        int(block_tables.shape[1]), _ptr(seq_lens), _ptr(seq_slots), B, Hq, float(scale),
+        int(split_lo), int(split_hi), int(bool(include_residual)), _ptr(part_ml), _ptr(part_o),
+        _ptr(err), C.c_void_p(_stream(stream))))
+
+
+def merge_partials(part_ml: torch.Tensor, part_o: torch.Tensor, out: torch.Tensor,
+                   stream=None) -> torch.Tensor:
+    """LSE merge (paged_attention_v2.cu:132-170).  part_ml: [S, B, Hq, 2],
+    part_o: [S, B, Hq, D] fp32; out: [B, Hq, D]."""
+    _need_cuda(part_ml, part_o, out)
+    S, B, Hq, D = part_o.shape
+    L.check("tkv_merge_partials", L.lib().tkv_merge_partials(
+        _ptr(part_ml), _ptr(part_o), S, B, Hq, D, _ptr(out), _DT[out.dtype],
+        C.c_void_p(_stream(stream))))
+    return out
