@@ -46,7 +46,8 @@
  *              b=4: w = mb,    bit = 4*(k + 4*e)
  *              b=2: w = mb/2,  bit = 2*(4*(mb%2) + k + 8*e)
  *            and word w of lane l is stored at byte
- *              ((w / VW) * 32 + l) * 4*VW + (w % VW) * 4,  VW = min(D*b/16, 4).
+ *              ((w / VW) * 32 + l) * 4*VW + (w % VW) * 4,  VW = min(D*b/64, 4)
+ *              (D*b/64 words per lane).
  *            (This is the A-operand register layout of mma.m16n8k16 for
  *            V^T tiles, so the decode kernel reads it with 16-byte loads.)
  *   V meta   [16 tokens][ceil(D/G) groups][fp16 step, fp16 zero].
@@ -167,13 +168,15 @@ TKV_API int tkv_kivi_roundtrip_inplace(void* d_kv_f16, int n_vecs, int head_dim,
  * k_new/v_new[cu_new[s] : cu_new[s+1]] ([T_total, n_kv_heads, D], fp16 or bf16)
  * after its seq_lens_old[s] existing tokens: every key/value group that becomes
  * complete is quantised into its pages, the rest goes to the fp16 ring.  The
- * block table must already cover the new length.  max_new_tokens bounds
- * cu_new[s+1]-cu_new[s] (it sizes the grid).  Two kernel launches. */
+ * block table must already cover the new length.  total_new_tokens is the
+ * number of rows in k_new / v_new; max_new_tokens bounds cu_new[s+1]-cu_new[s]
+ * (it sizes the grid).  Sequences whose offsets fall outside these bounds are
+ * skipped and flagged with TKV_ERR_BAD_LENGTH.  Two kernel launches. */
 TKV_API int tkv_paged_append(const tkv_cache_t* cache, const void* k_new, const void* v_new, int in_dtype,
                      const int32_t* cu_new, const int32_t* seq_lens_old,
                      const int32_t* block_tables, int max_blocks_per_seq,
-                     const int32_t* seq_slots, int num_seqs, int max_new_tokens, int* err_flag,
-                     void* stream);
+                     const int32_t* seq_slots, int num_seqs, int total_new_tokens,
+                     int max_new_tokens, int* err_flag, void* stream);
 
 /* ---------------------------------------------------------------- */
 /* Paged KIVI: decode attention                                       */

@@ -304,7 +304,7 @@ static void vcode_pos(const or_fmt* f, int c, int t, int* byte_off, int* shift) 
   int g = cc % 8, rh = cc / 8;
   int th = t / 8, tig = (t % 8) / 2, e = t % 2;
   int lane = g * 4 + tig;
-  int W = f->head_dim * f->bits / 16; /* 32-bit words per lane */
+  int W = f->head_dim * f->bits / 64; /* 32-bit words per lane */
   int VW = W < 4 ? W : 4;              /* words per vector chunk */
   int k = rh * 2 + th;                 /* register slot: R0=0,R2=1,R1=2,R3=3 -> see header */
   int w, bitpos;

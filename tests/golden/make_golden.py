@@ -4,13 +4,16 @@ compiled unmodified into oracle/_ref/libkivi_ref.so by `make -C oracle ref`)
 on a GPU.
 
     python tests/golden/make_golden.py <out_dir>
+    TKV_REF_LIB=oracle/_ref/libkivi_ref_O3.so python tests/golden/make_golden.py <out_dir>
 
 Writes refkivi_<case>.npz with x (fp16 bits), packed (bytes after compress
 into a buffer pre-filled with 0x00), unpacked (fp16 bits after decompress),
-n_outliers, group_size.  The committed fixtures in tests/golden/ were made by
-this script on a B200.
+n_outliers, group_size.  The committed fixtures were made by this script on a
+B200: tests/golden/ from the -G build (libkivi_ref.so, the source semantics)
+and tests/golden/o3/ from the default-optimised build (libkivi_ref_O3.so).
 """
 import ctypes as C
+import os
 import sys
 from pathlib import Path
 
@@ -18,7 +21,7 @@ import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parents[2]
-REF = ROOT / "oracle" / "_ref" / "libkivi_ref.so"
+REF = Path(os.environ.get("TKV_REF_LIB", ROOT / "oracle" / "_ref" / "libkivi_ref.so"))
 
 
 def cases():

@@ -1,9 +1,10 @@
 """GPU parity of the reference-format KIVI kernels (tkv_kivi_compress /
 tkv_kivi_decompress / tkv_kivi_roundtrip_inplace) against the CPU oracle and,
-when oracle/_ref/libkivi_ref.so was built, against the unmodified reference
-kernels (src/inference/backends/cuda/compression/kivi_cache.cu) on the same
-inputs.  Byte records must be equal except for the slack bytes the reference
-never writes."""
+when `make -C oracle ref` built them, against the unmodified reference kernels
+(src/inference/backends/cuda/compression/kivi_cache.cu) on the same inputs:
+byte for byte against the -G build (the source semantics), and against the
+default-optimised build up to the low byte of each fp16 step / zero, which
+that build stores as sat_u8(value)."""
 import ctypes as C
 from pathlib import Path
 
@@ -14,6 +15,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 REF = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libkivi_ref.so"
+REF_O3 = REF.with_name("libkivi_ref_O3.so")
 
 CASES = [(64, 32, 16), (128, 8, 16), (128, 8, 8), (128, 0, 128), (64, 0, 32), (96, 5, 16),
          (128, 64, 16), (64, 64, 16), (16, 3, 4), (128, 0, 2)]
@@ -78,6 +80,31 @@ def test_compress_decompress_match_reference_kernels(ops, cuda, D, n_out, G):
     ops.kivi_decompress(ref_packed, our_out, n, D, n_out, G)
     torch.cuda.synchronize()
     assert torch.equal(ref_out, our_out)
+
+
+@pytest.mark.skipif(not REF_O3.exists(), reason="reference kernels not built (make -C oracle ref)")
+@pytest.mark.parametrize("D,n_out,G", CASES)
+def test_optimised_reference_differs_only_in_meta_low_bytes(ops, cuda, D, n_out, G):
+    from test_oracle_reference import meta_offsets, sat_u8_lowbyte
+    lib = C.CDLL(str(REF_O3))
+    n = 97
+    x = _inputs(D, n, 3 + D + n_out + G)
+    stride = ops.kivi_compressed_bytes(D, n_out, G)
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    xin = _t(x, cuda)
+    ref_packed = torch.full((n * stride,), 0x5A, dtype=torch.uint8, device=cuda)
+    our_packed = torch.full((n * stride,), 0x5A, dtype=torch.uint8, device=cuda)
+    assert lib.ref_kivi_compress(C.c_void_p(xin.data_ptr()), C.c_void_p(ref_packed.data_ptr()),
+                                 n, D, n_out, G, s) == 0
+    ops.kivi_compress(xin, our_packed, n, D, n_out, G)
+    torch.cuda.synchronize()
+    ours = our_packed.cpu().numpy().reshape(n, stride)
+    theirs = ref_packed.cpu().numpy().reshape(n, stride)
+    mo = meta_offsets(D, n_out, G)
+    expect = ours.copy()
+    expect[:, mo] = sat_u8_lowbyte(ours[:, mo].astype(np.uint16) |
+                                   (ours[:, mo + 1].astype(np.uint16) << 8))
+    assert np.array_equal(expect, theirs)
 
 
 def test_unsupported_params_noop(ops, cuda):

@@ -153,3 +153,43 @@ def test_oracle_matches_reference_golden(O, name):
 
 def test_golden_fixtures_present():
     assert len(list(GOLDEN.glob("refkivi_*.npz"))) > 0, "reference golden vectors missing"
+    assert len(list((GOLDEN / "o3").glob("refkivi_*.npz"))) > 0
+
+
+def sat_u8_lowbyte(bits16: np.ndarray) -> np.ndarray:
+    """Low byte the nvcc 12.9-optimised reference stores for an fp16 value:
+    the value truncated toward zero and saturated to [0, 255]."""
+    v = np.asarray(bits16, np.uint16).view(np.float16).astype(np.float64)
+    v = np.where(np.isnan(v), 0, v)
+    return np.clip(np.trunc(v), 0, 255).astype(np.uint8)
+
+
+def meta_offsets(D, n_out, G):
+    """Byte offsets of every fp16 step / zero in one record."""
+    offs = []
+    pos = 3 * n_out
+    for gs in range(0, D - n_out, G):
+        ge = min(gs + G, D - n_out)
+        m = pos + (ge - gs + 1) // 2
+        offs += [m, m + 2]
+        pos += G // 2 + 4
+    return np.array(offs)
+
+
+@pytest.mark.parametrize("name", sorted(p.name for p in (GOLDEN / "o3").glob("refkivi_*.npz")))
+def test_optimised_reference_build_deviation_is_exactly_the_lowbyte_rule(O, name):
+    """The reference built with default device optimisation differs from its
+    source semantics only in the low byte of each fp16 step / zero, which
+    holds sat_u8(trunc(value)); decompress is unaffected."""
+    g = np.load(GOLDEN / "o3" / name)
+    n_out, G = int(g["n_outliers"]), int(g["group_size"])
+    x = g["x"]
+    D = x.shape[1]
+    rec = O.kivi_compress(x, n_out, G)
+    mo = meta_offsets(D, n_out, G)
+    expect = rec.copy()
+    vals = rec[:, mo] .astype(np.uint16) | (rec[:, mo + 1].astype(np.uint16) << 8)
+    expect[:, mo] = sat_u8_lowbyte(vals)
+    mask = O.written_mask(D, n_out, G)
+    assert np.array_equal(expect[:, mask], g["packed"][:, mask])
+    assert np.array_equal(O.kivi_decompress(g["packed"], D, n_out, G), g["unpacked"])

@@ -68,7 +68,7 @@ SIGNATURES = {
     "tkv_kivi_decompress": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp]),
     "tkv_kivi_roundtrip_inplace": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp]),
     "tkv_paged_append": (_i32, [C.POINTER(TkvCache), _vp, _vp, _i32, _vp, _vp, _vp, _i32, _vp,
-                                _i32, _i32, _vp, _vp]),
+                                _i32, _i32, _i32, _vp, _vp]),
     "tkv_decode_num_splits": (_i32, [_i32]),
     "tkv_decode_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32]),
     "tkv_paged_decode": (_i32, [C.POINTER(TkvCache), _vp, _i32, _vp, _i32, _vp, _i32, _vp, _vp,

@@ -169,11 +169,12 @@ int tkv_kivi_roundtrip_inplace(void* d_kv, int n_vecs, int head_dim, int n_outli
 int tkv_paged_append(const tkv_cache_t* cache, const void* k_new, const void* v_new, int in_dtype,
                      const int32_t* cu_new, const int32_t* seq_lens_old,
                      const int32_t* block_tables, int max_blocks_per_seq,
-                     const int32_t* seq_slots, int num_seqs, int max_new_tokens, int* err_flag,
-                     void* stream) {
+                     const int32_t* seq_slots, int num_seqs, int total_new_tokens,
+                     int max_new_tokens, int* err_flag, void* stream) {
   if (!cache_ok(cache)) return TKV_INVALID_ARGUMENT;
   if (in_dtype != TKV_F16 && in_dtype != TKV_BF16) return TKV_NOT_IMPLEMENTED;
-  if (num_seqs < 0 || num_seqs > 65535 || max_new_tokens < 0 || max_blocks_per_seq <= 0)
+  if (num_seqs < 0 || num_seqs > 65535 || max_new_tokens < 0 || total_new_tokens < 0 ||
+      max_blocks_per_seq <= 0)
     return TKV_INVALID_ARGUMENT;
   if (num_seqs == 0 || max_new_tokens == 0) return TKV_OK;
   if (!k_new || !v_new || !cu_new || !seq_lens_old || !block_tables) return TKV_INVALID_ARGUMENT;
@@ -207,6 +208,7 @@ int tkv_paged_append(const tkv_cache_t* cache, const void* k_new, const void* v_
   a.block_tables = block_tables;
   a.max_blocks = max_blocks_per_seq;
   a.seq_slots = seq_slots;
+  a.total_new = total_new_tokens;
   a.max_new = max_new_tokens;
   a.err = err_flag;
   return launch_append(a, num_seqs, as_stream(stream));

@@ -39,6 +39,14 @@ __device__ __forceinline__ uint16_t* ring_chunk(const AppendArgs& a, int slot_ro
   return a.ring + ((((int64_t)slot_row * a.n_kv_heads + h) * chunks + s / kPage) * 2 + kv) * elems;
 }
 
+// Every index a sequence's append touches stays inside the caller's buffers:
+// input rows [c0, c1) within [0, total_new), the new length within the block
+// table, the token count within the grid bound.
+__device__ __forceinline__ bool append_lengths_ok(const AppendArgs& a, int L, int c0, int c1) {
+  return L >= 0 && c0 >= 0 && c1 >= c0 && c1 <= a.total_new && c1 - c0 <= a.max_new &&
+         (int64_t)L + (c1 - c0) <= (int64_t)a.max_blocks * kPage;
+}
+
 constexpr int kFlushThreads = 256;
 constexpr int kMaxG = 128, kMaxD = 128;
 
@@ -60,9 +68,9 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
   const int b = blockIdx.z, h = blockIdx.y, gi = blockIdx.x;
   const int D = a.head_dim, G = a.group, TS = D + 2;
   const int L = a.lens_old[b];
-  const int T = a.cu_new[b + 1] - a.cu_new[b];
-  if (L < 0 || T < 0 || T > a.max_new ||
-      (int64_t)L + T > (int64_t)a.max_blocks * kPage) {
+  const int c0 = a.cu_new[b], c1 = a.cu_new[b + 1];
+  const int T = c1 - c0;
+  if (!append_lengths_ok(a, L, c0, c1)) {
     if (threadIdx.x == 0 && gi == 0 && h == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
     return;
   }
@@ -184,7 +192,7 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
   const int pages = G / kPage;
   const int rb = D * a.bits / 8;            // K code bytes per token row
   const int kwords = kPage * rb / 4;        // K code words per page
-  const int W = D * a.bits / 16;            // V code words per lane
+  const int W = D * a.bits / 64;            // V code words per lane
   const int VW = W < 4 ? W : 4;
   const int vwords = 32 * W;                // V code words per page
   const int vmwords = kPage * a.n_vgroups;  // V meta words per page
@@ -258,7 +266,7 @@ __global__ void __launch_bounds__(256) residual_write_kernel(AppendArgs a) {
   const int D = a.head_dim;
   const int L = a.lens_old[b];
   const int T = a.cu_new[b + 1] - a.cu_new[b];
-  if (L < 0 || T < 0 || T > a.max_new || (int64_t)L + T > (int64_t)a.max_blocks * kPage) return;
+  if (!append_lengths_ok(a, L, a.cu_new[b], a.cu_new[b + 1])) return;
   const int L2 = L + T;
   const int nq1 = nq_of(L2, a.residual, a.group);
   const int start = nq1 > L ? nq1 : L;

@@ -121,6 +121,28 @@ __device__ __forceinline__ uint32_t ext2(uint32_t w) {
   return (x & 0x00C000C0u) | 0x3C003C00u;
 }
 
+// Codes -> exact integer-valued f16 pairs.  lop3 ORs the masked code bits
+// into the mantissa of 1024.0 (0x6400), giving 1024 + c * 2^k; one HFMA2 by
+// (2^-k, -1024 * 2^-k) then yields c exactly.  MASK selects the code pair.
+template <uint32_t MASK>
+__device__ __forceinline__ uint32_t code_pair(uint32_t w) {
+  constexpr uint32_t lo = MASK & 0xffffu;
+  constexpr int k = lo == 0x000fu || lo == 0x0003u ? 0 : lo == 0x000cu ? 2 : lo == 0x00f0u || lo == 0x0030u ? 4 : 6;
+  constexpr uint32_t mul = k == 0 ? 0x3C003C00u : k == 2 ? 0x34003400u : k == 4 ? 0x2C002C00u : 0x24002400u;
+  constexpr uint32_t add = k == 0 ? 0xE400E400u : k == 2 ? 0xDC00DC00u : k == 4 ? 0xD400D400u : 0xCC00CC00u;
+  uint32_t x = (w & MASK) | 0x64006400u;
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(r) : "r"(x), "r"(mul), "r"(add));
+  return r;
+}
+
+// fp16x2 fused multiply-add, round to nearest even: d = a * b + c.
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
 __device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
 
 // ---------------------------------------------------------------------------
@@ -171,6 +193,7 @@ struct AppendArgs {
   const int32_t* block_tables;
   int max_blocks;
   const int32_t* seq_slots;
+  int total_new;  // rows in k_new / v_new
   int max_new;
   int* err;
 };

@@ -18,11 +18,13 @@
 //   * lane 0 issues one 1-D TMA bulk copy (cp.async.bulk, no multicast) per
 //     (page, head) block into shared memory, completing on an mbarrier;
 //   * QK^T runs on the tensor cores as S^T[16 tokens x 8 heads] =
-//     K[16 x D] * Q'^T[D x 8] with mma.m16n8k16 (f16 in, f32 accumulate).
-//     A fragments are built straight from the packed codes: a code c becomes
-//     the f16 value 1 + c/16 with one shift + one LOP3 per pair, and the
-//     per-channel key scale is folded into Q' = f16(q * step * alpha), so
-//     q.k = 16 * sum (1 + c/16) Q' - 16 sum Q' + alpha sum q * zero;
+//     K[16 x D] * Q^T[D x 8] with mma.m16n8k16 (f16 in, f32 accumulate).
+//     A fragments are built straight from the packed codes in registers: a
+//     LOP3 puts a code pair into the mantissa of 1024.0, one HFMA2 recovers
+//     the integer codes, a second HFMA2 applies the per-channel (step, zero)
+//     -- k = fp16(code * step + zero), the value the reference decompress
+//     writes -- and q stays exact in f16, so scores differ from the
+//     reference only by fp32 summation order;
 //   * online softmax in the exp2 domain with warp shuffles;
 //   * PV runs as O^T[D x 8] += V^T[D x 16] * P'^T[16 x 8] where P' = p * step_v
 //     (per-token value scale folded into P) and the value zero points are
@@ -51,30 +53,39 @@ __device__ __forceinline__ constexpr int kchan(int kb, int hi, int e) {
                    : 16 * (kb / 4) + 2 * (kb % 4) + hi + 8 * e;
 }
 
-// A-fragment registers (R0..R3 = {a0a1},{a2a3},{a4a5},{a6a7}) of k-block kb
-// from the thread's key-code words of rows g (wg) and g+8 (wh).
+// A-fragment registers (R0..R3 = {a0a1},{a2a3},{a4a5},{a6a7}) of k-block KB:
+// fp16 keys dequantised exactly as the reference decompress rounds them,
+// k = fp16(code * step + zero), from the thread's key-code words of rows g (wg)
+// and g+8 (wh) and the per-channel (step, zero) pairs of this key group.
 template <int BITS, int KB>
-__device__ __forceinline__ void key_frag(const uint32_t* wg, const uint32_t* wh, uint32_t (&r)[4]) {
+__device__ __forceinline__ void key_frag(const uint32_t* wg, const uint32_t* wh,
+                                         const uint32_t (&ks)[2], const uint32_t (&kz)[2],
+                                         uint32_t (&r)[4]) {
   if (BITS == 4) {
     constexpr int j = KB / 2;
-    if (KB % 2 == 0) {
-      r[0] = ext4<6>(wg[j]);
-      r[1] = ext4<6>(wh[j]);
-      r[2] = ext4<2>(wg[j]);
-      r[3] = ext4<2>(wh[j]);
-    } else {
-      r[0] = ext4<-2>(wg[j]);
-      r[1] = ext4<-2>(wh[j]);
-      r[2] = ext4<-6>(wg[j]);
-      r[3] = ext4<-6>(wh[j]);
+    if (KB % 2 == 0) {  // nibbles (0,4) -> hi 0, (1,5) -> hi 1
+      r[0] = hfma2(code_pair<0x000F000Fu>(wg[j]), ks[0], kz[0]);
+      r[1] = hfma2(code_pair<0x000F000Fu>(wh[j]), ks[0], kz[0]);
+      r[2] = hfma2(code_pair<0x00F000F0u>(wg[j]), ks[1], kz[1]);
+      r[3] = hfma2(code_pair<0x00F000F0u>(wh[j]), ks[1], kz[1]);
+    } else {            // nibbles (2,6) -> hi 0, (3,7) -> hi 1
+      const uint32_t g8 = wg[j] >> 8, h8 = wh[j] >> 8;
+      r[0] = hfma2(code_pair<0x000F000Fu>(g8), ks[0], kz[0]);
+      r[1] = hfma2(code_pair<0x000F000Fu>(h8), ks[0], kz[0]);
+      r[2] = hfma2(code_pair<0x00F000F0u>(g8), ks[1], kz[1]);
+      r[3] = hfma2(code_pair<0x00F000F0u>(h8), ks[1], kz[1]);
     }
   } else {
+    // 2-bit codes i and i+8 pair up; kb = 4j + i/2, hi = i%2
     constexpr int j = KB / 4, u = KB % 4;
-    constexpr int i0 = 2 * u, i1 = 2 * u + 1;  // pair indices for hi = 0 / 1
-    r[0] = ext2<6 - 2 * i0>(wg[j]);
-    r[1] = ext2<6 - 2 * i0>(wh[j]);
-    r[2] = ext2<6 - 2 * i1>(wg[j]);
-    r[3] = ext2<6 - 2 * i1>(wh[j]);
+    const uint32_t g_ = u < 2 ? wg[j] : (wg[j] >> 8);
+    const uint32_t h_ = u < 2 ? wh[j] : (wh[j] >> 8);
+    constexpr uint32_t m0 = (u % 2 == 0) ? 0x00030003u : 0x00300030u;  // i = 2u (mod 4)
+    constexpr uint32_t m1 = (u % 2 == 0) ? 0x000C000Cu : 0x00C000C0u;  // i = 2u+1 (mod 4)
+    r[0] = hfma2(code_pair<m0>(g_), ks[0], kz[0]);
+    r[1] = hfma2(code_pair<m0>(h_), ks[0], kz[0]);
+    r[2] = hfma2(code_pair<m1>(g_), ks[1], kz[1]);
+    r[3] = hfma2(code_pair<m1>(h_), ks[1], kz[1]);
   }
 }
 
@@ -177,7 +188,7 @@ __device__ void warp_quantized(const DecodeArgs& a, WarpState<D, NVG>& st, uint8
   constexpr int CH = D / 4;          // channels per thread chunk
   constexpr int RB = D * BITS / 8;   // key-code bytes per token row
   constexpr int TW = RB / 16;        // key-code words per thread per row (RB/4/4)
-  constexpr int VWN = D * BITS / 16; // value-code words per lane
+  constexpr int VWN = D * BITS / 64; // value-code words per lane
   constexpr int VW = VWN < 4 ? VWN : 4;
   constexpr int MB_PER_VG = (D / 16) / NVG;
   const int64_t pb = a.page_bytes;
@@ -198,55 +209,51 @@ __device__ void warp_quantized(const DecodeArgs& a, WarpState<D, NVG>& st, uint8
     }
   }
 
-  // ---- q for head g of this kv head, in this thread's key-channel order ----
+  // ---- B operand: q of head g as exact f16, in this thread's key-channel
+  //      order (k-slot 2tig+8hi+e <-> channel tig*CH + kchan(kb, hi, e)) ----
   const int hq = h * a.grp + g;
-  float qv[CH];
+  uint32_t bq[NKB][2];
   {
     const bool ok = g < a.grp;
     const int64_t qb = ((int64_t)b * a.num_q_heads + hq) * D + tig * CH;
 #pragma unroll
-    for (int j = 0; j < CH; ++j) qv[j] = ok ? load_q(a, qb + j) : 0.f;
+    for (int kb = 0; kb < NKB; ++kb)
+#pragma unroll
+      for (int hi = 0; hi < 2; ++hi) {
+        const float f0 = ok ? load_q(a, qb + kchan<BITS>(kb, hi, 0)) : 0.f;
+        const float f1 = ok ? load_q(a, qb + kchan<BITS>(kb, hi, 1)) : 0.f;
+        bq[kb][hi] = pack_h2(f0, f1);
+      }
   }
+  const bool hv0 = 2 * tig < a.grp, hv1 = 2 * tig + 1 < a.grp;
 
   const int pages_per_group = a.group / kPage;
   for (int p0 = 0; p0 < n_pages; p0 += pages_per_group) {
     // wait for the whole key group (its meta is spread over its pages)
     for (int i = 0; i < pages_per_group; ++i) mbar_wait(&bars[p0 + i], 0, a.err);
 
-    // ---- Q' fragments and the per-head constant for this key group ----
-    uint32_t bk[NKB][2];
-    float cpart = 0.f;
+    // ---- per-channel (step, zero) pairs of this key group, as f16x2 ----
+    uint32_t ks[NKB][2], kz[NKB][2];
 #pragma unroll
     for (int kb = 0; kb < NKB; ++kb)
 #pragma unroll
       for (int hi = 0; hi < 2; ++hi) {
-        float f[2];
+        uint32_t mw[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int cl = kchan<BITS>(kb, hi, e);
-          const int c = tig * CH + cl;
+          const int c = tig * CH + kchan<BITS>(kb, hi, e);
           const int byte = c * 4;
           const int pi = byte / a.k_meta_slice, off = byte % a.k_meta_slice;
-          const uint32_t mw = *reinterpret_cast<const uint32_t*>(
-              wsmem + (int64_t)(p0 + pi) * pb + a.k_meta_off + off);
-          const float2 sz = unpack_h2(mw);  // x = step, y = zero
-          f[e] = qv[cl] * sz.x * a.alpha;
-          cpart = fmaf(qv[cl] * a.alpha, sz.y, cpart);
+          mw[e] = *reinterpret_cast<const uint32_t*>(wsmem + (int64_t)(p0 + pi) * pb +
+                                                     a.k_meta_off + off);
         }
-        bk[kb][hi] = pack_h2(f[0], f[1]);
-        const float2 rr = unpack_h2(bk[kb][hi]);
-        cpart -= 16.f * (rr.x + rr.y);
+        ks[kb][hi] = __byte_perm(mw[0], mw[1], 0x5410);  // (step c0, step c1)
+        kz[kb][hi] = __byte_perm(mw[0], mw[1], 0x7632);  // (zero c0, zero c1)
       }
-    cpart += __shfl_xor_sync(0xffffffffu, cpart, 1);
-    cpart += __shfl_xor_sync(0xffffffffu, cpart, 2);
-    // constant for heads 2tig, 2tig+1 (held by lanes 4*(2tig), 4*(2tig+1))
-    const float cst0 = __shfl_sync(0xffffffffu, cpart, (2 * tig) * 4);
-    const float cst1 = __shfl_sync(0xffffffffu, cpart, (2 * tig + 1) * 4);
-    const bool hv0 = 2 * tig < a.grp, hv1 = 2 * tig + 1 < a.grp;
 
     for (int pi = 0; pi < pages_per_group; ++pi) {
       const uint8_t* pg = wsmem + (int64_t)(p0 + pi) * pb;
-      // ---- S^T = K Q'^T ----
+      // ---- S^T = K Q^T (exact fp16 products, fp32 accumulation) ----
       uint32_t wg[TW > 0 ? TW : 1], wh[TW > 0 ? TW : 1];
       {
         const uint8_t* kc = pg + a.k_codes_off;
@@ -272,17 +279,17 @@ __device__ void warp_quantized(const DecodeArgs& a, WarpState<D, NVG>& st, uint8
         switch (kb) {  // template dispatch on the unrolled index
 #define TKV_KF(K) \
   case K:         \
-    key_frag<BITS, (K < NKB ? K : 0)>(wg, wh, r); \
+    key_frag<BITS, (K < NKB ? K : 0)>(wg, wh, ks[K < NKB ? K : 0], kz[K < NKB ? K : 0], r); \
     break;
           TKV_KF(0) TKV_KF(1) TKV_KF(2) TKV_KF(3) TKV_KF(4) TKV_KF(5) TKV_KF(6) TKV_KF(7)
 #undef TKV_KF
         }
-        mma16816(s, r[0], r[1], r[2], r[3], bk[kb][0], bk[kb][1]);
+        mma16816(s, r[0], r[1], r[2], r[3], bq[kb][0], bq[kb][1]);
       }
-      s[0] = hv0 ? fmaf(16.f, s[0], cst0) : -INFINITY;
-      s[1] = hv1 ? fmaf(16.f, s[1], cst1) : -INFINITY;
-      s[2] = hv0 ? fmaf(16.f, s[2], cst0) : -INFINITY;
-      s[3] = hv1 ? fmaf(16.f, s[3], cst1) : -INFINITY;
+      s[0] = hv0 ? s[0] * a.alpha : -INFINITY;
+      s[1] = hv1 ? s[1] * a.alpha : -INFINITY;
+      s[2] = hv0 ? s[2] * a.alpha : -INFINITY;
+      s[3] = hv1 ? s[3] * a.alpha : -INFINITY;
       softmax_tile<D, NVG>(st, s);
 
       // ---- O^T += V^T P'^T ----
@@ -377,7 +384,8 @@ __device__ void warp_residual(const DecodeArgs& a, WarpState<D, NVG>& st, uint8_
   if (mine > 0) issue(0);
   if (mine > 1) issue(1);
 
-  // Q fragments (identity channel order), scaled by alpha, head g
+  // Q fragments (identity channel order, exact f16), head g; the softmax scale
+  // is applied to the fp32 accumulator
   const int hq = h * a.grp + g;
   const bool hok = g < a.grp;
   uint32_t bq[NKB][2];
@@ -388,8 +396,8 @@ __device__ void warp_residual(const DecodeArgs& a, WarpState<D, NVG>& st, uint8_
 #pragma unroll
       for (int hi = 0; hi < 2; ++hi) {
         const int c = 16 * kb + 2 * tig + 8 * hi;
-        const float f0 = hok ? load_q(a, qb + c) * a.alpha : 0.f;
-        const float f1 = hok ? load_q(a, qb + c + 1) * a.alpha : 0.f;
+        const float f0 = hok ? load_q(a, qb + c) : 0.f;
+        const float f1 = hok ? load_q(a, qb + c + 1) : 0.f;
         bq[kb][hi] = pack_h2(f0, f1);
       }
   }
@@ -408,10 +416,10 @@ __device__ void warp_residual(const DecodeArgs& a, WarpState<D, NVG>& st, uint8_
       const uint4 x = *reinterpret_cast<const uint4*>(ck + (kb * 32 + lane) * 16);
       mma16816(s, x.x, x.y, x.z, x.w, bq[kb][0], bq[kb][1]);
     }
-    s[0] = (hv0 && vg0) ? s[0] : -INFINITY;
-    s[1] = (hv1 && vg0) ? s[1] : -INFINITY;
-    s[2] = (hv0 && vg8) ? s[2] : -INFINITY;
-    s[3] = (hv1 && vg8) ? s[3] : -INFINITY;
+    s[0] = (hv0 && vg0) ? s[0] * a.alpha : -INFINITY;
+    s[1] = (hv1 && vg0) ? s[1] * a.alpha : -INFINITY;
+    s[2] = (hv0 && vg8) ? s[2] * a.alpha : -INFINITY;
+    s[3] = (hv1 && vg8) ? s[3] * a.alpha : -INFINITY;
     softmax_tile<D, NVG>(st, s);
     const uint32_t h2a = pack_h2(s[0], s[1]);
     const uint32_t h2b = pack_h2(s[2], s[3]);

@@ -169,7 +169,7 @@ def paged_append(cache: KiviPagedCache, k_new: torch.Tensor, v_new: torch.Tensor
     L.check("tkv_paged_append", L.lib().tkv_paged_append(
         C.byref(c), _ptr(k_new.contiguous()), _ptr(v_new.contiguous()), _DT[k_new.dtype],
         _ptr(cu_new), _ptr(seq_lens_old), _ptr(block_tables), int(block_tables.shape[1]),
-        _ptr(seq_slots), B, mnt, _ptr(err), C.c_void_p(_stream(stream))))
+        _ptr(seq_slots), B, int(k_new.shape[0]), mnt, _ptr(err), C.c_void_p(_stream(stream))))
 
 
 def decode_workspace_bytes(num_seqs: int, num_q_heads: int, head_dim: int,
