@@ -22,7 +22,6 @@ import importlib
 import json
 import math
 import os
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -39,7 +38,7 @@ UNIT = "seq-tokens/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="config2", choices=["config2", "config4", "config5"])
     ap.add_argument("--impl", default="kivi", choices=["kivi", "reference"])
@@ -97,49 +96,55 @@ def build_gpu_cache(ops, w, dev, torch):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML from a
+    background thread every ~2 ms while the timed region runs (read-only)."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4}
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
-        self.path = Path("/tmp") / f"tkv_clocks_{os.getpid()}.csv"
+        self.samples = []
+        self.stop = None
+        self.th = None
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index),
-                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
-                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            return self
+        self.stop = threading.Event()
+
+        def run():
+            while not self.stop.is_set():
+                try:
+                    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((sm, rs))
+                except Exception:
+                    pass
+                time.sleep(0.002)
+
+        self.th = threading.Thread(target=run, daemon=True)
+        self.th.start()
         return self
 
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self.stop is not None:
+            self.stop.set()
+            self.th.join(timeout=2)
 
     def summary(self):
-        if not self.path.exists():
+        if not self.samples:
             return None
-        rows = [r.split(",") for r in self.path.read_text().strip().splitlines() if r.strip()]
-        rows = [[x.strip() for x in r] for r in rows if len(r) >= 7]
-        if not rows:
-            return None
-        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
-        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i] == "Active"})
-        self.path.unlink(missing_ok=True)
-        return {"sm_mhz": float(np.median(sm)) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+        sm = [s for s, _ in self.samples]
+        reasons = sorted({n for _, r in self.samples for n, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(self.max_mhz),
+                "reasons": reasons, "samples": len(sm)}
 
 
 def ncu_traffic(workload: str):

@@ -173,7 +173,7 @@ def meta_offsets(D, n_out, G):
         m = pos + (ge - gs + 1) // 2
         offs += [m, m + 2]
         pos += G // 2 + 4
-    return np.array(offs)
+    return np.array(offs, dtype=np.int64)
 
 
 @pytest.mark.parametrize("name", sorted(p.name for p in (GOLDEN / "o3").glob("refkivi_*.npz")))

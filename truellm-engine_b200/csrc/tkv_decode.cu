@@ -36,8 +36,6 @@
 
 namespace tkv {
 
-constexpr int kDecodeWarps = 4;
-constexpr int kPagesPerWarp = kSplitPages / kDecodeWarps;  // 8
 
 
 __device__ __forceinline__ int nq_len(int len, int R, int G) {
@@ -177,334 +175,86 @@ __device__ __forceinline__ float load_q(const DecodeArgs& a, int64_t idx) {
 }
 
 // ---------------------------------------------------------------------------
-// quantised pages of one warp
+// compile-time layout of one paged format (same numbers as tkv_format_init)
 // ---------------------------------------------------------------------------
-template <int D, int BITS, int NVG>
-__device__ void warp_quantized(const DecodeArgs& a, WarpState<D, NVG>& st, uint8_t* wsmem,
-                               uint64_t* bars, int b, int h, int page_lo, int n_pages,
-                               bool issue) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
-  constexpr int NKB = D / 16;
-  constexpr int CH = D / 4;          // channels per thread chunk
-  constexpr int RB = D * BITS / 8;   // key-code bytes per token row
-  constexpr int TW = RB / 16;        // key-code words per thread per row (RB/4/4)
-  constexpr int VWN = D * BITS / 64; // value-code words per lane
-  constexpr int VW = VWN < 4 ? VWN : 4;
-  constexpr int MB_PER_VG = (D / 16) / NVG;
-  const int64_t pb = a.page_bytes;
-  const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
+template <int D, int BITS, int G>
+struct Fmt {
+  static constexpr int NKB = D / 16;             // k-blocks of QK / m-blocks of PV
+  static constexpr int CH = D / 4;               // key channels per thread chunk
+  static constexpr int RB = D * BITS / 8;        // key-code bytes per token row
+  static constexpr int TW = RB / 16;             // key-code words per thread per row
+  static constexpr int VWN = D * BITS / 64;      // value-code words per lane
+  static constexpr int VW = VWN < 4 ? VWN : 4;   // value-code words per 16-byte vector
+  static constexpr int NVG = D > G ? D / G : 1;  // value groups per token
+  static constexpr int MB_PER_VG = (D / 16) / NVG;
+  static constexpr int CODES = kPage * D * BITS / 8;
+  static constexpr int V_CODES_OFF = CODES;
+  static constexpr int V_META_OFF = 2 * CODES;
+  static constexpr int BODY = 2 * CODES + kPage * NVG * 4;  // page bytes before the key meta
+  static constexpr int KMS = D * 4 * kPage / G;              // key-meta slice bytes per page
+  static constexpr int PB = (BODY + KMS + 15) / 16 * 16;     // page_bytes
+  static constexpr int PPG = G / kPage;                      // pages per key group
+  static constexpr int META = D * 4;                         // key meta bytes per group
+  static constexpr int RUNIT = 2048;                         // residual copy unit
+  static constexpr int RU = (kPage * D * 2) / RUNIT;         // units per residual K or V block
+  static constexpr int STAGE = ((BODY > RUNIT ? BODY : RUNIT) + 127) / 128 * 128;
+  static_assert(TW >= 1 && (RB % 16) == 0, "key row split");
+  static_assert((KMS % 16) == 0 && (BODY % 16) == 0, "bulk-copy sizes are multiples of 16");
+};
 
-  // ---- issue all page loads of this warp (lane 0) ----
-  if (issue && lane == 0) {
-    for (int i = 0; i < n_pages; ++i) {
-      const int phys = bt[page_lo + i];
-      if (phys < 0 || phys >= a.num_pages) {
-        set_err(a.err, TKV_ERR_BAD_PAGE);
-        mbar_arrive(&bars[i]);
-      } else {
-        mbar_arrive_expect_tx(&bars[i], static_cast<uint32_t>(pb));
-        bulk_g2s(wsmem + (int64_t)i * pb, a.pool + ((int64_t)phys * a.n_kv_heads + h) * pb,
-                 static_cast<uint32_t>(pb), &bars[i]);
-      }
-    }
-  }
+constexpr int kStages = 6;                    // ring stages per warp
+constexpr int kBars = kStages + 2;            // ring barriers + 2 key-meta barriers
 
-  // ---- B operand: q of head g as exact f16, in this thread's key-channel
-  //      order (k-slot 2tig+8hi+e <-> channel tig*CH + kchan(kb, hi, e)) ----
-  const int hq = h * a.grp + g;
-  uint32_t bq[NKB][2];
-  {
-    const bool ok = g < a.grp;
-    const int64_t qb = ((int64_t)b * a.num_q_heads + hq) * D + tig * CH;
-#pragma unroll
-    for (int kb = 0; kb < NKB; ++kb)
-#pragma unroll
-      for (int hi = 0; hi < 2; ++hi) {
-        const float f0 = ok ? load_q(a, qb + kchan<BITS>(kb, hi, 0)) : 0.f;
-        const float f1 = ok ? load_q(a, qb + kchan<BITS>(kb, hi, 1)) : 0.f;
-        bq[kb][hi] = pack_h2(f0, f1);
-      }
-  }
-  const bool hv0 = 2 * tig < a.grp, hv1 = 2 * tig + 1 < a.grp;
-
-  const int pages_per_group = a.group / kPage;
-  for (int p0 = 0; p0 < n_pages; p0 += pages_per_group) {
-    // wait for the whole key group (its meta is spread over its pages)
-    for (int i = 0; i < pages_per_group; ++i) mbar_wait(&bars[p0 + i], 0, a.err);
-
-    // ---- per-channel (step, zero) pairs of this key group, as f16x2 ----
-    uint32_t ks[NKB][2], kz[NKB][2];
-#pragma unroll
-    for (int kb = 0; kb < NKB; ++kb)
-#pragma unroll
-      for (int hi = 0; hi < 2; ++hi) {
-        uint32_t mw[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int c = tig * CH + kchan<BITS>(kb, hi, e);
-          const int byte = c * 4;
-          const int pi = byte / a.k_meta_slice, off = byte % a.k_meta_slice;
-          mw[e] = *reinterpret_cast<const uint32_t*>(wsmem + (int64_t)(p0 + pi) * pb +
-                                                     a.k_meta_off + off);
-        }
-        ks[kb][hi] = __byte_perm(mw[0], mw[1], 0x5410);  // (step c0, step c1)
-        kz[kb][hi] = __byte_perm(mw[0], mw[1], 0x7632);  // (zero c0, zero c1)
-      }
-
-    for (int pi = 0; pi < pages_per_group; ++pi) {
-      const uint8_t* pg = wsmem + (int64_t)(p0 + pi) * pb;
-      // ---- S^T = K Q^T (exact fp16 products, fp32 accumulation) ----
-      uint32_t wg[TW > 0 ? TW : 1], wh[TW > 0 ? TW : 1];
-      {
-        const uint8_t* kc = pg + a.k_codes_off;
-        if (RB / 4 == 16) {  // 16 bytes per thread per row
-          const uint4 x = *reinterpret_cast<const uint4*>(kc + g * RB + tig * 16);
-          const uint4 y = *reinterpret_cast<const uint4*>(kc + (g + 8) * RB + tig * 16);
-          wg[0] = x.x; wg[1] = x.y; wg[2] = x.z; wg[3] = x.w;
-          wh[0] = y.x; wh[1] = y.y; wh[2] = y.z; wh[3] = y.w;
-        } else if (RB / 4 == 8) {
-          const uint2 x = *reinterpret_cast<const uint2*>(kc + g * RB + tig * 8);
-          const uint2 y = *reinterpret_cast<const uint2*>(kc + (g + 8) * RB + tig * 8);
-          wg[0] = x.x; wg[1] = x.y;
-          wh[0] = y.x; wh[1] = y.y;
-        } else {
-          wg[0] = *reinterpret_cast<const uint32_t*>(kc + g * RB + tig * 4);
-          wh[0] = *reinterpret_cast<const uint32_t*>(kc + (g + 8) * RB + tig * 4);
-        }
-      }
-      float s[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int kb = 0; kb < NKB; ++kb) {
-        uint32_t r[4];
-        switch (kb) {  // template dispatch on the unrolled index
-#define TKV_KF(K) \
-  case K:         \
-    key_frag<BITS, (K < NKB ? K : 0)>(wg, wh, ks[K < NKB ? K : 0], kz[K < NKB ? K : 0], r); \
-    break;
-          TKV_KF(0) TKV_KF(1) TKV_KF(2) TKV_KF(3) TKV_KF(4) TKV_KF(5) TKV_KF(6) TKV_KF(7)
-#undef TKV_KF
-        }
-        mma16816(s, r[0], r[1], r[2], r[3], bq[kb][0], bq[kb][1]);
-      }
-      s[0] = hv0 ? s[0] * a.alpha : -INFINITY;
-      s[1] = hv1 ? s[1] * a.alpha : -INFINITY;
-      s[2] = hv0 ? s[2] * a.alpha : -INFINITY;
-      s[3] = hv1 ? s[3] * a.alpha : -INFINITY;
-      softmax_tile<D, NVG>(st, s);
-
-      // ---- O^T += V^T P'^T ----
-      uint32_t vw[VWN];
-      {
-        const uint8_t* vc = pg + a.v_codes_off;
-#pragma unroll
-        for (int v = 0; v < VWN / VW; ++v) {
-          if (VW == 4) {
-            const uint4 x = *reinterpret_cast<const uint4*>(vc + (v * 32 + lane) * 16);
-            vw[4 * v + 0] = x.x; vw[4 * v + 1] = x.y; vw[4 * v + 2] = x.z; vw[4 * v + 3] = x.w;
-          } else {
-            const uint2 x = *reinterpret_cast<const uint2*>(vc + lane * 8);
-            vw[0] = x.x; vw[1] = x.y;
-          }
-        }
-      }
-      const uint32_t* vm = reinterpret_cast<const uint32_t*>(pg + a.v_meta_off);
-#pragma unroll
-      for (int vg = 0; vg < NVG; ++vg) {
-        const float2 sza = unpack_h2(vm[g * NVG + vg]);        // token g
-        const float2 szb = unpack_h2(vm[(g + 8) * NVG + vg]);  // token g+8
-        const uint32_t h2a = pack_h2(s[0] * sza.x, s[1] * sza.x);
-        const uint32_t h2b = pack_h2(s[2] * szb.x, s[3] * szb.x);
-        const float2 ra = unpack_h2(h2a), rb = unpack_h2(h2b);
-        st.w[vg][0] += s[0] * sza.y + s[2] * szb.y - 16.f * (ra.x + rb.x);
-        st.w[vg][1] += s[1] * sza.y + s[3] * szb.y - 16.f * (ra.y + rb.y);
-        uint32_t b01, b23;
-        p_to_bfrag(h2a, h2b, lane, b01, b23);
-#pragma unroll
-        for (int k = 0; k < MB_PER_VG; ++k) {
-          const int mb = vg * MB_PER_VG + k;
-          uint32_t r[4];
-          switch (mb) {
-#define TKV_VF(M) \
-  case M:         \
-    value_frag<BITS, (M < D / 16 ? M : 0)>(vw, r); \
-    break;
-            TKV_VF(0) TKV_VF(1) TKV_VF(2) TKV_VF(3) TKV_VF(4) TKV_VF(5) TKV_VF(6) TKV_VF(7)
-#undef TKV_VF
-          }
-          mma16816(st.o[mb], r[0], r[1], r[2], r[3], b01, b23);
-        }
-      }
-    }
-  }
-  // finalise: O^T = 16 * acc + per-head value-zero correction
-#pragma unroll
-  for (int vg = 0; vg < NVG; ++vg)
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      float w = st.w[vg][hh];
-      w += __shfl_xor_sync(0xffffffffu, w, 4);
-      w += __shfl_xor_sync(0xffffffffu, w, 8);
-      w += __shfl_xor_sync(0xffffffffu, w, 16);
-      st.w[vg][hh] = w;
-    }
-#pragma unroll
-  for (int mb = 0; mb < D / 16; ++mb) {
-    const int vg = mb / MB_PER_VG;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) st.o[mb][i] = fmaf(16.f, st.o[mb][i], st.w[vg][i & 1]);
-  }
+template <int D, int BITS, int G>
+constexpr int decode_smem_bytes() {
+  using F = Fmt<D, BITS, G>;
+  return 128 + kStages * F::STAGE + 2 * F::META;
 }
 
-// ---------------------------------------------------------------------------
-// fp16 residual ring of one sequence: this warp's 16-token chunks
-// ---------------------------------------------------------------------------
-template <int D, int NVG>
-__device__ void warp_residual(const DecodeArgs& a, WarpState<D, NVG>& st, uint8_t* wsmem,
-                              uint64_t* bars, int b, int h, int row, int nq, int len) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
-  constexpr int NKB = D / 16;
-  constexpr int CHUNK_BYTES = 2 * kPage * D * 2;  // K block + V block
-  const int n_chunks = (len - nq + kPage - 1) / kPage;
-  const int64_t chunks_per_row = a.ring_cap / kPage;
-  const uint8_t* ring_base =
-      reinterpret_cast<const uint8_t*>(a.ring) +
-      (((int64_t)row * a.n_kv_heads + h) * chunks_per_row) * CHUNK_BYTES;
-  // my chunks: warp, warp + 4, ...
-  const int mine = n_chunks > warp ? (n_chunks - warp + kDecodeWarps - 1) / kDecodeWarps : 0;
-  auto issue = [&](int k) {
-    if (lane == 0) {
-      const int ci = warp + k * kDecodeWarps;
-      const int tok = nq + ci * kPage;
-      const int chunk = (tok % a.ring_cap) / kPage;
-      mbar_arrive_expect_tx(&bars[k & 1], CHUNK_BYTES);
-      bulk_g2s(wsmem + (k & 1) * CHUNK_BYTES, ring_base + (int64_t)chunk * CHUNK_BYTES,
-               CHUNK_BYTES, &bars[k & 1]);
-    }
-  };
-  if (mine > 0) issue(0);
-  if (mine > 1) issue(1);
-
-  // Q fragments (identity channel order, exact f16), head g; the softmax scale
-  // is applied to the fp32 accumulator
-  const int hq = h * a.grp + g;
-  const bool hok = g < a.grp;
-  uint32_t bq[NKB][2];
-  {
-    const int64_t qb = ((int64_t)b * a.num_q_heads + hq) * D;
-#pragma unroll
-    for (int kb = 0; kb < NKB; ++kb)
-#pragma unroll
-      for (int hi = 0; hi < 2; ++hi) {
-        const int c = 16 * kb + 2 * tig + 8 * hi;
-        const float f0 = hok ? load_q(a, qb + c) : 0.f;
-        const float f1 = hok ? load_q(a, qb + c + 1) : 0.f;
-        bq[kb][hi] = pack_h2(f0, f1);
-      }
-  }
-  const bool hv0 = 2 * tig < a.grp, hv1 = 2 * tig + 1 < a.grp;
-
-  for (int k = 0; k < mine; ++k) {
-    mbar_wait(&bars[k & 1], (k >> 1) & 1, a.err);
-    const uint8_t* ck = wsmem + (k & 1) * CHUNK_BYTES;
-    const uint8_t* cv = ck + CHUNK_BYTES / 2;
-    const int ci = warp + k * kDecodeWarps;
-    const int tb = nq + ci * kPage;  // first token of the chunk
-    const bool vg0 = tb + g < len, vg8 = tb + g + 8 < len;
-    float s[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int kb = 0; kb < NKB; ++kb) {
-      const uint4 x = *reinterpret_cast<const uint4*>(ck + (kb * 32 + lane) * 16);
-      mma16816(s, x.x, x.y, x.z, x.w, bq[kb][0], bq[kb][1]);
-    }
-    s[0] = (hv0 && vg0) ? s[0] * a.alpha : -INFINITY;
-    s[1] = (hv1 && vg0) ? s[1] * a.alpha : -INFINITY;
-    s[2] = (hv0 && vg8) ? s[2] * a.alpha : -INFINITY;
-    s[3] = (hv1 && vg8) ? s[3] * a.alpha : -INFINITY;
-    softmax_tile<D, NVG>(st, s);
-    const uint32_t h2a = pack_h2(s[0], s[1]);
-    const uint32_t h2b = pack_h2(s[2], s[3]);
-    uint32_t b01, b23;
-    p_to_bfrag(h2a, h2b, lane, b01, b23);
-    // zero the V^T columns of tokens past the end (their ring slots may hold
-    // stale data, and 0 * inf would poison the sum)
-    const int t0 = tb + 2 * tig;
-    const uint32_t m01 = (t0 < len ? 0x0000ffffu : 0u) | (t0 + 1 < len ? 0xffff0000u : 0u);
-    const uint32_t m23 = (t0 + 8 < len ? 0x0000ffffu : 0u) | (t0 + 9 < len ? 0xffff0000u : 0u);
-#pragma unroll
-    for (int mb = 0; mb < D / 16; ++mb) {
-      const uint4 x = *reinterpret_cast<const uint4*>(cv + (mb * 32 + lane) * 16);
-      mma16816(st.o[mb], x.x & m01, x.y & m01, x.z & m23, x.w & m23, b01, b23);
-    }
-    __syncwarp();
-    if (k + 2 < mine) issue(k + 2);
-  }
-}
-
-// ---------------------------------------------------------------------------
-// split kernel
-// ---------------------------------------------------------------------------
-template <int D, int BITS, int NVG>
-__global__ void __launch_bounds__(kDecodeWarps * 32, 3) decode_split_kernel(DecodeArgs a) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int slot = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);  // 8 per warp
-  uint8_t* wsmem = smem + 512 + warp * a.warp_smem;
-  uint64_t* wbars = bars + warp * 8;
-
-  const int len = a.seq_lens[b];
-  const int64_t ml_base = ((int64_t)slot * a.num_seqs + b) * a.num_q_heads + h * a.grp;
-  if (len < 0 || len > a.max_blocks * kPage) {
-    if (threadIdx.x == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
-  }
-  const bool len_ok = len >= 0 && len <= a.max_blocks * kPage;
-  const int nq = len_ok ? nq_len(len, a.residual, a.group) : 0;
-  const int n_qsplit = a.split_hi - a.split_lo;
-  const bool is_res = a.include_residual && slot == n_qsplit;
-
-  // which work does this CTA have?
-  int page_lo = 0, n_pages = 0;
-  int row = 0;
-  bool work = false;
-  if (len_ok && !is_res && slot < n_qsplit) {
-    const int sp = a.split_lo + slot;
-    page_lo = sp * kSplitPages + warp * kPagesPerWarp;
-    const int nqp = nq / kPage;
-    n_pages = min(kPagesPerWarp, nqp - page_lo);
-    if (n_pages < 0) n_pages = 0;
-    work = sp * kSplitPages < nqp;
-  } else if (len_ok && is_res && len > nq) {
-    row = a.seq_slots ? a.seq_slots[b] : b;
-    if (row < 0 || row >= a.max_seqs) {
-      if (threadIdx.x == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
-    } else {
-      work = true;
-    }
-  }
-  if (!work) {  // empty slot: m = -inf, l = 0 for every q head of this kv head
-    for (int j = threadIdx.x; j < a.grp; j += blockDim.x) {
-      a.part_ml[(ml_base + j) * 2 + 0] = -INFINITY;
-      a.part_ml[(ml_base + j) * 2 + 1] = 0.f;
-    }
-    return;
-  }
-
-  if (lane == 0) {
-    for (int i = 0; i < 8; ++i) mbar_init(&wbars[i], 1);
-    fence_mbar_init();
-  }
-  __syncwarp();
-
-  WarpState<D, NVG> st;
-  st.init();
-  if (!is_res) {
-    if (n_pages > 0)
-      warp_quantized<D, BITS, NVG>(a, st, wsmem, wbars, b, h, page_lo, n_pages, true);
+// Loads the thread's 8 (or fewer) key-code words of rows g and g+8.
+template <int D, int BITS>
+__device__ __forceinline__ void load_key_words(const uint8_t* kc, int g, int tig,
+                                               uint32_t (&wg)[D * BITS / 128],
+                                               uint32_t (&wh)[D * BITS / 128]) {
+  constexpr int RB = D * BITS / 8, TB = RB / 4;
+  if constexpr (TB == 16) {
+    const uint4 x = *reinterpret_cast<const uint4*>(kc + g * RB + tig * 16);
+    const uint4 y = *reinterpret_cast<const uint4*>(kc + (g + 8) * RB + tig * 16);
+    wg[0] = x.x; wg[1] = x.y; wg[2] = x.z; wg[3] = x.w;
+    wh[0] = y.x; wh[1] = y.y; wh[2] = y.z; wh[3] = y.w;
+  } else if constexpr (TB == 8) {
+    const uint2 x = *reinterpret_cast<const uint2*>(kc + g * RB + tig * 8);
+    const uint2 y = *reinterpret_cast<const uint2*>(kc + (g + 8) * RB + tig * 8);
+    wg[0] = x.x; wg[1] = x.y;
+    wh[0] = y.x; wh[1] = y.y;
   } else {
-    warp_residual<D, NVG>(a, st, wsmem, wbars, b, h, row, nq, len);
+    wg[0] = *reinterpret_cast<const uint32_t*>(kc + g * RB + tig * 4);
+    wh[0] = *reinterpret_cast<const uint32_t*>(kc + (g + 8) * RB + tig * 4);
   }
+}
 
-  // ---- reduce l over the 8 row groups, then merge the 4 warps ----
+template <int D, int BITS>
+__device__ __forceinline__ void load_value_words(const uint8_t* vc, int lane,
+                                                 uint32_t (&vw)[D * BITS / 64]) {
+  constexpr int VWN = D * BITS / 64, VW = VWN < 4 ? VWN : 4;
+#pragma unroll
+  for (int v = 0; v < VWN / VW; ++v) {
+    if constexpr (VW == 4) {
+      const uint4 x = *reinterpret_cast<const uint4*>(vc + (v * 32 + lane) * 16);
+      vw[4 * v + 0] = x.x; vw[4 * v + 1] = x.y; vw[4 * v + 2] = x.z; vw[4 * v + 3] = x.w;
+    } else {
+      const uint2 x = *reinterpret_cast<const uint2*>(vc + lane * 8);
+      vw[0] = x.x; vw[1] = x.y;
+    }
+  }
+}
+
+// Writes this warp's partial (m, l, o[D]) for the q heads of kv head h.
+template <int D, int NVG>
+__device__ __forceinline__ void write_partial(const DecodeArgs& a, WarpState<D, NVG>& st,
+                                              int64_t ml_base, bool quantized) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+  constexpr int MB_PER_VG = (D / 16) / NVG;
 #pragma unroll
   for (int hh = 0; hh < 2; ++hh) {
     float l = st.l[hh];
@@ -512,52 +262,288 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 3) decode_split_kernel(Deco
     l += __shfl_xor_sync(0xffffffffu, l, 8);
     l += __shfl_xor_sync(0xffffffffu, l, 16);
     st.l[hh] = l;
+#pragma unroll
+    for (int vg = 0; vg < NVG; ++vg) {
+      float w = st.w[vg][hh];
+      w += __shfl_xor_sync(0xffffffffu, w, 4);
+      w += __shfl_xor_sync(0xffffffffu, w, 8);
+      w += __shfl_xor_sync(0xffffffffu, w, 16);
+      st.w[vg][hh] = w;
+    }
+  }
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int hd = 2 * tig + hh;
+    if (hd >= a.grp) continue;
+    float* po = a.part_o + (ml_base + hd) * D;
+#pragma unroll
+    for (int mb = 0; mb < D / 16; ++mb) {
+      const int vg = mb / MB_PER_VG;
+      float o0 = st.o[mb][hh], o1 = st.o[mb][2 + hh];
+      if (quantized) {  // O^T = 16 * acc + value-zero correction
+        o0 = fmaf(16.f, o0, st.w[vg][hh]);
+        o1 = fmaf(16.f, o1, st.w[vg][hh]);
+      }
+      po[16 * mb + g] = o0;
+      po[16 * mb + g + 8] = o1;
+    }
+    if (g == 0) {
+      a.part_ml[(ml_base + hd) * 2 + 0] = st.m[hh];
+      a.part_ml[(ml_base + hd) * 2 + 1] = st.l[hh];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// split kernel: one warp per (split slot, kv head, sequence)
+// ---------------------------------------------------------------------------
+template <int D, int BITS, int G>
+__global__ void __launch_bounds__(32, 16) decode_warp_kernel(DecodeArgs a) {
+  using F = Fmt<D, BITS, G>;
+  constexpr int NVG = F::NVG;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint8_t* ring = smem + 128;
+  uint8_t* meta = ring + kStages * F::STAGE;  // 2 x key-group meta [D][step, zero]
+  const int slot = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int lane = threadIdx.x, g = lane >> 2, tig = lane & 3;
+
+  const int64_t ml_base = ((int64_t)slot * a.num_seqs + b) * a.num_q_heads + h * a.grp;
+  const int len = a.seq_lens[b];
+  const bool len_ok = len >= 0 && len <= a.max_blocks * kPage;
+  if (!len_ok && lane == 0 && h == 0 && slot == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
+  const int nq = len_ok ? nq_len(len, a.residual, G) : 0;
+  const int n_qsplit = a.split_hi - a.split_lo;
+  const bool is_res = a.include_residual && slot == n_qsplit;
+  const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
+
+  // ---- what does this warp do? ----
+  int n_units = 0, page_lo = 0, row = 0;
+  if (len_ok && !is_res && slot < n_qsplit) {
+    page_lo = (a.split_lo + slot) * kSplitPages;
+    n_units = min(kSplitPages, nq / kPage - page_lo);  // pages, a multiple of PPG
+    // every block-table entry of the split must name a pool page
+    bool bad = false;
+    for (int i = lane; i < n_units; i += 32) {
+      const int phys = bt[page_lo + i];
+      bad |= phys < 0 || phys >= a.num_pages;
+    }
+    if (__any_sync(0xffffffffu, bad)) {
+      if (lane == 0) set_err(a.err, TKV_ERR_BAD_PAGE);
+      n_units = 0;
+    }
+  } else if (len_ok && is_res && len > nq) {
+    row = a.seq_slots ? a.seq_slots[b] : b;
+    if (row < 0 || row >= a.max_seqs) {
+      if (lane == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
+    } else {
+      n_units = ((len - nq + kPage - 1) / kPage) * 2 * F::RU;
+    }
+  }
+  if (n_units <= 0) {
+    if (lane < a.grp) {
+      a.part_ml[(ml_base + lane) * 2 + 0] = -INFINITY;
+      a.part_ml[(ml_base + lane) * 2 + 1] = 0.f;
+    }
+    return;
+  }
+
+  if (lane == 0) {
+    for (int i = 0; i < kBars; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
   }
   __syncwarp();
-  // per-warp staging (reuses this warp's page buffers): m[8], l[8], o[8][D]
-  float* stg = reinterpret_cast<float*>(wsmem);
-  if (g == 0) {
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      stg[2 * tig + hh] = st.m[hh];
-      stg[8 + 2 * tig + hh] = st.l[hh];
+
+  WarpState<D, NVG> st;
+  st.init();
+  const bool hv0 = 2 * tig < a.grp, hv1 = 2 * tig + 1 < a.grp;
+  const int hq = h * a.grp + g;
+  const bool hok = g < a.grp;
+  const int64_t qrow = ((int64_t)b * a.num_q_heads + hq) * D;
+
+  if (!is_res) {
+    // =================== quantised split ===================
+    const int n = n_units;
+    auto issue_page = [&](int u) {  // lane 0
+      const int phys = bt[page_lo + u];
+      uint64_t* bar = &bars[u % kStages];
+      mbar_arrive_expect_tx(bar, F::BODY);
+      bulk_g2s(ring + (u % kStages) * F::STAGE,
+               a.pool + ((int64_t)phys * a.n_kv_heads + h) * F::PB, F::BODY, bar);
+    };
+    auto issue_meta = [&](int grp) {  // lane 0: the group's key-meta slices
+      uint64_t* bar = &bars[kStages + (grp & 1)];
+      mbar_arrive_expect_tx(bar, F::META);
+      for (int i = 0; i < F::PPG; ++i) {
+        const int phys = bt[page_lo + grp * F::PPG + i];
+        bulk_g2s(meta + (grp & 1) * F::META + i * F::KMS,
+                 a.pool + ((int64_t)phys * a.n_kv_heads + h) * F::PB + F::BODY, F::KMS, bar);
+      }
+    };
+    if (lane == 0) {
+      issue_meta(0);
+      for (int u = 0; u < min(kStages, n); ++u) issue_page(u);
     }
-  }
+    // B operand: q of head g as exact f16 in this thread's key-channel order
+    uint32_t bq[F::NKB][2];
 #pragma unroll
-  for (int mb = 0; mb < D / 16; ++mb)
+    for (int kb = 0; kb < F::NKB; ++kb)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int c = 16 * mb + g + ((i >> 1) << 3);
-      const int hd = 2 * tig + (i & 1);
-      stg[16 + hd * D + c] = st.o[mb][i];
-    }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < a.grp * D; idx += blockDim.x) {
-    const int hd = idx / D, c = idx % D;
-    float M = -INFINITY;
+      for (int hi = 0; hi < 2; ++hi) {
+        const int64_t c0 = qrow + tig * F::CH + kchan<BITS>(kb, hi, 0);
+        const int64_t c1 = qrow + tig * F::CH + kchan<BITS>(kb, hi, 1);
+        bq[kb][hi] = pack_h2(hok ? load_q(a, c0) : 0.f, hok ? load_q(a, c1) : 0.f);
+      }
+
+    const int ngroups = n / F::PPG;
+    for (int grp = 0; grp < ngroups; ++grp) {
+      if (lane == 0 && grp + 1 < ngroups) issue_meta(grp + 1);
+      mbar_wait(&bars[kStages + (grp & 1)], (grp >> 1) & 1, a.err);
+      // per-channel (step, zero) pairs of this key group as f16x2
+      uint32_t ks[F::NKB][2], kz[F::NKB][2];
+      const uint32_t* mwords = reinterpret_cast<const uint32_t*>(meta + (grp & 1) * F::META);
 #pragma unroll
-    for (int w = 0; w < kDecodeWarps; ++w) {
-      const float* sw = reinterpret_cast<const float*>(smem + 512 + w * a.warp_smem);
-      M = fmaxf(M, sw[hd]);
-    }
-    float L = 0.f, O = 0.f;
-    if (M != -INFINITY) {
+      for (int kb = 0; kb < F::NKB; ++kb)
 #pragma unroll
-      for (int w = 0; w < kDecodeWarps; ++w) {
-        const float* sw = reinterpret_cast<const float*>(smem + 512 + w * a.warp_smem);
-        const float mw = sw[hd];
-        if (mw == -INFINITY) continue;
-        const float f = fast_exp2(mw - M);
-        L = fmaf(sw[8 + hd], f, L);
-        O = fmaf(sw[16 + hd * D + c], f, O);
+        for (int hi = 0; hi < 2; ++hi) {
+          const uint32_t m0 = mwords[tig * F::CH + kchan<BITS>(kb, hi, 0)];
+          const uint32_t m1 = mwords[tig * F::CH + kchan<BITS>(kb, hi, 1)];
+          ks[kb][hi] = __byte_perm(m0, m1, 0x5410);
+          kz[kb][hi] = __byte_perm(m0, m1, 0x7632);
+        }
+      for (int pi = 0; pi < F::PPG; ++pi) {
+        const int u = grp * F::PPG + pi;
+        mbar_wait(&bars[u % kStages], (u / kStages) & 1, a.err);
+        const uint8_t* pg = ring + (u % kStages) * F::STAGE;
+        // ---- S^T = K Q^T ----
+        uint32_t wg[F::TW], wh[F::TW];
+        load_key_words<D, BITS>(pg, g, tig, wg, wh);
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kb = 0; kb < F::NKB; ++kb) {
+          uint32_t r[4];
+          switch (kb) {
+#define TKV_KF(K)                                                                              \
+  case K:                                                                                      \
+    key_frag<BITS, (K < F::NKB ? K : 0)>(wg, wh, ks[K < F::NKB ? K : 0], kz[K < F::NKB ? K : 0], \
+                                         r);                                                   \
+    break;
+            TKV_KF(0) TKV_KF(1) TKV_KF(2) TKV_KF(3) TKV_KF(4) TKV_KF(5) TKV_KF(6) TKV_KF(7)
+#undef TKV_KF
+          }
+          mma16816(s, r[0], r[1], r[2], r[3], bq[kb][0], bq[kb][1]);
+        }
+        s[0] = hv0 ? s[0] * a.alpha : -INFINITY;
+        s[1] = hv1 ? s[1] * a.alpha : -INFINITY;
+        s[2] = hv0 ? s[2] * a.alpha : -INFINITY;
+        s[3] = hv1 ? s[3] * a.alpha : -INFINITY;
+        softmax_tile<D, NVG>(st, s);
+        // ---- O^T += V^T P'^T, P' = p * step_v (per token) ----
+        uint32_t vw[F::VWN];
+        load_value_words<D, BITS>(pg + F::V_CODES_OFF, lane, vw);
+        const uint32_t* vm = reinterpret_cast<const uint32_t*>(pg + F::V_META_OFF);
+#pragma unroll
+        for (int vg = 0; vg < NVG; ++vg) {
+          const float2 sza = unpack_h2(vm[g * NVG + vg]);
+          const float2 szb = unpack_h2(vm[(g + 8) * NVG + vg]);
+          const uint32_t h2a = pack_h2(s[0] * sza.x, s[1] * sza.x);
+          const uint32_t h2b = pack_h2(s[2] * szb.x, s[3] * szb.x);
+          const float2 ra = unpack_h2(h2a), rb = unpack_h2(h2b);
+          st.w[vg][0] += s[0] * sza.y + s[2] * szb.y - 16.f * (ra.x + rb.x);
+          st.w[vg][1] += s[1] * sza.y + s[3] * szb.y - 16.f * (ra.y + rb.y);
+          uint32_t b01, b23;
+          p_to_bfrag(h2a, h2b, lane, b01, b23);
+#pragma unroll
+          for (int k = 0; k < F::MB_PER_VG; ++k) {
+            const int mb = vg * F::MB_PER_VG + k;
+            uint32_t r[4];
+            switch (mb) {
+#define TKV_VF(M)                                         \
+  case M:                                                 \
+    value_frag<BITS, (M < D / 16 ? M : 0)>(vw, r);        \
+    break;
+              TKV_VF(0) TKV_VF(1) TKV_VF(2) TKV_VF(3) TKV_VF(4) TKV_VF(5) TKV_VF(6) TKV_VF(7)
+#undef TKV_VF
+            }
+            mma16816(st.o[mb], r[0], r[1], r[2], r[3], b01, b23);
+          }
+        }
+        __syncwarp();
+        if (lane == 0 && u + kStages < n) issue_page(u + kStages);
       }
     }
-    a.part_o[(ml_base + hd) * D + c] = O;
-    if (c == 0) {
-      a.part_ml[(ml_base + hd) * 2 + 0] = M;
-      a.part_ml[(ml_base + hd) * 2 + 1] = L;
+    write_partial<D, NVG>(a, st, ml_base, true);
+    return;
+  }
+
+  // =================== fp16 residual ring ===================
+  constexpr int CHUNK = 2 * kPage * D * 2;  // K block + V block of 16 tokens
+  const int64_t chunks_per_row = a.ring_cap / kPage;
+  const uint8_t* ring_base = reinterpret_cast<const uint8_t*>(a.ring) +
+                             (((int64_t)row * a.n_kv_heads + h) * chunks_per_row) * CHUNK;
+  const int n = n_units;  // 2*RU units per 16-token chunk: K halves then V halves
+  constexpr int UPC = 2 * F::RU;
+  auto issue_unit = [&](int u) {  // lane 0
+    const int ci = u / UPC, part = u % UPC;
+    const int tok = nq + ci * kPage;
+    const int chunk = (tok % a.ring_cap) / kPage;
+    uint64_t* bar = &bars[u % kStages];
+    mbar_arrive_expect_tx(bar, F::RUNIT);
+    bulk_g2s(ring + (u % kStages) * F::STAGE,
+             ring_base + (int64_t)chunk * CHUNK + (int64_t)part * F::RUNIT, F::RUNIT, bar);
+  };
+  int issued = min(kStages, n);
+  if (lane == 0)
+    for (int u = 0; u < issued; ++u) issue_unit(u);
+  uint32_t bq[F::NKB][2];
+#pragma unroll
+  for (int kb = 0; kb < F::NKB; ++kb)
+#pragma unroll
+    for (int hi = 0; hi < 2; ++hi) {
+      const int c = 16 * kb + 2 * tig + 8 * hi;
+      bq[kb][hi] = pack_h2(hok ? load_q(a, qrow + c) : 0.f, hok ? load_q(a, qrow + c + 1) : 0.f);
+    }
+  const int n_chunks = n / UPC;
+  for (int ci = 0; ci < n_chunks; ++ci) {
+    for (int p = 0; p < UPC; ++p) {
+      const int u = ci * UPC + p;
+      mbar_wait(&bars[u % kStages], (u / kStages) & 1, a.err);
+    }
+    const int tb = nq + ci * kPage;
+    const bool vg0 = tb + g < len, vg8 = tb + g + 8 < len;
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kb = 0; kb < F::NKB; ++kb) {
+      const int u = ci * UPC + kb / 4;  // 4 k-blocks per 2 KB unit
+      const uint8_t* ck = ring + (u % kStages) * F::STAGE;
+      const uint4 x = *reinterpret_cast<const uint4*>(ck + ((kb % 4) * 32 + lane) * 16);
+      mma16816(s, x.x, x.y, x.z, x.w, bq[kb][0], bq[kb][1]);
+    }
+    s[0] = (hv0 && vg0) ? s[0] * a.alpha : -INFINITY;
+    s[1] = (hv1 && vg0) ? s[1] * a.alpha : -INFINITY;
+    s[2] = (hv0 && vg8) ? s[2] * a.alpha : -INFINITY;
+    s[3] = (hv1 && vg8) ? s[3] * a.alpha : -INFINITY;
+    softmax_tile<D, NVG>(st, s);
+    uint32_t b01, b23;
+    p_to_bfrag(pack_h2(s[0], s[1]), pack_h2(s[2], s[3]), lane, b01, b23);
+    // zero the V^T columns of tokens past the end (stale ring slots)
+    const int t0 = tb + 2 * tig;
+    const uint32_t m01 = (t0 < len ? 0x0000ffffu : 0u) | (t0 + 1 < len ? 0xffff0000u : 0u);
+    const uint32_t m23 = (t0 + 8 < len ? 0x0000ffffu : 0u) | (t0 + 9 < len ? 0xffff0000u : 0u);
+#pragma unroll
+    for (int mb = 0; mb < D / 16; ++mb) {
+      const int u = ci * UPC + F::RU + mb / 4;
+      const uint8_t* cv = ring + (u % kStages) * F::STAGE;
+      const uint4 x = *reinterpret_cast<const uint4*>(cv + ((mb % 4) * 32 + lane) * 16);
+      mma16816(st.o[mb], x.x & m01, x.y & m01, x.z & m23, x.w & m23, b01, b23);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      const int lim = min(n, (ci + 1) * UPC + kStages);
+      for (; issued < lim; ++issued) issue_unit(issued);
     }
   }
+  write_partial<D, NVG>(a, st, ml_base, false);
 }
 
 // ---------------------------------------------------------------------------
@@ -600,54 +586,37 @@ __global__ void __launch_bounds__(128) merge_kernel(const float* __restrict__ pa
 // ---------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------
-template <int D, int BITS, int NVG>
-static int launch_split_t(const DecodeArgs& a, dim3 grid, size_t smem, cudaStream_t stream) {
+template <int D, int BITS, int G>
+static int launch_warp_t(const DecodeArgs& a, dim3 grid, cudaStream_t stream) {
+  constexpr int smem = decode_smem_bytes<D, BITS, G>();
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(decode_split_kernel<D, BITS, NVG>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             227 * 1024) != cudaSuccess)
+    if (cudaFuncSetAttribute(decode_warp_kernel<D, BITS, G>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return TKV_BACKEND_ERROR;
     attr = true;
   }
-  decode_split_kernel<D, BITS, NVG><<<grid, kDecodeWarps * 32, smem, stream>>>(a);
+  decode_warp_kernel<D, BITS, G><<<grid, 32, smem, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
 }
 
 template <int D, int BITS>
-static int launch_split_d(const DecodeArgs& a, int nvg, dim3 grid, size_t smem,
-                          cudaStream_t stream) {
-  switch (nvg) {
-    case 1: return launch_split_t<D, BITS, 1>(a, grid, smem, stream);
-    case 2: return launch_split_t<D, BITS, 2>(a, grid, smem, stream);
-    case 4: return launch_split_t<D, BITS, 4>(a, grid, smem, stream);
-    case 8:
-      if constexpr (D / 16 >= 8) return launch_split_t<D, BITS, 8>(a, grid, smem, stream);
-      break;
+static int launch_warp_g(const DecodeArgs& a, dim3 grid, cudaStream_t stream) {
+  switch (a.group) {
+    case 16: return launch_warp_t<D, BITS, 16>(a, grid, stream);
+    case 32: return launch_warp_t<D, BITS, 32>(a, grid, stream);
+    case 64: return launch_warp_t<D, BITS, 64>(a, grid, stream);
+    case 128: return launch_warp_t<D, BITS, 128>(a, grid, stream);
   }
   return TKV_NOT_IMPLEMENTED;
 }
 
-int warp_smem_bytes(int head_dim, int64_t page_bytes) {
-  const int64_t quant = kPagesPerWarp * page_bytes;
-  const int64_t resid = 2 * (2 * kPage * head_dim * 2);
-  const int64_t stage = (16 + 8 * head_dim) * 4;
-  int64_t m = quant > resid ? quant : resid;
-  m = m > stage ? m : stage;
-  return static_cast<int>((m + 127) / 128 * 128);
-}
-
-int launch_decode_splits(DecodeArgs a, int head_dim, int bits, int n_vgroups, cudaStream_t stream) {
-  a.warp_smem = warp_smem_bytes(head_dim, a.page_bytes);
-  const size_t smem = 512 + static_cast<size_t>(kDecodeWarps) * a.warp_smem;
-  if (smem > 227 * 1024) return TKV_NOT_IMPLEMENTED;
+int launch_decode_splits(DecodeArgs a, int head_dim, int bits, int, cudaStream_t stream) {
   dim3 grid(a.n_slots, a.n_kv_heads, a.num_seqs);
   if (head_dim == 128)
-    return bits == 4 ? launch_split_d<128, 4>(a, n_vgroups, grid, smem, stream)
-                     : launch_split_d<128, 2>(a, n_vgroups, grid, smem, stream);
+    return bits == 4 ? launch_warp_g<128, 4>(a, grid, stream) : launch_warp_g<128, 2>(a, grid, stream);
   if (head_dim == 64)
-    return bits == 4 ? launch_split_d<64, 4>(a, n_vgroups, grid, smem, stream)
-                     : launch_split_d<64, 2>(a, n_vgroups, grid, smem, stream);
+    return bits == 4 ? launch_warp_g<64, 4>(a, grid, stream) : launch_warp_g<64, 2>(a, grid, stream);
   return TKV_NOT_IMPLEMENTED;
 }
 
