@@ -262,6 +262,7 @@ def run_kivi(args):
     part_ml = torch.empty((S, w.B, w.Hq, 2), dtype=torch.float32, device=dev)
     part_o = torch.empty((S, w.B, w.Hq, w.D), dtype=torch.float32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
+    work = torch.zeros(2, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
 
     def step(ev=None):
@@ -269,7 +270,7 @@ def run_kivi(args):
         if ev is not None:
             ev[0].record(stream)
         ops.paged_decode_partials(cache, q, bt, lens, 0, S - 1, True, part_ml, part_o,
-                                  scale=scale, err=err, stream=stream)
+                                  scale=scale, err=err, work=work, stream=stream)
         if ev is not None:
             ev[1].record(stream)
         ops.merge_partials(part_ml, part_o, out, stream=stream)
@@ -308,7 +309,7 @@ def run_kivi(args):
     out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
     q_dev = torch.empty_like(q)
     lens_dev = torch.empty_like(lens)
-    ws = torch.empty(ops.decode_workspace_bytes(w.B, w.Hq, w.D, max_ctx), dtype=torch.uint8,
+    ws = torch.zeros(ops.decode_workspace_bytes(w.B, w.Hq, w.D, max_ctx), dtype=torch.uint8,
                      device=dev)
 
     def e2e_step():

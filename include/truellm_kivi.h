@@ -184,7 +184,10 @@ TKV_API int tkv_paged_append(const tkv_cache_t* cache, const void* k_new, const 
 /* Number of split slots per sequence: ceil(max_context_len / TKV_SPLIT_TOKENS) + 1
  * (the last one holds the fp16 residual). */
 TKV_API int tkv_decode_num_splits(int max_context_len);
-/* Workspace bytes for tkv_paged_decode. */
+/* Workspace bytes for tkv_paged_decode.  The first 256 bytes hold the split
+ * kernel's work counters: zero them once when the workspace is allocated; every
+ * call leaves them zero again.  Calls that share a workspace must not overlap
+ * on the GPU. */
 TKV_API size_t tkv_decode_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
                                   int max_context_len);
 
@@ -207,13 +210,15 @@ TKV_API int tkv_paged_decode(const tkv_cache_t* cache, const void* q, int q_dtyp
  *   part_ml [n_split_slots][num_seqs][num_q_heads][2] f32  (m in log2 units, l)
  *   part_o  [n_split_slots][num_seqs][num_q_heads][D] f32  (unnormalised)
  * slot index = split - split_lo for quantised splits and split_hi - split_lo
- * for the residual.  Empty slots get m = -inf, l = 0. */
+ * for the residual.  Empty slots get m = -inf, l = 0.  work: 8 bytes of
+ * device memory, zero before the first call and left zero by every call
+ * (the persistent kernel's work counters). */
 TKV_API int tkv_paged_decode_partials(const tkv_cache_t* cache, const void* q, int q_dtype,
                               const int32_t* block_tables, int max_blocks_per_seq,
                               const int32_t* seq_lens, const int32_t* seq_slots, int num_seqs,
                               int num_q_heads, float scale, int split_lo, int split_hi,
-                              int include_residual, float* part_ml, float* part_o, int* err_flag,
-                              void* stream);
+                              int include_residual, float* part_ml, float* part_o, void* work,
+                              int* err_flag, void* stream);
 
 /* Log-sum-exp merge of n_slots partial sets laid out as above
  * (paged_attention_v2.cu:132-170) into out [num_seqs, num_q_heads, D]. */

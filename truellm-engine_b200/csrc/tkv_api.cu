@@ -222,12 +222,14 @@ int tkv_decode_num_splits(int max_context_len) {
   return (max_context_len + TKV_SPLIT_TOKENS - 1) / TKV_SPLIT_TOKENS + 1;
 }
 
+static constexpr size_t kWorkBytes = 256;  // work counters at the start of the workspace
+
 size_t tkv_decode_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
                                   int max_context_len) {
   if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || max_context_len < 0) return 0;
   const size_t slots = (size_t)tkv_decode_num_splits(max_context_len);
   const size_t n = slots * (size_t)num_seqs * (size_t)num_q_heads;
-  return n * 2 * sizeof(float) + n * (size_t)head_dim * sizeof(float);
+  return kWorkBytes + n * 2 * sizeof(float) + n * (size_t)head_dim * sizeof(float);
 }
 
 static int decode_partials_impl(const tkv_cache_t* cache, const void* q, int q_dtype,
@@ -235,7 +237,7 @@ static int decode_partials_impl(const tkv_cache_t* cache, const void* q, int q_d
                                 const int32_t* seq_lens, const int32_t* seq_slots, int num_seqs,
                                 int num_q_heads, float scale, int split_lo, int split_hi,
                                 int include_residual, float* part_ml, float* part_o,
-                                int* err_flag, cudaStream_t stream) {
+                                void* work, int* err_flag, cudaStream_t stream) {
   if (!cache_ok(cache)) return TKV_INVALID_ARGUMENT;
   const tkv_format_t& f = cache->fmt;
   if (q_dtype != TKV_F16 && q_dtype != TKV_BF16) return TKV_NOT_IMPLEMENTED;
@@ -243,7 +245,8 @@ static int decode_partials_impl(const tkv_cache_t* cache, const void* q, int q_d
   if (num_q_heads % f.n_kv_heads != 0) return TKV_INVALID_ARGUMENT;
   const int grp = num_q_heads / f.n_kv_heads;
   if (grp > 8) return TKV_NOT_IMPLEMENTED;  // one mma n-tile of 8 q heads per kv head
-  if (!q || !block_tables || !seq_lens || !part_ml || !part_o || max_blocks_per_seq <= 0)
+  if (!q || !block_tables || !seq_lens || !part_ml || !part_o || !work ||
+      max_blocks_per_seq <= 0)
     return TKV_INVALID_ARGUMENT;
   if (split_lo < 0 || split_hi < split_lo || !(scale > 0.f) || !isfinite(scale))
     return TKV_INVALID_ARGUMENT;
@@ -280,6 +283,7 @@ static int decode_partials_impl(const tkv_cache_t* cache, const void* q, int q_d
   a.n_slots = (split_hi - split_lo) + a.include_residual;
   a.part_ml = part_ml;
   a.part_o = part_o;
+  a.work = static_cast<unsigned int*>(work);
   a.err = err_flag;
   if (a.n_slots == 0) return TKV_OK;
   return launch_decode_splits(a, f.head_dim, f.bits, f.n_vgroups, stream);
@@ -289,11 +293,12 @@ int tkv_paged_decode_partials(const tkv_cache_t* cache, const void* q, int q_dty
                               const int32_t* block_tables, int max_blocks_per_seq,
                               const int32_t* seq_lens, const int32_t* seq_slots, int num_seqs,
                               int num_q_heads, float scale, int split_lo, int split_hi,
-                              int include_residual, float* part_ml, float* part_o, int* err_flag,
-                              void* stream) {
+                              int include_residual, float* part_ml, float* part_o, void* work,
+                              int* err_flag, void* stream) {
   return decode_partials_impl(cache, q, q_dtype, block_tables, max_blocks_per_seq, seq_lens,
                               seq_slots, num_seqs, num_q_heads, scale, split_lo, split_hi,
-                              include_residual, part_ml, part_o, err_flag, as_stream(stream));
+                              include_residual, part_ml, part_o, work, err_flag,
+                              as_stream(stream));
 }
 
 int tkv_merge_partials(const float* part_ml, const float* part_o, int n_slots, int num_seqs,
@@ -319,11 +324,12 @@ int tkv_paged_decode(const tkv_cache_t* cache, const void* q, int q_dtype, void*
   if (workspace_bytes < need || !aligned16(workspace)) return TKV_INVALID_ARGUMENT;
   const int slots = tkv_decode_num_splits(max_context_len);
   const size_t n = (size_t)slots * num_seqs * num_q_heads;
-  float* part_ml = static_cast<float*>(workspace);
+  void* work = workspace;
+  float* part_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWorkBytes);
   float* part_o = part_ml + 2 * n;
   int st = decode_partials_impl(cache, q, q_dtype, block_tables, max_blocks_per_seq, seq_lens,
                                 seq_slots, num_seqs, num_q_heads, scale, 0, slots - 1, 1, part_ml,
-                                part_o, err_flag, as_stream(stream));
+                                part_o, work, err_flag, as_stream(stream));
   if (st != TKV_OK) return st;
   return tkv_merge_partials(part_ml, part_o, slots, num_seqs, num_q_heads, D, out, out_dtype,
                             stream);

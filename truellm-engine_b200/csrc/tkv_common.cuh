@@ -17,10 +17,12 @@ namespace tkv {
 constexpr int kPage = TKV_PAGE_SIZE;
 constexpr int kSplitTokens = TKV_SPLIT_TOKENS;
 constexpr int kSplitPages = kSplitTokens / kPage;  // 32
-// A bounded mbarrier wait gives up after this many try_wait polls (each poll
-// may itself suspend the thread for a hardware-chosen time), then reports
-// TKV_ERR_TIMEOUT instead of spinning forever.
-constexpr uint32_t kMaxPolls = 1u << 22;
+// A bounded mbarrier wait gives up after this many try_wait polls, each of
+// which suspends the thread for at most kSuspendNs while the phase is still
+// open (about 2 s in total), then reports TKV_ERR_TIMEOUT instead of
+// spinning forever.
+constexpr uint32_t kMaxPolls = 2000;
+constexpr uint32_t kSuspendNs = 1000000;
 
 __device__ __forceinline__ void set_err(int* err, int bit) {
   if (err) atomicOr(err, bit);
@@ -57,11 +59,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   asm volatile(
       "{\n"
       ".reg .pred p;\n"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       "selp.u32 %0, 1, 0, p;\n"
       "}\n"
       : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return done != 0;
 }
@@ -107,18 +109,26 @@ __device__ __forceinline__ float2 unpack_h2(uint32_t u) {
   return __half22float2(h);
 }
 
+// (x & mask) | bits as one LOP3.  Keeping both constants in registers lets
+// ptxas emit a single LOP3 (SASS LOP3 takes at most one immediate).
+__device__ __forceinline__ uint32_t and_or(uint32_t x, uint32_t mask, uint32_t bits) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(r) : "r"(x), "r"(mask), "r"(bits));
+  return r;
+}
+
 // Codes -> f16 pairs holding 1 + code/16 (exact).  For 4-bit codes the pair is
 // the nibbles at bits [s0, s0+4) and [s0+16, s0+20) of w; for 2-bit codes the
 // 2-bit fields at the same positions.  SHIFT moves bit s0 to bit 6.
 template <int SHIFT>
 __device__ __forceinline__ uint32_t ext4(uint32_t w) {
   uint32_t x = SHIFT >= 0 ? (w << SHIFT) : (w >> (-SHIFT));
-  return (x & 0x03C003C0u) | 0x3C003C00u;
+  return and_or(x, 0x03C003C0u, 0x3C003C00u);
 }
 template <int SHIFT>
 __device__ __forceinline__ uint32_t ext2(uint32_t w) {
   uint32_t x = SHIFT >= 0 ? (w << SHIFT) : (w >> (-SHIFT));
-  return (x & 0x00C000C0u) | 0x3C003C00u;
+  return and_or(x, 0x00C000C0u, 0x3C003C00u);
 }
 
 // Codes -> exact integer-valued f16 pairs.  lop3 ORs the masked code bits
@@ -130,7 +140,7 @@ __device__ __forceinline__ uint32_t code_pair(uint32_t w) {
   constexpr int k = lo == 0x000fu || lo == 0x0003u ? 0 : lo == 0x000cu ? 2 : lo == 0x00f0u || lo == 0x0030u ? 4 : 6;
   constexpr uint32_t mul = k == 0 ? 0x3C003C00u : k == 2 ? 0x34003400u : k == 4 ? 0x2C002C00u : 0x24002400u;
   constexpr uint32_t add = k == 0 ? 0xE400E400u : k == 2 ? 0xDC00DC00u : k == 4 ? 0xD400D400u : 0xCC00CC00u;
-  uint32_t x = (w & MASK) | 0x64006400u;
+  uint32_t x = and_or(w, MASK, 0x64006400u);
   uint32_t r;
   asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(r) : "r"(x), "r"(mul), "r"(add));
   return r;
@@ -143,7 +153,13 @@ __device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
   return d;
 }
 
-__device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
+// 2^x with the hardware approximation (ex2.approx, relative error ~2^-22;
+// 2^-inf = +0).  Used for softmax weights and LSE merge factors.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // ---------------------------------------------------------------------------
 // reference quantizer arithmetic (kivi_cache.cu:92-124), IEEE ops spelled out
@@ -204,7 +220,6 @@ struct DecodeArgs {
   int num_pages, max_seqs, n_kv_heads, group, residual, ring_cap;
   int k_codes_off, v_codes_off, v_meta_off, k_meta_off, k_meta_slice;
   int64_t page_bytes;
-  int warp_smem;  // bytes of shared memory per warp
   const void* q;
   bool q_bf16;
   const int32_t* block_tables;
@@ -214,6 +229,8 @@ struct DecodeArgs {
   int num_seqs, num_q_heads, grp;
   float alpha;  // scale * log2(e)
   int split_lo, split_hi, include_residual, n_slots;
+  int n_items;              // n_slots * num_seqs * n_kv_heads
+  unsigned int* work;       // [0] next work item, [1] finished warps; zero between launches
   float* part_ml;
   float* part_o;
   int* err;

@@ -6,17 +6,19 @@
 // score = scale * q.k, kv_head = q_head / (Hq/Hkv), max-subtracted softmax,
 // out = sum p v, fp32 accumulation.
 //
-// Work decomposition (flash-decoding): grid = (split slot, kv head, sequence).
-// A quantised split covers TKV_SPLIT_TOKENS = 512 tokens = 32 pages; each of
-// the CTA's 4 warps owns 8 consecutive pages (one 128-token key group at
-// G = 128).  The last slot of a sequence covers the fp16 residual ring.  Every
-// CTA writes one unnormalised partial (m, l, o[D]) per q head; a second
-// kernel merges the partials with the log-sum-exp rule of
-// paged_attention_v2.cu:132-170.
+// Work decomposition (flash-decoding): a work item is (split slot, sequence,
+// kv head).  A quantised split covers TKV_SPLIT_TOKENS = 512 tokens = 32
+// pages; one more slot per sequence covers the fp16 residual ring.  The split
+// kernel is persistent: one warp per CTA, as many CTAs as fit on the GPU, each
+// taking items from a global counter until none are left.  Every item leaves
+// one unnormalised partial (m, l, o[D]) per q head; a second kernel merges the
+// partials with the log-sum-exp rule of paged_attention_v2.cu:132-170.
 //
 // Per warp:
-//   * lane 0 issues one 1-D TMA bulk copy (cp.async.bulk, no multicast) per
-//     (page, head) block into shared memory, completing on an mbarrier;
+//   * a 6-stage ring in shared memory, filled by 1-D TMA bulk copies
+//     (cp.async.bulk, no multicast) of each page's codes + value meta, one
+//     mbarrier per stage; the key-group meta slices are fetched one group
+//     ahead into a double buffer;
 //   * QK^T runs on the tensor cores as S^T[16 tokens x 8 heads] =
 //     K[16 x D] * Q^T[D x 8] with mma.m16n8k16 (f16 in, f32 accumulate).
 //     A fragments are built straight from the packed codes in registers: a
@@ -88,14 +90,29 @@ __device__ __forceinline__ void key_frag(const uint32_t* wg, const uint32_t* wh,
 }
 
 // A-fragment registers of m-block MB of V^T from the lane's value-code words.
+// 4-bit codes: each register pair becomes 64 + c exactly (the nibble is moved
+// to mantissa bits 4..7 of 64.0); 2-bit codes: 1 + c/16.  In both cases
+// value = kVScale * reg - kVBeta with the constants below.
+// 4-bit codes: tokens 0-7 of the page (k-slots of b01) become 1024 + c, tokens
+// 8-15 become 64 + c (nibbles OR-ed into the mantissas of 1024.0 and 64.0);
+// value = reg - beta with beta = 1024 / 64 for the two token halves.
+// 2-bit codes: 1 + c/16 for both halves, value = 16 * reg - 16.
+template <int BITS> struct VEnc;
+template <> struct VEnc<4> {
+  static constexpr float kScale = 1.f, kBetaLo = 1024.f, kBetaHi = 64.f;
+};
+template <> struct VEnc<2> {
+  static constexpr float kScale = 16.f, kBetaLo = 16.f, kBetaHi = 16.f;
+};
+
 template <int BITS, int MB>
 __device__ __forceinline__ void value_frag(const uint32_t* vw, uint32_t (&r)[4]) {
   if (BITS == 4) {
-    const uint32_t w = vw[MB];
-    r[0] = ext4<6>(w);   // k=0: rows g,   tokens 2tig, 2tig+1
-    r[2] = ext4<2>(w);   // k=1: rows g,   tokens +8
-    r[1] = ext4<-2>(w);  // k=2: rows g+8, tokens 2tig, 2tig+1
-    r[3] = ext4<-6>(w);  // k=3: rows g+8, tokens +8
+    const uint32_t w = vw[MB], w8 = w >> 8;
+    r[0] = and_or(w, 0x000F000Fu, 0x64006400u);   // nibbles 0,4: rows g,   tokens 2tig, 2tig+1
+    r[2] = and_or(w, 0x00F000F0u, 0x54005400u);   // nibbles 1,5: rows g,   tokens +8
+    r[1] = and_or(w8, 0x000F000Fu, 0x64006400u);  // nibbles 2,6: rows g+8, tokens 2tig, 2tig+1
+    r[3] = and_or(w8, 0x00F000F0u, 0x54005400u);  // nibbles 3,7: rows g+8, tokens +8
   } else {
     const uint32_t w = vw[MB / 2];
     constexpr int base = 4 * (MB % 2);
@@ -122,24 +139,36 @@ struct WarpState {
   }
 };
 
-// Online-softmax update for one 16-token tile.  s[4]: S^T accumulator
-// (rows g, g+8; cols 2tig, 2tig+1), already in log2 units; invalid entries
-// must be -inf.  Returns p in s.
-template <int D, int NVG>
-__device__ __forceinline__ void softmax_tile(WarpState<D, NVG>& st, float (&s)[4]) {
+// Running maxima are only raised when a tile's maximum exceeds them by more
+// than kLazyLog2 (log2 units), so most tiles skip the O rescale; weights are
+// then at most 2^kLazyLog2 = 4, which keeps p * step_v inside the f16 range for
+// any fp16 value range (step_v <= 131008 / 15).
+constexpr float kLazyLog2 = 2.0f;
+
+// Online-softmax update for NP 16-token tiles.  s[p][4]: raw S^T accumulators
+// (rows g, g+8; cols = heads 2tig, 2tig+1), masked entries -inf; alpha =
+// softmax scale * log2(e).  Replaces s by the unnormalised weights
+// p = 2^(alpha * s - m) (m in log2 units).
+template <int D, int NVG, int NP>
+__device__ __forceinline__ void softmax_update(WarpState<D, NVG>& st, float (&s)[NP][4],
+                                               float alpha) {
+  float t[2];
 #pragma unroll
   for (int hh = 0; hh < 2; ++hh) {
-    float t = fmaxf(s[hh], s[2 + hh]);
-    t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, 4));
-    t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, 8));
-    t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, 16));
-    const float mnew = fmaxf(st.m[hh], t);
-    // mnew == -inf only when every score so far is masked: keep p = 0 then.
-    const float msafe = (mnew == -INFINITY) ? 0.f : mnew;
-    const float r = fast_exp2(st.m[hh] - msafe);
-    s[hh] = fast_exp2(s[hh] - msafe);
-    s[2 + hh] = fast_exp2(s[2 + hh] - msafe);
-    if (r != 1.f) {
+    float x = fmaxf(s[0][hh], s[0][2 + hh]);
+#pragma unroll
+    for (int p = 1; p < NP; ++p) x = fmaxf(x, fmaxf(s[p][hh], s[p][2 + hh]));
+    x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 4));
+    x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 8));
+    x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 16));
+    t[hh] = x * alpha;  // raw scores: alpha > 0 keeps the order
+  }
+  const bool need = t[0] > st.m[0] + kLazyLog2 || t[1] > st.m[1] + kLazyLog2;
+  if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const float mnew = fmaxf(st.m[hh], t[hh]);
+      const float r = st.m[hh] == -INFINITY ? 0.f : fast_exp2(st.m[hh] - mnew);
       st.l[hh] *= r;
 #pragma unroll
       for (int v = 0; v < NVG; ++v) st.w[v][hh] *= r;
@@ -148,9 +177,20 @@ __device__ __forceinline__ void softmax_tile(WarpState<D, NVG>& st, float (&s)[4
         st.o[i][hh] *= r;
         st.o[i][2 + hh] *= r;
       }
+      st.m[hh] = mnew;
     }
-    st.l[hh] += s[hh] + s[2 + hh];
-    st.m[hh] = mnew;
+  }
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const float nbase = st.m[hh] == -INFINITY ? 0.f : -st.m[hh];
+    float sum = 0.f;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      s[p][hh] = fast_exp2(fmaf(s[p][hh], alpha, nbase));
+      s[p][2 + hh] = fast_exp2(fmaf(s[p][2 + hh], alpha, nbase));
+      sum += s[p][hh] + s[p][2 + hh];
+    }
+    st.l[hh] += sum;
   }
 }
 
@@ -195,20 +235,18 @@ struct Fmt {
   static constexpr int PB = (BODY + KMS + 15) / 16 * 16;     // page_bytes
   static constexpr int PPG = G / kPage;                      // pages per key group
   static constexpr int META = D * 4;                         // key meta bytes per group
-  static constexpr int RUNIT = 2048;                         // residual copy unit
-  static constexpr int RU = (kPage * D * 2) / RUNIT;         // units per residual K or V block
-  static constexpr int STAGE = ((BODY > RUNIT ? BODY : RUNIT) + 127) / 128 * 128;
+  static constexpr int NP = PPG >= 2 ? 2 : 1;                // pages per ring stage / softmax step
+  static constexpr int RBLK = kPage * D * 2;                 // residual K (or V) block of a chunk
+  static constexpr int SB = ((NP * BODY > RBLK ? NP * BODY : RBLK) + 127) / 128 * 128;
+  static constexpr int ST = (13312 / SB) < 2 ? 2 : (13312 / SB) > 8 ? 8 : (13312 / SB);  // stages
   static_assert(TW >= 1 && (RB % 16) == 0, "key row split");
   static_assert((KMS % 16) == 0 && (BODY % 16) == 0, "bulk-copy sizes are multiples of 16");
 };
 
-constexpr int kStages = 6;                    // ring stages per warp
-constexpr int kBars = kStages + 2;            // ring barriers + 2 key-meta barriers
-
 template <int D, int BITS, int G>
 constexpr int decode_smem_bytes() {
   using F = Fmt<D, BITS, G>;
-  return 128 + kStages * F::STAGE + 2 * F::META;
+  return 128 + F::ST * F::SB + 2 * F::META;
 }
 
 // Loads the thread's 8 (or fewer) key-code words of rows g and g+8.
@@ -252,7 +290,7 @@ __device__ __forceinline__ void load_value_words(const uint8_t* vc, int lane,
 // Writes this warp's partial (m, l, o[D]) for the q heads of kv head h.
 template <int D, int NVG>
 __device__ __forceinline__ void write_partial(const DecodeArgs& a, WarpState<D, NVG>& st,
-                                              int64_t ml_base, bool quantized) {
+                                              int64_t ml_base, float oscale) {
   const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
   constexpr int MB_PER_VG = (D / 16) / NVG;
 #pragma unroll
@@ -279,11 +317,9 @@ __device__ __forceinline__ void write_partial(const DecodeArgs& a, WarpState<D, 
 #pragma unroll
     for (int mb = 0; mb < D / 16; ++mb) {
       const int vg = mb / MB_PER_VG;
-      float o0 = st.o[mb][hh], o1 = st.o[mb][2 + hh];
-      if (quantized) {  // O^T = 16 * acc + value-zero correction
-        o0 = fmaf(16.f, o0, st.w[vg][hh]);
-        o1 = fmaf(16.f, o1, st.w[vg][hh]);
-      }
+      // O^T = oscale * acc + value-zero correction (0 for the fp16 ring)
+      const float o0 = fmaf(oscale, st.o[mb][hh], st.w[vg][hh]);
+      const float o1 = fmaf(oscale, st.o[mb][2 + hh], st.w[vg][hh]);
       po[16 * mb + g] = o0;
       po[16 * mb + g + 8] = o1;
     }
@@ -295,255 +331,318 @@ __device__ __forceinline__ void write_partial(const DecodeArgs& a, WarpState<D, 
 }
 
 // ---------------------------------------------------------------------------
-// split kernel: one warp per (split slot, kv head, sequence)
+// persistent split kernel: each resident warp takes work items
+// (split slot, sequence, kv head) from a global counter until none are left
 // ---------------------------------------------------------------------------
 template <int D, int BITS, int G>
-__global__ void __launch_bounds__(32, 16) decode_warp_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(32, 15) decode_warp_kernel(DecodeArgs a) {
   using F = Fmt<D, BITS, G>;
-  constexpr int NVG = F::NVG;
+  constexpr int NVG = F::NVG, NP = F::NP, ST = F::ST, SB = F::SB;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);  // ST ring + 2 meta barriers
   uint8_t* ring = smem + 128;
-  uint8_t* meta = ring + kStages * F::STAGE;  // 2 x key-group meta [D][step, zero]
-  const int slot = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  uint8_t* meta = ring + ST * SB;  // 2 x key-group meta [D][step, zero]
   const int lane = threadIdx.x, g = lane >> 2, tig = lane & 3;
-
-  const int64_t ml_base = ((int64_t)slot * a.num_seqs + b) * a.num_q_heads + h * a.grp;
-  const int len = a.seq_lens[b];
-  const bool len_ok = len >= 0 && len <= a.max_blocks * kPage;
-  if (!len_ok && lane == 0 && h == 0 && slot == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
-  const int nq = len_ok ? nq_len(len, a.residual, G) : 0;
+  const bool hok = g < a.grp;
   const int n_qsplit = a.split_hi - a.split_lo;
-  const bool is_res = a.include_residual && slot == n_qsplit;
-  const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
-
-  // ---- what does this warp do? ----
-  int n_units = 0, page_lo = 0, row = 0;
-  if (len_ok && !is_res && slot < n_qsplit) {
-    page_lo = (a.split_lo + slot) * kSplitPages;
-    n_units = min(kSplitPages, nq / kPage - page_lo);  // pages, a multiple of PPG
-    // every block-table entry of the split must name a pool page
-    bool bad = false;
-    for (int i = lane; i < n_units; i += 32) {
-      const int phys = bt[page_lo + i];
-      bad |= phys < 0 || phys >= a.num_pages;
-    }
-    if (__any_sync(0xffffffffu, bad)) {
-      if (lane == 0) set_err(a.err, TKV_ERR_BAD_PAGE);
-      n_units = 0;
-    }
-  } else if (len_ok && is_res && len > nq) {
-    row = a.seq_slots ? a.seq_slots[b] : b;
-    if (row < 0 || row >= a.max_seqs) {
-      if (lane == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
-    } else {
-      n_units = ((len - nq + kPage - 1) / kPage) * 2 * F::RU;
-    }
-  }
-  if (n_units <= 0) {
-    if (lane < a.grp) {
-      a.part_ml[(ml_base + lane) * 2 + 0] = -INFINITY;
-      a.part_ml[(ml_base + lane) * 2 + 1] = 0.f;
-    }
-    return;
-  }
+  const int per_slot = a.num_seqs * a.n_kv_heads;
+  const float alpha = a.alpha;
 
   if (lane == 0) {
-    for (int i = 0; i < kBars; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < ST + 2; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
   }
   __syncwarp();
+  // ring and meta-buffer positions carry over from item to item
+  int stage = 0;
+  uint32_t phase = 0;
+  int gcount = 0;  // key groups consumed so far (meta buffer = gcount & 1)
 
-  WarpState<D, NVG> st;
-  st.init();
-  const bool hv0 = 2 * tig < a.grp, hv1 = 2 * tig + 1 < a.grp;
-  const int hq = h * a.grp + g;
-  const bool hok = g < a.grp;
-  const int64_t qrow = ((int64_t)b * a.num_q_heads + hq) * D;
+  for (;;) {
+    int item = 0;
+    if (lane == 0) item = static_cast<int>(atomicAdd(&a.work[0], 1u));
+    item = __shfl_sync(0xffffffffu, item, 0);
+    if (item >= a.n_items) break;
+    // residual slot first (largest items), then quantised splits in order
+    const int sidx = item / per_slot, rem = item - sidx * per_slot;
+    const int b = rem / a.n_kv_heads, h = rem - b * a.n_kv_heads;
+    const bool is_res = a.include_residual && sidx == 0;
+    const int slot = a.include_residual ? (sidx == 0 ? n_qsplit : sidx - 1) : sidx;
+    const int64_t ml_base = ((int64_t)slot * a.num_seqs + b) * a.num_q_heads + h * a.grp;
+    const int len = a.seq_lens[b];
+    const bool len_ok = len >= 0 && len <= a.max_blocks * kPage;
+    if (!len_ok && lane == 0 && h == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
+    const int nq = len_ok ? nq_len(len, a.residual, G) : 0;
+    const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
 
-  if (!is_res) {
-    // =================== quantised split ===================
-    const int n = n_units;
-    auto issue_page = [&](int u) {  // lane 0
-      const int phys = bt[page_lo + u];
-      uint64_t* bar = &bars[u % kStages];
-      mbar_arrive_expect_tx(bar, F::BODY);
-      bulk_g2s(ring + (u % kStages) * F::STAGE,
-               a.pool + ((int64_t)phys * a.n_kv_heads + h) * F::PB, F::BODY, bar);
-    };
-    auto issue_meta = [&](int grp) {  // lane 0: the group's key-meta slices
-      uint64_t* bar = &bars[kStages + (grp & 1)];
-      mbar_arrive_expect_tx(bar, F::META);
-      for (int i = 0; i < F::PPG; ++i) {
-        const int phys = bt[page_lo + grp * F::PPG + i];
-        bulk_g2s(meta + (grp & 1) * F::META + i * F::KMS,
-                 a.pool + ((int64_t)phys * a.n_kv_heads + h) * F::PB + F::BODY, F::KMS, bar);
+    int n_units = 0, page_lo = 0, row = 0, my_phys = 0;
+    if (len_ok && !is_res) {
+      page_lo = (a.split_lo + slot) * kSplitPages;
+      n_units = min(kSplitPages, nq / kPage - page_lo);  // pages, a multiple of PPG
+      if (n_units > 0) {
+        my_phys = lane < n_units ? bt[page_lo + lane] : 0;
+        if (__any_sync(0xffffffffu, my_phys < 0 || my_phys >= a.num_pages)) {
+          if (lane == 0) set_err(a.err, TKV_ERR_BAD_PAGE);
+          n_units = 0;
+        }
       }
-    };
-    if (lane == 0) {
-      issue_meta(0);
-      for (int u = 0; u < min(kStages, n); ++u) issue_page(u);
+    } else if (len_ok && is_res && len > nq) {
+      row = a.seq_slots ? a.seq_slots[b] : b;
+      if (row < 0 || row >= a.max_seqs) {
+        if (lane == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
+      } else {
+        n_units = ((len - nq + kPage - 1) / kPage) * 2;  // K block + V block per chunk
+      }
     }
-    // B operand: q of head g as exact f16 in this thread's key-channel order
-    uint32_t bq[F::NKB][2];
-#pragma unroll
-    for (int kb = 0; kb < F::NKB; ++kb)
-#pragma unroll
-      for (int hi = 0; hi < 2; ++hi) {
-        const int64_t c0 = qrow + tig * F::CH + kchan<BITS>(kb, hi, 0);
-        const int64_t c1 = qrow + tig * F::CH + kchan<BITS>(kb, hi, 1);
-        bq[kb][hi] = pack_h2(hok ? load_q(a, c0) : 0.f, hok ? load_q(a, c1) : 0.f);
+    if (n_units <= 0) {
+      if (lane < a.grp) {
+        a.part_ml[(ml_base + lane) * 2 + 0] = -INFINITY;
+        a.part_ml[(ml_base + lane) * 2 + 1] = 0.f;
       }
+      continue;
+    }
 
-    const int ngroups = n / F::PPG;
-    for (int grp = 0; grp < ngroups; ++grp) {
-      if (lane == 0 && grp + 1 < ngroups) issue_meta(grp + 1);
-      mbar_wait(&bars[kStages + (grp & 1)], (grp >> 1) & 1, a.err);
-      // per-channel (step, zero) pairs of this key group as f16x2
-      uint32_t ks[F::NKB][2], kz[F::NKB][2];
-      const uint32_t* mwords = reinterpret_cast<const uint32_t*>(meta + (grp & 1) * F::META);
+    WarpState<D, NVG> st;
+    st.init();
+    const int64_t qrow = ((int64_t)b * a.num_q_heads + h * a.grp + g) * D;
+
+    if (!is_res) {
+      // =================== quantised split ===================
+      const int n_steps = n_units / NP;
+      const uint8_t* pool_h = a.pool + (int64_t)h * F::PB;
+      const int64_t page_stride = (int64_t)a.n_kv_heads * F::PB;
+      // step j (NP pages) goes to ring stage stg; whole warp (shuffles), lane 0 issues
+      auto issue_step = [&](int j, int stg) {
+        int phys[NP];
+#pragma unroll
+        for (int p = 0; p < NP; ++p) phys[p] = __shfl_sync(0xffffffffu, my_phys, j * NP + p);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bars[stg], NP * F::BODY);
+#pragma unroll
+          for (int p = 0; p < NP; ++p)
+            bulk_g2s(ring + stg * SB + p * F::BODY, pool_h + phys[p] * page_stride, F::BODY,
+                     &bars[stg]);
+        }
+      };
+      auto issue_meta = [&](int grp, int buf) {  // the group's key-meta slices
+        int phys[F::PPG];
+#pragma unroll
+        for (int i = 0; i < F::PPG; ++i)
+          phys[i] = __shfl_sync(0xffffffffu, my_phys, grp * F::PPG + i);
+        if (lane == 0) {
+          uint64_t* bar = &bars[ST + buf];
+          mbar_arrive_expect_tx(bar, F::META);
+#pragma unroll
+          for (int i = 0; i < F::PPG; ++i)
+            bulk_g2s(meta + buf * F::META + i * F::KMS, pool_h + phys[i] * page_stride + F::BODY,
+                     F::KMS, bar);
+        }
+      };
+      issue_meta(0, gcount & 1);
+      {
+        int s2 = stage;
+        for (int j = 0; j < min(ST, n_steps); ++j) {
+          issue_step(j, s2);
+          s2 = s2 + 1 == ST ? 0 : s2 + 1;
+        }
+      }
+      // B operand: q of head g as exact f16 in this thread's key-channel order
+      uint32_t bq[F::NKB][2];
 #pragma unroll
       for (int kb = 0; kb < F::NKB; ++kb)
 #pragma unroll
         for (int hi = 0; hi < 2; ++hi) {
-          const uint32_t m0 = mwords[tig * F::CH + kchan<BITS>(kb, hi, 0)];
-          const uint32_t m1 = mwords[tig * F::CH + kchan<BITS>(kb, hi, 1)];
-          ks[kb][hi] = __byte_perm(m0, m1, 0x5410);
-          kz[kb][hi] = __byte_perm(m0, m1, 0x7632);
+          const int64_t c0 = qrow + tig * F::CH + kchan<BITS>(kb, hi, 0);
+          const int64_t c1 = qrow + tig * F::CH + kchan<BITS>(kb, hi, 1);
+          bq[kb][hi] = pack_h2(hok ? load_q(a, c0) : 0.f, hok ? load_q(a, c1) : 0.f);
         }
-      for (int pi = 0; pi < F::PPG; ++pi) {
-        const int u = grp * F::PPG + pi;
-        mbar_wait(&bars[u % kStages], (u / kStages) & 1, a.err);
-        const uint8_t* pg = ring + (u % kStages) * F::STAGE;
-        // ---- S^T = K Q^T ----
-        uint32_t wg[F::TW], wh[F::TW];
-        load_key_words<D, BITS>(pg, g, tig, wg, wh);
-        float s[4] = {0.f, 0.f, 0.f, 0.f};
+
+      const int ngroups = n_units / F::PPG;
+      int j = 0;  // step index within the item
+      for (int grp = 0; grp < ngroups; ++grp, ++gcount) {
+        const int buf = gcount & 1;
+        if (grp + 1 < ngroups) issue_meta(grp + 1, buf ^ 1);
+        mbar_wait(&bars[ST + buf], (gcount >> 1) & 1, a.err);
+        // per-channel (step, zero) pairs of this key group as f16x2
+        uint32_t ks[F::NKB][2], kz[F::NKB][2];
+        const uint32_t* mwords = reinterpret_cast<const uint32_t*>(meta + buf * F::META);
 #pragma unroll
-        for (int kb = 0; kb < F::NKB; ++kb) {
-          uint32_t r[4];
-          switch (kb) {
+        for (int kb = 0; kb < F::NKB; ++kb)
+#pragma unroll
+          for (int hi = 0; hi < 2; ++hi) {
+            const uint32_t m0 = mwords[tig * F::CH + kchan<BITS>(kb, hi, 0)];
+            const uint32_t m1 = mwords[tig * F::CH + kchan<BITS>(kb, hi, 1)];
+            ks[kb][hi] = __byte_perm(m0, m1, 0x5410);
+            kz[kb][hi] = __byte_perm(m0, m1, 0x7632);
+          }
+        for (int pi = 0; pi < F::PPG; pi += NP, ++j) {
+          mbar_wait(&bars[stage], phase, a.err);
+          const uint8_t* sbase = ring + stage * SB;
+          // ---- S^T = K Q^T for NP pages (independent MMA chains).  Columns of
+          //      padded heads (>= grp) see q = 0: their weights are computed and
+          //      never used. ----
+          float sc[NP][4];
+#pragma unroll
+          for (int p = 0; p < NP; ++p) {
+            uint32_t wg[F::TW], wh[F::TW];
+            load_key_words<D, BITS>(sbase + p * F::BODY, g, tig, wg, wh);
+            sc[p][0] = sc[p][1] = sc[p][2] = sc[p][3] = 0.f;
+#pragma unroll
+            for (int kb = 0; kb < F::NKB; ++kb) {
+              uint32_t r[4];
+              switch (kb) {
 #define TKV_KF(K)                                                                              \
   case K:                                                                                      \
     key_frag<BITS, (K < F::NKB ? K : 0)>(wg, wh, ks[K < F::NKB ? K : 0], kz[K < F::NKB ? K : 0], \
                                          r);                                                   \
     break;
-            TKV_KF(0) TKV_KF(1) TKV_KF(2) TKV_KF(3) TKV_KF(4) TKV_KF(5) TKV_KF(6) TKV_KF(7)
+                TKV_KF(0) TKV_KF(1) TKV_KF(2) TKV_KF(3) TKV_KF(4) TKV_KF(5) TKV_KF(6) TKV_KF(7)
 #undef TKV_KF
+              }
+              mma16816(sc[p], r[0], r[1], r[2], r[3], bq[kb][0], bq[kb][1]);
+            }
           }
-          mma16816(s, r[0], r[1], r[2], r[3], bq[kb][0], bq[kb][1]);
-        }
-        s[0] = hv0 ? s[0] * a.alpha : -INFINITY;
-        s[1] = hv1 ? s[1] * a.alpha : -INFINITY;
-        s[2] = hv0 ? s[2] * a.alpha : -INFINITY;
-        s[3] = hv1 ? s[3] * a.alpha : -INFINITY;
-        softmax_tile<D, NVG>(st, s);
-        // ---- O^T += V^T P'^T, P' = p * step_v (per token) ----
-        uint32_t vw[F::VWN];
-        load_value_words<D, BITS>(pg + F::V_CODES_OFF, lane, vw);
-        const uint32_t* vm = reinterpret_cast<const uint32_t*>(pg + F::V_META_OFF);
+          softmax_update<D, NVG, NP>(st, sc, alpha);
+          // ---- O^T += V^T P'^T, P' = p * step_v (per token) ----
 #pragma unroll
-        for (int vg = 0; vg < NVG; ++vg) {
-          const float2 sza = unpack_h2(vm[g * NVG + vg]);
-          const float2 szb = unpack_h2(vm[(g + 8) * NVG + vg]);
-          const uint32_t h2a = pack_h2(s[0] * sza.x, s[1] * sza.x);
-          const uint32_t h2b = pack_h2(s[2] * szb.x, s[3] * szb.x);
-          const float2 ra = unpack_h2(h2a), rb = unpack_h2(h2b);
-          st.w[vg][0] += s[0] * sza.y + s[2] * szb.y - 16.f * (ra.x + rb.x);
-          st.w[vg][1] += s[1] * sza.y + s[3] * szb.y - 16.f * (ra.y + rb.y);
-          uint32_t b01, b23;
-          p_to_bfrag(h2a, h2b, lane, b01, b23);
+          for (int p = 0; p < NP; ++p) {
+            const uint8_t* pg = sbase + p * F::BODY;
+            uint32_t vw[F::VWN];
+            load_value_words<D, BITS>(pg + F::V_CODES_OFF, lane, vw);
+            const uint32_t* vm = reinterpret_cast<const uint32_t*>(pg + F::V_META_OFF);
 #pragma unroll
-          for (int k = 0; k < F::MB_PER_VG; ++k) {
-            const int mb = vg * F::MB_PER_VG + k;
-            uint32_t r[4];
-            switch (mb) {
+            for (int vg = 0; vg < NVG; ++vg) {
+              const float2 sza = unpack_h2(vm[g * NVG + vg]);        // token g:   (step, zero)
+              const float2 szb = unpack_h2(vm[(g + 8) * NVG + vg]);  // token g+8
+              const uint32_t h2a = pack_h2(sc[p][0] * sza.x, sc[p][1] * sza.x);
+              const uint32_t h2b = pack_h2(sc[p][2] * szb.x, sc[p][3] * szb.x);
+              const float2 ra = unpack_h2(h2a), rb = unpack_h2(h2b);
+              constexpr float blo = VEnc<BITS>::kBetaLo, bhi = VEnc<BITS>::kBetaHi;
+              st.w[vg][0] += fmaf(sc[p][0], sza.y, fmaf(sc[p][2], szb.y, -(blo * ra.x + bhi * rb.x)));
+              st.w[vg][1] += fmaf(sc[p][1], sza.y, fmaf(sc[p][3], szb.y, -(blo * ra.y + bhi * rb.y)));
+              uint32_t b01, b23;
+              p_to_bfrag(h2a, h2b, lane, b01, b23);
+#pragma unroll
+              for (int k = 0; k < F::MB_PER_VG; ++k) {
+                const int mb = vg * F::MB_PER_VG + k;
+                uint32_t r[4];
+                switch (mb) {
 #define TKV_VF(M)                                         \
   case M:                                                 \
     value_frag<BITS, (M < D / 16 ? M : 0)>(vw, r);        \
     break;
-              TKV_VF(0) TKV_VF(1) TKV_VF(2) TKV_VF(3) TKV_VF(4) TKV_VF(5) TKV_VF(6) TKV_VF(7)
+                  TKV_VF(0) TKV_VF(1) TKV_VF(2) TKV_VF(3) TKV_VF(4) TKV_VF(5) TKV_VF(6) TKV_VF(7)
 #undef TKV_VF
+                }
+                mma16816(st.o[mb], r[0], r[1], r[2], r[3], b01, b23);
+              }
             }
-            mma16816(st.o[mb], r[0], r[1], r[2], r[3], b01, b23);
+          }
+          __syncwarp();
+          if (j + ST < n_steps) issue_step(j + ST, stage);
+          if (++stage == ST) {
+            stage = 0;
+            phase ^= 1u;
           }
         }
-        __syncwarp();
-        if (lane == 0 && u + kStages < n) issue_page(u + kStages);
+      }
+      write_partial<D, NVG>(a, st, ml_base, VEnc<BITS>::kScale);
+      continue;
+    }
+
+    // =================== fp16 residual ring ===================
+    // unit 2*ci = K block of 16-token chunk ci, unit 2*ci+1 = its V block
+    constexpr int CHUNK = 2 * F::RBLK;
+    const int64_t chunks_per_row = a.ring_cap / kPage;
+    const uint8_t* ring_base = reinterpret_cast<const uint8_t*>(a.ring) +
+                               (((int64_t)row * a.n_kv_heads + h) * chunks_per_row) * CHUNK;
+    const int n = n_units;
+    auto issue_unit = [&](int u, int stg) {  // lane 0
+      const int ci = u >> 1;
+      const int chunk = ((nq + ci * kPage) % a.ring_cap) / kPage;
+      mbar_arrive_expect_tx(&bars[stg], F::RBLK);
+      bulk_g2s(ring + stg * SB, ring_base + (int64_t)chunk * CHUNK + (u & 1) * F::RBLK, F::RBLK,
+               &bars[stg]);
+    };
+    int issued = min(ST, n);
+    int istage = stage;  // stage of the next unit to issue
+    if (lane == 0)
+      for (int u = 0; u < issued; ++u) {
+        issue_unit(u, istage);
+        istage = istage + 1 == ST ? 0 : istage + 1;
+      }
+    uint32_t bq[F::NKB][2];
+#pragma unroll
+    for (int kb = 0; kb < F::NKB; ++kb)
+#pragma unroll
+      for (int hi = 0; hi < 2; ++hi) {
+        const int c = 16 * kb + 2 * tig + 8 * hi;
+        bq[kb][hi] = pack_h2(hok ? load_q(a, qrow + c) : 0.f, hok ? load_q(a, qrow + c + 1) : 0.f);
+      }
+    const bool hv0 = 2 * tig < a.grp, hv1 = 2 * tig + 1 < a.grp;
+    const int n_chunks = n >> 1;
+    for (int ci = 0; ci < n_chunks; ++ci) {
+      const int sk = stage;
+      mbar_wait(&bars[stage], phase, a.err);
+      if (++stage == ST) {
+        stage = 0;
+        phase ^= 1u;
+      }
+      const int sv = stage;
+      mbar_wait(&bars[stage], phase, a.err);
+      if (++stage == ST) {
+        stage = 0;
+        phase ^= 1u;
+      }
+      const int tb = nq + ci * kPage;
+      const bool vg0 = tb + g < len, vg8 = tb + g + 8 < len;
+      float sc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+      float (&s)[4] = sc[0];
+      const uint8_t* ck = ring + sk * SB;
+#pragma unroll
+      for (int kb = 0; kb < F::NKB; ++kb) {
+        const uint4 x = *reinterpret_cast<const uint4*>(ck + (kb * 32 + lane) * 16);
+        mma16816(s, x.x, x.y, x.z, x.w, bq[kb][0], bq[kb][1]);
+      }
+      s[0] = (hv0 && vg0) ? s[0] : -INFINITY;
+      s[1] = (hv1 && vg0) ? s[1] : -INFINITY;
+      s[2] = (hv0 && vg8) ? s[2] : -INFINITY;
+      s[3] = (hv1 && vg8) ? s[3] : -INFINITY;
+      softmax_update<D, NVG, 1>(st, sc, alpha);
+      uint32_t b01, b23;
+      p_to_bfrag(pack_h2(s[0], s[1]), pack_h2(s[2], s[3]), lane, b01, b23);
+      // zero the V^T columns of tokens past the end (stale ring slots)
+      const int t0 = tb + 2 * tig;
+      const uint32_t m01 = (t0 < len ? 0x0000ffffu : 0u) | (t0 + 1 < len ? 0xffff0000u : 0u);
+      const uint32_t m23 = (t0 + 8 < len ? 0x0000ffffu : 0u) | (t0 + 9 < len ? 0xffff0000u : 0u);
+      const uint8_t* cv = ring + sv * SB;
+#pragma unroll
+      for (int mb = 0; mb < D / 16; ++mb) {
+        const uint4 x = *reinterpret_cast<const uint4*>(cv + (mb * 32 + lane) * 16);
+        mma16816(st.o[mb], x.x & m01, x.y & m01, x.z & m23, x.w & m23, b01, b23);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        const int lim = min(n, 2 * (ci + 1) + ST);
+        for (; issued < lim; ++issued) {
+          issue_unit(issued, istage);
+          istage = istage + 1 == ST ? 0 : istage + 1;
+        }
       }
     }
-    write_partial<D, NVG>(a, st, ml_base, true);
-    return;
+    write_partial<D, NVG>(a, st, ml_base, 1.f);
   }
 
-  // =================== fp16 residual ring ===================
-  constexpr int CHUNK = 2 * kPage * D * 2;  // K block + V block of 16 tokens
-  const int64_t chunks_per_row = a.ring_cap / kPage;
-  const uint8_t* ring_base = reinterpret_cast<const uint8_t*>(a.ring) +
-                             (((int64_t)row * a.n_kv_heads + h) * chunks_per_row) * CHUNK;
-  const int n = n_units;  // 2*RU units per 16-token chunk: K halves then V halves
-  constexpr int UPC = 2 * F::RU;
-  auto issue_unit = [&](int u) {  // lane 0
-    const int ci = u / UPC, part = u % UPC;
-    const int tok = nq + ci * kPage;
-    const int chunk = (tok % a.ring_cap) / kPage;
-    uint64_t* bar = &bars[u % kStages];
-    mbar_arrive_expect_tx(bar, F::RUNIT);
-    bulk_g2s(ring + (u % kStages) * F::STAGE,
-             ring_base + (int64_t)chunk * CHUNK + (int64_t)part * F::RUNIT, F::RUNIT, bar);
-  };
-  int issued = min(kStages, n);
-  if (lane == 0)
-    for (int u = 0; u < issued; ++u) issue_unit(u);
-  uint32_t bq[F::NKB][2];
-#pragma unroll
-  for (int kb = 0; kb < F::NKB; ++kb)
-#pragma unroll
-    for (int hi = 0; hi < 2; ++hi) {
-      const int c = 16 * kb + 2 * tig + 8 * hi;
-      bq[kb][hi] = pack_h2(hok ? load_q(a, qrow + c) : 0.f, hok ? load_q(a, qrow + c + 1) : 0.f);
-    }
-  const int n_chunks = n / UPC;
-  for (int ci = 0; ci < n_chunks; ++ci) {
-    for (int p = 0; p < UPC; ++p) {
-      const int u = ci * UPC + p;
-      mbar_wait(&bars[u % kStages], (u / kStages) & 1, a.err);
-    }
-    const int tb = nq + ci * kPage;
-    const bool vg0 = tb + g < len, vg8 = tb + g + 8 < len;
-    float s[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int kb = 0; kb < F::NKB; ++kb) {
-      const int u = ci * UPC + kb / 4;  // 4 k-blocks per 2 KB unit
-      const uint8_t* ck = ring + (u % kStages) * F::STAGE;
-      const uint4 x = *reinterpret_cast<const uint4*>(ck + ((kb % 4) * 32 + lane) * 16);
-      mma16816(s, x.x, x.y, x.z, x.w, bq[kb][0], bq[kb][1]);
-    }
-    s[0] = (hv0 && vg0) ? s[0] * a.alpha : -INFINITY;
-    s[1] = (hv1 && vg0) ? s[1] * a.alpha : -INFINITY;
-    s[2] = (hv0 && vg8) ? s[2] * a.alpha : -INFINITY;
-    s[3] = (hv1 && vg8) ? s[3] * a.alpha : -INFINITY;
-    softmax_tile<D, NVG>(st, s);
-    uint32_t b01, b23;
-    p_to_bfrag(pack_h2(s[0], s[1]), pack_h2(s[2], s[3]), lane, b01, b23);
-    // zero the V^T columns of tokens past the end (stale ring slots)
-    const int t0 = tb + 2 * tig;
-    const uint32_t m01 = (t0 < len ? 0x0000ffffu : 0u) | (t0 + 1 < len ? 0xffff0000u : 0u);
-    const uint32_t m23 = (t0 + 8 < len ? 0x0000ffffu : 0u) | (t0 + 9 < len ? 0xffff0000u : 0u);
-#pragma unroll
-    for (int mb = 0; mb < D / 16; ++mb) {
-      const int u = ci * UPC + F::RU + mb / 4;
-      const uint8_t* cv = ring + (u % kStages) * F::STAGE;
-      const uint4 x = *reinterpret_cast<const uint4*>(cv + ((mb % 4) * 32 + lane) * 16);
-      mma16816(st.o[mb], x.x & m01, x.y & m01, x.z & m23, x.w & m23, b01, b23);
-    }
-    __syncwarp();
-    if (lane == 0) {
-      const int lim = min(n, (ci + 1) * UPC + kStages);
-      for (; issued < lim; ++issued) issue_unit(issued);
+  // the last warp to finish resets the work counters for the next launch
+  if (lane == 0) {
+    __threadfence();
+    const unsigned int done = atomicAdd(&a.work[1], 1u);
+    if (done == gridDim.x - 1) {
+      a.work[0] = 0u;
+      a.work[1] = 0u;
+      __threadfence();
     }
   }
-  write_partial<D, NVG>(a, st, ml_base, false);
 }
 
 // ---------------------------------------------------------------------------
@@ -587,36 +686,44 @@ __global__ void __launch_bounds__(128) merge_kernel(const float* __restrict__ pa
 // host launchers
 // ---------------------------------------------------------------------------
 template <int D, int BITS, int G>
-static int launch_warp_t(const DecodeArgs& a, dim3 grid, cudaStream_t stream) {
+static int launch_warp_t(const DecodeArgs& a, cudaStream_t stream) {
   constexpr int smem = decode_smem_bytes<D, BITS, G>();
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(decode_warp_kernel<D, BITS, G>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+  static int resident = 0;  // CTAs that fit on the device at once
+  if (resident == 0) {
+    int dev = 0, sms = 0, per_sm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaFuncSetAttribute(decode_warp_kernel<D, BITS, G>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_warp_kernel<D, BITS, G>, 32,
+                                                      smem) != cudaSuccess ||
+        per_sm <= 0)
       return TKV_BACKEND_ERROR;
-    attr = true;
+    resident = sms * per_sm;
   }
+  const int grid = a.n_items < resident ? a.n_items : resident;
   decode_warp_kernel<D, BITS, G><<<grid, 32, smem, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
 }
 
 template <int D, int BITS>
-static int launch_warp_g(const DecodeArgs& a, dim3 grid, cudaStream_t stream) {
+static int launch_warp_g(const DecodeArgs& a, cudaStream_t stream) {
   switch (a.group) {
-    case 16: return launch_warp_t<D, BITS, 16>(a, grid, stream);
-    case 32: return launch_warp_t<D, BITS, 32>(a, grid, stream);
-    case 64: return launch_warp_t<D, BITS, 64>(a, grid, stream);
-    case 128: return launch_warp_t<D, BITS, 128>(a, grid, stream);
+    case 16: return launch_warp_t<D, BITS, 16>(a, stream);
+    case 32: return launch_warp_t<D, BITS, 32>(a, stream);
+    case 64: return launch_warp_t<D, BITS, 64>(a, stream);
+    case 128: return launch_warp_t<D, BITS, 128>(a, stream);
   }
   return TKV_NOT_IMPLEMENTED;
 }
 
 int launch_decode_splits(DecodeArgs a, int head_dim, int bits, int, cudaStream_t stream) {
-  dim3 grid(a.n_slots, a.n_kv_heads, a.num_seqs);
+  a.n_items = a.n_slots * a.num_seqs * a.n_kv_heads;
+  if (a.n_items <= 0) return TKV_OK;
   if (head_dim == 128)
-    return bits == 4 ? launch_warp_g<128, 4>(a, grid, stream) : launch_warp_g<128, 2>(a, grid, stream);
+    return bits == 4 ? launch_warp_g<128, 4>(a, stream) : launch_warp_g<128, 2>(a, stream);
   if (head_dim == 64)
-    return bits == 4 ? launch_warp_g<64, 4>(a, grid, stream) : launch_warp_g<64, 2>(a, grid, stream);
+    return bits == 4 ? launch_warp_g<64, 4>(a, stream) : launch_warp_g<64, 2>(a, stream);
   return TKV_NOT_IMPLEMENTED;
 }
 

@@ -200,8 +200,8 @@ def paged_decode(cache: KiviPagedCache, q: torch.Tensor, block_tables: torch.Ten
     if out is None:
         out = torch.empty((B, Hq, D), dtype=out_dtype or q.dtype, device=q.device)
     ws_bytes = decode_workspace_bytes(B, Hq, D, max_context_len)
-    if workspace is None:
-        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    if workspace is None:  # work counters at its start must be zero: allocate zeroed
+        workspace = torch.zeros(ws_bytes, dtype=torch.uint8, device=q.device)
     c = cache.c_struct()
     L.check("tkv_paged_decode", L.lib().tkv_paged_decode(
         C.byref(c), _ptr(q.contiguous()), _DT[q.dtype], _ptr(out), _DT[out.dtype],
@@ -216,10 +216,14 @@ def paged_decode_partials(cache: KiviPagedCache, q: torch.Tensor, block_tables: 
                           include_residual: bool, part_ml: torch.Tensor, part_o: torch.Tensor,
                           scale: Optional[float] = None,
                           seq_slots: Optional[torch.Tensor] = None,
-                          err: Optional[torch.Tensor] = None, stream=None) -> None:
+                          err: Optional[torch.Tensor] = None,
+                          work: Optional[torch.Tensor] = None, stream=None) -> None:
     """Split-KV partials (m, l, o) of quantised splits [split_lo, split_hi)
-    (+ the residual split) for sequences split across GPUs."""
+    (+ the residual split) for sequences split across GPUs.  work: >= 8 bytes
+    of zeroed device memory reused across calls (allocated when omitted)."""
     _need_cuda(q, block_tables, seq_lens, part_ml, part_o)
+    if work is None:
+        work = torch.zeros(2, dtype=torch.int32, device=q.device)
     B, Hq, D = q.shape
     if scale is None:
         scale = 1.0 / math.sqrt(D)
@@ -228,7 +232,7 @@ def paged_decode_partials(cache: KiviPagedCache, q: torch.Tensor, block_tables: 
         C.byref(c), _ptr(q.contiguous()), _DT[q.dtype], _ptr(block_tables),
         int(block_tables.shape[1]), _ptr(seq_lens), _ptr(seq_slots), B, Hq, float(scale),
         int(split_lo), int(split_hi), int(bool(include_residual)), _ptr(part_ml), _ptr(part_o),
-        _ptr(err), C.c_void_p(_stream(stream))))
+        _ptr(work), _ptr(err), C.c_void_p(_stream(stream))))
 
 
 def merge_partials(part_ml: torch.Tensor, part_o: torch.Tensor, out: torch.Tensor,
