@@ -84,7 +84,9 @@ extern "C" {
 #define TKV_ABI_VERSION 1
 #define TKV_FORMAT_VERSION 1
 #define TKV_PAGE_SIZE 16
+#ifndef TKV_SPLIT_TOKENS
 #define TKV_SPLIT_TOKENS 512 /* decode split (flash-decoding partition) length */
+#endif
 
 /* Status codes: the values of truellm::ErrorCode (include/truellm/types.h:20-32). */
 typedef enum tkv_status {

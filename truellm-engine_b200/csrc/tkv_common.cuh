@@ -10,7 +10,7 @@
 #include <float.h>
 #include <stdint.h>
 
-#include "../../include/truellm_kivi.h"
+#include "truellm_kivi.h"  // include/ is on the include path
 
 namespace tkv {
 

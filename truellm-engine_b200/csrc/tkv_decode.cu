@@ -334,8 +334,15 @@ __device__ __forceinline__ void write_partial(const DecodeArgs& a, WarpState<D, 
 // persistent split kernel: each resident warp takes work items
 // (split slot, sequence, kv head) from a global counter until none are left
 // ---------------------------------------------------------------------------
+#ifndef TKV_DECODE_MIN_BLOCKS
+#define TKV_DECODE_MIN_BLOCKS 12  // resident warps per SM the register budget targets
+#endif
+#ifndef TKV_QK_CHAINS
+#define TKV_QK_CHAINS 1  // independent accumulator chains per page in QK^T
+#endif
+
 template <int D, int BITS, int G>
-__global__ void __launch_bounds__(32, 15) decode_warp_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(DecodeArgs a) {
   using F = Fmt<D, BITS, G>;
   constexpr int NVG = F::NVG, NP = F::NP, ST = F::ST, SB = F::SB;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -487,6 +494,7 @@ __global__ void __launch_bounds__(32, 15) decode_warp_kernel(DecodeArgs a) {
             uint32_t wg[F::TW], wh[F::TW];
             load_key_words<D, BITS>(sbase + p * F::BODY, g, tig, wg, wh);
             sc[p][0] = sc[p][1] = sc[p][2] = sc[p][3] = 0.f;
+            float sx[4] = {0.f, 0.f, 0.f, 0.f};  // second chain (odd k-blocks)
 #pragma unroll
             for (int kb = 0; kb < F::NKB; ++kb) {
               uint32_t r[4];
@@ -499,7 +507,14 @@ __global__ void __launch_bounds__(32, 15) decode_warp_kernel(DecodeArgs a) {
                 TKV_KF(0) TKV_KF(1) TKV_KF(2) TKV_KF(3) TKV_KF(4) TKV_KF(5) TKV_KF(6) TKV_KF(7)
 #undef TKV_KF
               }
-              mma16816(sc[p], r[0], r[1], r[2], r[3], bq[kb][0], bq[kb][1]);
+              if (TKV_QK_CHAINS == 2 && (kb & 1))
+                mma16816(sx, r[0], r[1], r[2], r[3], bq[kb][0], bq[kb][1]);
+              else
+                mma16816(sc[p], r[0], r[1], r[2], r[3], bq[kb][0], bq[kb][1]);
+            }
+            if (TKV_QK_CHAINS == 2) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) sc[p][i] += sx[i];
             }
           }
           softmax_update<D, NVG, NP>(st, sc, alpha);
