@@ -206,6 +206,28 @@ TKV_API int tkv_paged_decode(const tkv_cache_t* cache, const void* q, int q_dtyp
                      int num_q_heads, float scale, int max_context_len, void* workspace,
                      size_t workspace_bytes, int* err_flag, void* stream);
 
+/* Size of the static device scratch used by tkv_paged_decode_noalloc. */
+#define TKV_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* tkv_paged_decode without a workspace argument.  No counterpart in the
+ * reference.  For callers that cannot allocate device memory -- a kernel
+ * plugin that only receives the engine's tensors, a host whose allocator owns
+ * all device memory, or a decode loop that must not call cudaMalloc -- the
+ * split-KV partials and work counters live in a static device array of
+ * TKV_NOALLOC_SCRATCH_BYTES that every GPU loading this library keeps until
+ * the process exits.  Nothing is allocated.  The first call on a device looks
+ * up the array's device address and zeroes its work counters (stream-ordered
+ * on `stream`); make that first call before any stream capture.  Calls whose
+ * tkv_decode_workspace_bytes() exceeds the scratch return TKV_OUT_OF_MEMORY
+ * without launching.  All calls on a device share the array, so calls that
+ * overlap on the GPU race; it keeps the last call's partials. */
+TKV_API int tkv_paged_decode_noalloc(const tkv_cache_t* cache, const void* q, int q_dtype,
+                                     void* out, int out_dtype, const int32_t* block_tables,
+                                     int max_blocks_per_seq, const int32_t* seq_lens,
+                                     const int32_t* seq_slots, int num_seqs, int num_q_heads,
+                                     float scale, int max_context_len, int* err_flag,
+                                     void* stream);
+
 /* Split-KV partials only (for sequences split across GPUs): computes the
  * quantised splits [split_lo, split_hi) of every sequence, plus the residual
  * split when include_residual != 0, into

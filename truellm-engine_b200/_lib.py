@@ -26,6 +26,8 @@ TKV_ERR_BAD_SLOT = 0x2
 TKV_ERR_BAD_LENGTH = 0x4
 TKV_ERR_TIMEOUT = 0x8
 
+TKV_NOALLOC_SCRATCH_BYTES = 16 << 20
+
 
 class TkvFormat(C.Structure):
     _fields_ = [
@@ -73,6 +75,8 @@ SIGNATURES = {
     "tkv_decode_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32]),
     "tkv_paged_decode": (_i32, [C.POINTER(TkvCache), _vp, _i32, _vp, _i32, _vp, _i32, _vp, _vp,
                                 _i32, _i32, _f32, _i32, _vp, _sz, _vp, _vp]),
+    "tkv_paged_decode_noalloc": (_i32, [C.POINTER(TkvCache), _vp, _i32, _vp, _i32, _vp, _i32,
+                                        _vp, _vp, _i32, _i32, _f32, _i32, _vp, _vp]),
     "tkv_paged_decode_partials": (_i32, [C.POINTER(TkvCache), _vp, _i32, _vp, _i32, _vp, _vp,
                                          _i32, _i32, _f32, _i32, _i32, _i32, _vp, _vp, _vp,
                                          _vp, _vp]),
