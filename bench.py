@@ -258,22 +258,20 @@ def run_kivi(args):
     out = torch.empty_like(q)
     max_ctx = int(w.lengths.max())
     scale = 1.0 / math.sqrt(w.D)
-    S = ops.decode_num_splits(max_ctx)
-    part_ml = torch.empty((S, w.B, w.Hq, 2), dtype=torch.float32, device=dev)
-    part_o = torch.empty((S, w.B, w.Hq, w.D), dtype=torch.float32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
-    work = torch.zeros(2, dtype=torch.int32, device=dev)
+    # workspace: split partials + counters, zeroed once (calls leave counters zero)
+    ws = torch.zeros(ops.decode_workspace_bytes(w.B, w.Hq, w.D, max_ctx), dtype=torch.uint8,
+                     device=dev)
     stream = torch.cuda.current_stream()
 
     def step(ev=None):
-        # one decode step = split kernel + merge kernel (2 launches)
+        # one decode step = one launch of the split kernel (merge fused in)
         if ev is not None:
             ev[0].record(stream)
-        ops.paged_decode_partials(cache, q, bt, lens, 0, S - 1, True, part_ml, part_o,
-                                  scale=scale, err=err, work=work, stream=stream)
+        ops.paged_decode(cache, q, bt, lens, max_ctx, scale=scale, out=out, workspace=ws,
+                         err=err, stream=stream)
         if ev is not None:
             ev[1].record(stream)
-        ops.merge_partials(part_ml, part_o, out, stream=stream)
 
     def barrier():
         if world > 1:
@@ -309,8 +307,6 @@ def run_kivi(args):
     out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
     q_dev = torch.empty_like(q)
     lens_dev = torch.empty_like(lens)
-    ws = torch.zeros(ops.decode_workspace_bytes(w.B, w.Hq, w.D, max_ctx), dtype=torch.uint8,
-                     device=dev)
 
     def e2e_step():
         q_dev.copy_(q_host, non_blocking=True)
@@ -371,12 +367,12 @@ def run_kivi(args):
                        "global_batch": world * w.B, "mean_context": float(w.lengths.mean()),
                        "parallelism": f"sequence-sharded x{world}",
                        "l2": "inputs larger than L2 (cache %.0f MB)" % (alg_bytes / 1e6)},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": args.steps,
             "e2e": {"value": world * w.B / t_e2e, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": traffic, "kernel": "decode_split_kernel<128,4,1>",
+                         "traffic": traffic, "kernel": "decode_warp_kernel<128,4,128> (split + fused merge)",
                          "alg_bytes_per_launch": alg_bytes,
                          "kernel_ms": t_split * 1e3},
             "cpu_baseline": cpu,

@@ -186,10 +186,10 @@ TKV_API int tkv_paged_append(const tkv_cache_t* cache, const void* k_new, const 
 /* Number of split slots per sequence: ceil(max_context_len / TKV_SPLIT_TOKENS) + 1
  * (the last one holds the fp16 residual). */
 TKV_API int tkv_decode_num_splits(int max_context_len);
-/* Workspace bytes for tkv_paged_decode.  The first 256 bytes hold the split
- * kernel's work counters: zero them once when the workspace is allocated; every
- * call leaves them zero again.  Calls that share a workspace must not overlap
- * on the GPU. */
+/* Workspace bytes for tkv_paged_decode: work counters, per-(sequence, kv head)
+ * completion counters and the split partials.  Zero the whole workspace once
+ * when it is allocated; every call leaves the counters zero again.  Calls that
+ * share a workspace must not overlap on the GPU. */
 TKV_API size_t tkv_decode_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
                                   int max_context_len);
 
@@ -199,7 +199,8 @@ TKV_API size_t tkv_decode_workspace_bytes(int num_seqs, int num_q_heads, int hea
  * seq_lens[s] tokens of sequence s, kv head = h / (num_q_heads / n_kv_heads)
  * (megakernel.cu:270-277).  q, out: [num_seqs, num_q_heads, D]; q is fp16 or
  * bf16, out is fp16, bf16 or f32.  Split-KV over TKV_SPLIT_TOKENS-token splits
- * plus a log-sum-exp merge (paged_attention_v2.cu:132-170).  Two launches. */
+ * plus a log-sum-exp merge (paged_attention_v2.cu:132-170), done by the warp
+ * that finishes the last split of each (sequence, kv head).  One launch. */
 TKV_API int tkv_paged_decode(const tkv_cache_t* cache, const void* q, int q_dtype, void* out,
                      int out_dtype, const int32_t* block_tables, int max_blocks_per_seq,
                      const int32_t* seq_lens, const int32_t* seq_slots, int num_seqs,
@@ -216,8 +217,8 @@ TKV_API int tkv_paged_decode(const tkv_cache_t* cache, const void* q, int q_dtyp
  * split-KV partials and work counters live in a static device array of
  * TKV_NOALLOC_SCRATCH_BYTES that every GPU loading this library keeps until
  * the process exits.  Nothing is allocated.  The first call on a device looks
- * up the array's device address and zeroes its work counters (stream-ordered
- * on `stream`); make that first call before any stream capture.  Calls whose
+ * up the array's device address and zeroes the array (stream-ordered on
+ * `stream`); make that first call before any stream capture.  Calls whose
  * tkv_decode_workspace_bytes() exceeds the scratch return TKV_OUT_OF_MEMORY
  * without launching.  All calls on a device share the array, so calls that
  * overlap on the GPU race; it keeps the last call's partials. */

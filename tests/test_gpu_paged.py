@@ -169,6 +169,42 @@ def test_long_context_split_partials_merge(ops, O, wl, cuda):
     check_close(full.cpu().numpy(), ref)
 
 
+def test_fused_merge_equals_split_kernel_plus_merge_kernel(ops, O, wl, cuda):
+    """tkv_paged_decode merges the split partials inside its one launch (the
+    warp that finishes a (sequence, kv head) pair's last split).  Its output
+    equals the split kernel followed by the standalone merge kernel bit for
+    bit: with more than 32 slots, a GQA group of 5 (not a multiple of the
+    merge's 4-head pass), and on repeated calls sharing one workspace (the
+    pair counters return to zero after every call)."""
+    lengths = [20000, 1, 700, 4100, 16]
+    tw, bt, lengths, rng = _build(ops, O, wl, cuda, 128, 128, 128, 4, 8, lengths, "bf16",
+                                  seed=41)
+    B, Hq, D = len(lengths), 40, 128
+    max_ctx = int(lengths.max())
+    q = bits_to_torch(wl.f32_to_bf16_bits(rng.standard_normal((B, Hq, D))), "bf16", cuda)
+    scale = 1 / math.sqrt(D)
+    bt_d, lens_d = i32(bt, cuda), i32(lengths, cuda)
+    S = ops.decode_num_splits(max_ctx)
+    assert S > 32
+    ws = torch.zeros(ops.decode_workspace_bytes(B, Hq, D, max_ctx), dtype=torch.uint8,
+                     device=cuda)
+    outs = [ops.paged_decode(tw.gpu, q, bt_d, lens_d, max_ctx, scale=scale,
+                             out_dtype=torch.float32, workspace=ws, err=tw.err)
+            for _ in range(3)]
+    ml = torch.empty((S, B, Hq, 2), dtype=torch.float32, device=cuda)
+    o = torch.empty((S, B, Hq, D), dtype=torch.float32, device=cuda)
+    ops.paged_decode_partials(tw.gpu, q, bt_d, lens_d, 0, S - 1, True, ml, o, scale=scale,
+                              err=tw.err)
+    merged = ops.merge_partials(ml, o, torch.empty((B, Hq, D), dtype=torch.float32,
+                                                   device=cuda))
+    torch.cuda.synchronize()
+    assert int(tw.err.item()) == 0
+    for out in outs:
+        assert torch.equal(out, merged)
+    ref = tw.cpu.decode(q.float().cpu().numpy(), bt, lengths, scale, n_threads=8)
+    check_close(outs[0].cpu().numpy(), ref)
+
+
 def test_bf16_and_fp16_outputs(ops, O, wl, cuda):
     lengths = [700, 300]
     tw, bt, lengths, rng = _build(ops, O, wl, cuda, 128, 128, 128, 4, 8, lengths, "bf16", seed=3)

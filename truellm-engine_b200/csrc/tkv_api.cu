@@ -222,14 +222,23 @@ int tkv_decode_num_splits(int max_context_len) {
   return (max_context_len + TKV_SPLIT_TOKENS - 1) / TKV_SPLIT_TOKENS + 1;
 }
 
-static constexpr size_t kWorkBytes = 256;  // work counters at the start of the workspace
+// Workspace layout: [work counters, 256 B][per-(sequence, kv head) counters,
+// num_seqs * num_q_heads * 4 B rounded up to 256 (num_q_heads bounds the kv
+// heads)][part_ml][part_o].  Counters must be zero before the first call and
+// every call leaves them zero.
+static constexpr size_t kWorkBytes = 256;
+
+static size_t pair_counter_bytes(int num_seqs, int num_q_heads) {
+  return ((size_t)num_seqs * (size_t)num_q_heads * 4 + 255) / 256 * 256;
+}
 
 size_t tkv_decode_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
                                   int max_context_len) {
   if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || max_context_len < 0) return 0;
   const size_t slots = (size_t)tkv_decode_num_splits(max_context_len);
   const size_t n = slots * (size_t)num_seqs * (size_t)num_q_heads;
-  return kWorkBytes + n * 2 * sizeof(float) + n * (size_t)head_dim * sizeof(float);
+  return kWorkBytes + pair_counter_bytes(num_seqs, num_q_heads) + n * 2 * sizeof(float) +
+         n * (size_t)head_dim * sizeof(float);
 }
 
 static int decode_partials_impl(const tkv_cache_t* cache, const void* q, int q_dtype,
@@ -237,7 +246,8 @@ static int decode_partials_impl(const tkv_cache_t* cache, const void* q, int q_d
                                 const int32_t* seq_lens, const int32_t* seq_slots, int num_seqs,
                                 int num_q_heads, float scale, int split_lo, int split_hi,
                                 int include_residual, float* part_ml, float* part_o,
-                                void* work, int* err_flag, cudaStream_t stream) {
+                                void* work, unsigned int* bh_count, void* out, int out_dtype,
+                                int* err_flag, cudaStream_t stream) {
   if (!cache_ok(cache)) return TKV_INVALID_ARGUMENT;
   const tkv_format_t& f = cache->fmt;
   if (q_dtype != TKV_F16 && q_dtype != TKV_BF16) return TKV_NOT_IMPLEMENTED;
@@ -284,6 +294,10 @@ static int decode_partials_impl(const tkv_cache_t* cache, const void* q, int q_d
   a.part_ml = part_ml;
   a.part_o = part_o;
   a.work = static_cast<unsigned int*>(work);
+  a.bh_count = bh_count;
+  a.fuse_merge = bh_count != nullptr && out != nullptr && a.include_residual;
+  a.out = out;
+  a.out_dtype = out_dtype;
   a.err = err_flag;
   if (a.n_slots == 0) return TKV_OK;
   return launch_decode_splits(a, f.head_dim, f.bits, f.n_vgroups, stream);
@@ -297,8 +311,8 @@ int tkv_paged_decode_partials(const tkv_cache_t* cache, const void* q, int q_dty
                               int* err_flag, void* stream) {
   return decode_partials_impl(cache, q, q_dtype, block_tables, max_blocks_per_seq, seq_lens,
                               seq_slots, num_seqs, num_q_heads, scale, split_lo, split_hi,
-                              include_residual, part_ml, part_o, work, err_flag,
-                              as_stream(stream));
+                              include_residual, part_ml, part_o, work, nullptr, nullptr, 0,
+                              err_flag, as_stream(stream));
 }
 
 int tkv_merge_partials(const float* part_ml, const float* part_o, int n_slots, int num_seqs,
@@ -322,17 +336,22 @@ int tkv_paged_decode(const tkv_cache_t* cache, const void* q, int q_dtype, void*
   const int D = cache->fmt.head_dim;
   const size_t need = tkv_decode_workspace_bytes(num_seqs, num_q_heads, D, max_context_len);
   if (workspace_bytes < need || !aligned16(workspace)) return TKV_INVALID_ARGUMENT;
+  if (out_dtype != TKV_F32 && out_dtype != TKV_F16 && out_dtype != TKV_BF16)
+    return TKV_NOT_IMPLEMENTED;
   const int slots = tkv_decode_num_splits(max_context_len);
   const size_t n = (size_t)slots * num_seqs * num_q_heads;
-  void* work = workspace;
-  float* part_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWorkBytes);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* work = ws;
+  unsigned int* bh_count = reinterpret_cast<unsigned int*>(ws + kWorkBytes);
+  float* part_ml =
+      reinterpret_cast<float*>(ws + kWorkBytes + pair_counter_bytes(num_seqs, num_q_heads));
   float* part_o = part_ml + 2 * n;
-  int st = decode_partials_impl(cache, q, q_dtype, block_tables, max_blocks_per_seq, seq_lens,
-                                seq_slots, num_seqs, num_q_heads, scale, 0, slots - 1, 1, part_ml,
-                                part_o, work, err_flag, as_stream(stream));
-  if (st != TKV_OK) return st;
-  return tkv_merge_partials(part_ml, part_o, slots, num_seqs, num_q_heads, D, out, out_dtype,
-                            stream);
+  // one launch: the split kernel merges each (sequence, kv head) when its last
+  // split finishes
+  return decode_partials_impl(cache, q, q_dtype, block_tables, max_blocks_per_seq, seq_lens,
+                              seq_slots, num_seqs, num_q_heads, scale, 0, slots - 1, 1, part_ml,
+                              part_o, work, bh_count, out, out_dtype, err_flag,
+                              as_stream(stream));
 }
 
 // ---------------------------------------------------------------------------

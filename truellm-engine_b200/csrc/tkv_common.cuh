@@ -87,6 +87,24 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
       : "memory");
 }
 
+// L2 policy for data read once per launch (cache pages): evict it first, so
+// lines that are read again soon (split partials) stay in L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(pol));
+  return pol;
+}
+
+// bulk_g2s with an L2 cache policy
+__device__ __forceinline__ void bulk_g2s_hint(void* dst_smem, const void* src_gmem,
+                                              uint32_t bytes, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+      "[%1], %2, [%3], %4;\n" ::"r"(smem_u32(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // tensor core: D = A(16x16 f16) * B(16x8 f16) + C (f32), mma.sync m16n8k16
 // ---------------------------------------------------------------------------
@@ -231,6 +249,10 @@ struct DecodeArgs {
   int split_lo, split_hi, include_residual, n_slots;
   int n_items;              // n_slots * num_seqs * n_kv_heads
   unsigned int* work;       // [0] next work item, [1] finished warps; zero between launches
+  unsigned int* bh_count;   // [num_seqs * n_kv_heads] finished slots; zero between launches
+  int fuse_merge;           // 1: the warp finishing a (sequence, kv head) merges it into out
+  void* out;                // [num_seqs, num_q_heads, D] when fuse_merge
+  int out_dtype;
   float* part_ml;
   float* part_o;
   int* err;

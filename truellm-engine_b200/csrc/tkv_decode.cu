@@ -331,6 +331,128 @@ __device__ __forceinline__ void write_partial(const DecodeArgs& a, WarpState<D, 
 }
 
 // ---------------------------------------------------------------------------
+// log-sum-exp merge of the split partials (paged_attention_v2.cu:132-170), one
+// warp for nh consecutive q heads i0 .. i0+nh-1 of one sequence:
+//   M = max_s m_s,  L = sum_s l_s 2^(m_s - M),
+//   out[c] = (sum_s o_s[c] 2^(m_s - M)) / L,  slots with m_s = -inf skipped.
+// The slots merged are t = 0 .. cnt-1 mapped to slot t for t < nv and to the
+// last slot (n_slots - 1, the residual) otherwise; the standalone merge passes
+// nv = cnt = n_slots.  M is a max (exact in any order); L and O are summed
+// over t in order, so a merge over only the written slots equals one over all
+// slots with -inf in the unwritten ones, bit for bit.  H heads and 128
+// channels go per pass (lane l owns channels l + 32k), the loads of 16/H
+// slots in flight at once: at the tail of the decode launch the merge's
+// latency is exposed.  Partials are read with ld.global.cg: other CTAs of the
+// same launch may have written them.
+// ---------------------------------------------------------------------------
+template <int H>
+__device__ __forceinline__ void merge_heads(const float* part_ml, const float* part_o,
+                                            int n_slots, int nv, int cnt, int64_t stride,
+                                            int64_t i0, int nh, int D, void* out, int out_dtype,
+                                            int lane) {
+  constexpr int CPL = 4, UB = 16 / H;
+  static_assert(H == 1 || H == 2 || H == 4, "heads per merge pass");
+  for (int j0 = 0; j0 < nh; j0 += H) {
+    float M[H], m0[H], l0[H];
+#pragma unroll
+    for (int q = 0; q < H; ++q) M[q] = m0[q] = -INFINITY, l0[q] = 0.f;
+    for (int t = lane; t < cnt; t += 32) {
+      const int64_t s = t < nv ? t : n_slots - 1;
+#pragma unroll
+      for (int q = 0; q < H; ++q) {
+        if (j0 + q >= nh) continue;
+        const int64_t r = (s * stride + i0 + j0 + q) * 2;
+        const float m = __ldcg(&part_ml[r]), l = __ldcg(&part_ml[r + 1]);
+        if (t < 32) m0[q] = m, l0[q] = l;
+        M[q] = fmaxf(M[q], m);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int q = 0; q < H; ++q) M[q] = fmaxf(M[q], __shfl_xor_sync(0xffffffffu, M[q], off));
+    for (int cb = 0; cb < D; cb += 32 * CPL) {
+      float O[H][CPL], L[H];
+#pragma unroll
+      for (int q = 0; q < H; ++q) {
+        L[q] = 0.f;
+#pragma unroll
+        for (int k = 0; k < CPL; ++k) O[q][k] = 0.f;
+      }
+      for (int c0 = 0; c0 < cnt; c0 += 32) {
+        // lane u of this chunk holds weight and l of t = c0 + u
+        float w[H], lw[H];
+        const int t = c0 + lane;
+        const int64_t s = t < nv ? t : n_slots - 1;
+#pragma unroll
+        for (int q = 0; q < H; ++q) {
+          float m = m0[q], l = l0[q];
+          if (c0 > 0) {
+            const bool ok = t < cnt && j0 + q < nh;
+            const int64_t r = (s * stride + i0 + j0 + q) * 2;
+            m = ok ? __ldcg(&part_ml[r]) : -INFINITY;
+            l = ok ? __ldcg(&part_ml[r + 1]) : 0.f;
+          }
+          w[q] = m != -INFINITY ? fast_exp2(m - M[q]) : 0.f;
+          lw[q] = l;
+        }
+        const int n = min(32, cnt - c0);
+        // UB slots per batch: all their loads are issued before the
+        // shuffles and FMAs that use them
+        for (int u0 = 0; u0 < n; u0 += UB) {
+          float ov[UB][H][CPL];
+#pragma unroll
+          for (int uu = 0; uu < UB; ++uu) {
+            const int tu = c0 + u0 + uu;
+            const int64_t su = tu < nv ? tu : n_slots - 1;
+            const int64_t row = (su * stride + i0 + j0) * D + cb + lane;
+#pragma unroll
+            for (int q = 0; q < H; ++q)
+#pragma unroll
+              for (int k = 0; k < CPL; ++k) {
+                const bool ok = u0 + uu < n && j0 + q < nh && cb + lane + 32 * k < D;
+                ov[uu][q][k] = ok ? __ldcg(&part_o[row + q * D + 32 * k]) : 0.f;
+              }
+          }
+#pragma unroll
+          for (int uu = 0; uu < UB; ++uu) {
+            const int src = (u0 + uu) & 31;
+#pragma unroll
+            for (int q = 0; q < H; ++q) {
+              const float wv = __shfl_sync(0xffffffffu, w[q], src);
+              const float lq = __shfl_sync(0xffffffffu, lw[q], src);
+              const float wq = u0 + uu < n ? wv : 0.f;
+              L[q] = wq != 0.f ? fmaf(lq, wq, L[q]) : L[q];
+#pragma unroll
+              for (int k = 0; k < CPL; ++k)
+                O[q][k] = wq != 0.f ? fmaf(ov[uu][q][k], wq, O[q][k]) : O[q][k];
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < H; ++q) {
+        if (j0 + q >= nh) continue;
+        const float inv = L[q] > 0.f ? 1.f / L[q] : 0.f;
+#pragma unroll
+        for (int k = 0; k < CPL; ++k) {
+          const int c = cb + lane + 32 * k;
+          if (c >= D) continue;
+          const float v = O[q][k] * inv;
+          const int64_t oi = (i0 + j0 + q) * D + c;
+          if (out_dtype == TKV_F32)
+            static_cast<float*>(out)[oi] = v;
+          else if (out_dtype == TKV_BF16)
+            static_cast<__nv_bfloat16*>(out)[oi] = __float2bfloat16_rn(v);
+          else
+            static_cast<__half*>(out)[oi] = __float2half_rn(v);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // persistent split kernel: each resident warp takes work items
 // (split slot, sequence, kv head) from a global counter until none are left
 // ---------------------------------------------------------------------------
@@ -354,6 +476,7 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
   const int n_qsplit = a.split_hi - a.split_lo;
   const int per_slot = a.num_seqs * a.n_kv_heads;
   const float alpha = a.alpha;
+  const uint64_t pol = l2_evict_first_policy();  // cache pages and ring: read once
 
   if (lane == 0) {
     for (int i = 0; i < ST + 2; ++i) mbar_init(&bars[i], 1);
@@ -364,6 +487,25 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
   int stage = 0;
   uint32_t phase = 0;
   int gcount = 0;  // key groups consumed so far (meta buffer = gcount & 1)
+
+  // After an item's partial is written: with fuse_merge, the warp that
+  // finishes the last of the nv + 1 written items of (sequence b, kv head h)
+  // (its nv quantised splits that hold pages, then the residual) merges them
+  // into out and resets the pair's counter for the next launch.
+  auto item_done = [&](int b, int h, int nv) {
+    if (!a.fuse_merge) return;
+    __syncwarp();
+    __threadfence();  // publish this warp's partial before counting it
+    unsigned int old = 0;
+    if (lane == 0) old = atomicAdd(&a.bh_count[b * a.n_kv_heads + h], 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old != static_cast<unsigned int>(nv)) return;
+    __threadfence();  // every other warp's partial of this pair is visible now
+    if (lane == 0) a.bh_count[b * a.n_kv_heads + h] = 0u;
+    merge_heads<4>(a.part_ml, a.part_o, a.n_slots, nv, nv + 1,
+                   (int64_t)a.num_seqs * a.num_q_heads, (int64_t)b * a.num_q_heads + h * a.grp,
+                   a.grp, D, a.out, a.out_dtype, lane);
+  };
 
   for (;;) {
     int item = 0;
@@ -381,6 +523,11 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
     if (!len_ok && lane == 0 && h == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
     const int nq = len_ok ? nq_len(len, a.residual, G) : 0;
     const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
+    // quantised splits of this sequence that hold pages; the fused merge
+    // counts and reads only those and the residual slot
+    const int nv =
+        max(0, min(n_qsplit, (nq / kPage + kSplitPages - 1) / kSplitPages - a.split_lo));
+    const bool real = is_res || slot < nv;
 
     int n_units = 0, page_lo = 0, row = 0, my_phys = 0;
     if (len_ok && !is_res) {
@@ -402,10 +549,11 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
       }
     }
     if (n_units <= 0) {
-      if (lane < a.grp) {
+      if (lane < a.grp && (real || !a.fuse_merge)) {
         a.part_ml[(ml_base + lane) * 2 + 0] = -INFINITY;
         a.part_ml[(ml_base + lane) * 2 + 1] = 0.f;
       }
+      if (real) item_done(b, h, nv);
       continue;
     }
 
@@ -427,8 +575,8 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
           mbar_arrive_expect_tx(&bars[stg], NP * F::BODY);
 #pragma unroll
           for (int p = 0; p < NP; ++p)
-            bulk_g2s(ring + stg * SB + p * F::BODY, pool_h + phys[p] * page_stride, F::BODY,
-                     &bars[stg]);
+            bulk_g2s_hint(ring + stg * SB + p * F::BODY, pool_h + phys[p] * page_stride, F::BODY,
+                          &bars[stg], pol);
         }
       };
       auto issue_meta = [&](int grp, int buf) {  // the group's key-meta slices
@@ -441,8 +589,8 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
           mbar_arrive_expect_tx(bar, F::META);
 #pragma unroll
           for (int i = 0; i < F::PPG; ++i)
-            bulk_g2s(meta + buf * F::META + i * F::KMS, pool_h + phys[i] * page_stride + F::BODY,
-                     F::KMS, bar);
+            bulk_g2s_hint(meta + buf * F::META + i * F::KMS,
+                          pool_h + phys[i] * page_stride + F::BODY, F::KMS, bar, pol);
         }
       };
       issue_meta(0, gcount & 1);
@@ -562,6 +710,7 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
         }
       }
       write_partial<D, NVG>(a, st, ml_base, VEnc<BITS>::kScale);
+      item_done(b, h, nv);
       continue;
     }
 
@@ -576,8 +725,8 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
       const int ci = u >> 1;
       const int chunk = ((nq + ci * kPage) % a.ring_cap) / kPage;
       mbar_arrive_expect_tx(&bars[stg], F::RBLK);
-      bulk_g2s(ring + stg * SB, ring_base + (int64_t)chunk * CHUNK + (u & 1) * F::RBLK, F::RBLK,
-               &bars[stg]);
+      bulk_g2s_hint(ring + stg * SB, ring_base + (int64_t)chunk * CHUNK + (u & 1) * F::RBLK,
+                    F::RBLK, &bars[stg], pol);
     };
     int issued = min(ST, n);
     int istage = stage;  // stage of the next unit to issue
@@ -646,6 +795,7 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
       }
     }
     write_partial<D, NVG>(a, st, ml_base, 1.f);
+    item_done(b, h, nv);
   }
 
   // the last warp to finish resets the work counters for the next launch
@@ -660,41 +810,15 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
   }
 }
 
-// ---------------------------------------------------------------------------
-// merge kernel: one CTA per (q head, sequence)
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) merge_kernel(const float* __restrict__ part_ml,
-                                                    const float* __restrict__ part_o, int n_slots,
-                                                    int num_seqs, int num_q_heads, int D,
-                                                    void* __restrict__ out, int out_dtype) {
-  const int hq = blockIdx.x, b = blockIdx.y;
-  const int64_t stride = (int64_t)num_seqs * num_q_heads;
-  const int64_t i0 = (int64_t)b * num_q_heads + hq;
-  float M = -INFINITY;
-  for (int s = 0; s < n_slots; ++s) M = fmaxf(M, part_ml[(s * stride + i0) * 2]);
-  float L = 0.f;
-  if (M != -INFINITY)
-    for (int s = 0; s < n_slots; ++s) {
-      const float m = part_ml[(s * stride + i0) * 2];
-      if (m != -INFINITY) L = fmaf(part_ml[(s * stride + i0) * 2 + 1], fast_exp2(m - M), L);
-    }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  for (int c = threadIdx.x; c < D; c += blockDim.x) {
-    float O = 0.f;
-    if (M != -INFINITY)
-      for (int s = 0; s < n_slots; ++s) {
-        const float m = part_ml[(s * stride + i0) * 2];
-        if (m != -INFINITY) O = fmaf(part_o[(s * stride + i0) * D + c], fast_exp2(m - M), O);
-      }
-    const float v = O * inv;
-    const int64_t oi = i0 * D + c;
-    if (out_dtype == TKV_F32)
-      static_cast<float*>(out)[oi] = v;
-    else if (out_dtype == TKV_BF16)
-      static_cast<__nv_bfloat16*>(out)[oi] = __float2bfloat16_rn(v);
-    else
-      static_cast<__half*>(out)[oi] = __float2half_rn(v);
-  }
+// merge kernel: one warp per (q head, sequence); same per-head arithmetic as
+// the merge fused into the decode kernel, so both give identical outputs
+__global__ void __launch_bounds__(32) merge_kernel(const float* __restrict__ part_ml,
+                                                   const float* __restrict__ part_o, int n_slots,
+                                                   int num_seqs, int num_q_heads, int D,
+                                                   void* __restrict__ out, int out_dtype) {
+  merge_heads<1>(part_ml, part_o, n_slots, n_slots, n_slots, (int64_t)num_seqs * num_q_heads,
+                 (int64_t)blockIdx.y * num_q_heads + blockIdx.x, 1, D, out, out_dtype,
+                 threadIdx.x);
 }
 
 // ---------------------------------------------------------------------------
@@ -745,7 +869,7 @@ int launch_decode_splits(DecodeArgs a, int head_dim, int bits, int, cudaStream_t
 int launch_merge(const float* part_ml, const float* part_o, int n_slots, int num_seqs,
                  int num_q_heads, int head_dim, void* out, int out_dtype, cudaStream_t stream) {
   dim3 grid(num_q_heads, num_seqs);
-  merge_kernel<<<grid, 128, 0, stream>>>(part_ml, part_o, n_slots, num_seqs, num_q_heads,
+  merge_kernel<<<grid, 32, 0, stream>>>(part_ml, part_o, n_slots, num_seqs, num_q_heads,
                                          head_dim, out, out_dtype);
   return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
 }

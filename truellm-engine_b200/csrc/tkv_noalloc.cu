@@ -6,7 +6,7 @@
 // provide one: a kernel plugin handed only the engine's tensors, a host whose
 // allocator owns all device memory and forbids side allocations, or a decode
 // loop that must not call cudaMalloc (it can synchronise the device) in the
-// per-token path.  tkv_paged_decode_noalloc runs the same two kernels with the
+// per-token path.  tkv_paged_decode_noalloc runs the same kernel with the
 // workspace taken from a fixed static device array instead.
 //
 // The array below lives in every GPU that loads this library, for the life of
@@ -21,7 +21,6 @@
 namespace {
 
 constexpr size_t kScratchBytes = TKV_NOALLOC_SCRATCH_BYTES;
-constexpr size_t kCounterBytes = 256;  // work counters at the start (must start at zero)
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_decode_scratch[kScratchBytes];
@@ -29,8 +28,9 @@ static __device__ __align__(256) unsigned char g_decode_scratch[kScratchBytes];
 std::mutex g_setup_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
 
-// Per-device set-up: device address of the scratch array and zeroed work
-// counters (the decode kernels leave them zero after every call).
+// Per-device set-up: device address of the scratch array, zeroed once (its
+// work and completion counters must start at zero; the decode kernel leaves
+// them zero after every call).
 int scratch_for_current_device(void** ptr, cudaStream_t stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
@@ -40,7 +40,7 @@ int scratch_for_current_device(void** ptr, cudaStream_t stream) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || p == nullptr)
       return TKV_BACKEND_ERROR;
-    if (cudaMemsetAsync(p, 0, kCounterBytes, stream) != cudaSuccess) return TKV_BACKEND_ERROR;
+    if (cudaMemsetAsync(p, 0, kScratchBytes, stream) != cudaSuccess) return TKV_BACKEND_ERROR;
     g_scratch_ptr[dev] = p;
   }
   *ptr = g_scratch_ptr[dev];
