@@ -566,32 +566,25 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
       const int n_steps = n_units / NP;
       const uint8_t* pool_h = a.pool + (int64_t)h * F::PB;
       const int64_t page_stride = (int64_t)a.n_kv_heads * F::PB;
-      // step j (NP pages) goes to ring stage stg; whole warp (shuffles), lane 0 issues
+      // step j (NP pages) goes to ring stage stg: lane 0 posts the byte count,
+      // lanes 0..NP-1 issue one page copy each (one warp instruction)
       auto issue_step = [&](int j, int stg) {
-        int phys[NP];
-#pragma unroll
-        for (int p = 0; p < NP; ++p) phys[p] = __shfl_sync(0xffffffffu, my_phys, j * NP + p);
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&bars[stg], NP * F::BODY);
-#pragma unroll
-          for (int p = 0; p < NP; ++p)
-            bulk_g2s_hint(ring + stg * SB + p * F::BODY, pool_h + phys[p] * page_stride, F::BODY,
-                          &bars[stg], pol);
-        }
+        const int ph = __shfl_sync(0xffffffffu, my_phys, (j * NP + lane) & 31);
+        if (lane == 0) mbar_arrive_expect_tx(&bars[stg], NP * F::BODY);
+        __syncwarp();
+        if (lane < NP)
+          bulk_g2s_hint(ring + stg * SB + lane * F::BODY, pool_h + ph * page_stride, F::BODY,
+                        &bars[stg], pol);
       };
-      auto issue_meta = [&](int grp, int buf) {  // the group's key-meta slices
-        int phys[F::PPG];
-#pragma unroll
-        for (int i = 0; i < F::PPG; ++i)
-          phys[i] = __shfl_sync(0xffffffffu, my_phys, grp * F::PPG + i);
-        if (lane == 0) {
-          uint64_t* bar = &bars[ST + buf];
-          mbar_arrive_expect_tx(bar, F::META);
-#pragma unroll
-          for (int i = 0; i < F::PPG; ++i)
-            bulk_g2s_hint(meta + buf * F::META + i * F::KMS,
-                          pool_h + phys[i] * page_stride + F::BODY, F::KMS, bar, pol);
-        }
+      // the group's key-meta slices, lanes 0..PPG-1 one slice each
+      auto issue_meta = [&](int grp, int buf) {
+        const int ph = __shfl_sync(0xffffffffu, my_phys, (grp * F::PPG + lane) & 31);
+        uint64_t* bar = &bars[ST + buf];
+        if (lane == 0) mbar_arrive_expect_tx(bar, F::META);
+        __syncwarp();
+        if (lane < F::PPG)
+          bulk_g2s_hint(meta + buf * F::META + lane * F::KMS,
+                        pool_h + ph * page_stride + F::BODY, F::KMS, bar, pol);
       };
       issue_meta(0, gcount & 1);
       {
@@ -721,20 +714,23 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
     const uint8_t* ring_base = reinterpret_cast<const uint8_t*>(a.ring) +
                                (((int64_t)row * a.n_kv_heads + h) * chunks_per_row) * CHUNK;
     const int n = n_units;
-    auto issue_unit = [&](int u, int stg) {  // lane 0
+    auto issue_unit = [&](int u, int stg) {  // one lane per unit
       const int ci = u >> 1;
       const int chunk = ((nq + ci * kPage) % a.ring_cap) / kPage;
       mbar_arrive_expect_tx(&bars[stg], F::RBLK);
       bulk_g2s_hint(ring + stg * SB, ring_base + (int64_t)chunk * CHUNK + (u & 1) * F::RBLK,
                     F::RBLK, &bars[stg], pol);
     };
-    int issued = min(ST, n);
+    // units u0 .. u0+cnt-1 into consecutive stages from istage, one per lane
+    int issued = 0;
     int istage = stage;  // stage of the next unit to issue
-    if (lane == 0)
-      for (int u = 0; u < issued; ++u) {
-        issue_unit(u, istage);
-        istage = istage + 1 == ST ? 0 : istage + 1;
-      }
+    auto issue_units = [&](int lim) {
+      const int cnt = lim - issued;
+      if (lane < cnt) issue_unit(issued + lane, (istage + lane) % ST);
+      istage = (istage + cnt) % ST;
+      issued = lim;
+    };
+    issue_units(min(ST, n));
     uint32_t bq[F::NKB][2];
 #pragma unroll
     for (int kb = 0; kb < F::NKB; ++kb)
@@ -786,13 +782,7 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
         mma16816(st.o[mb], x.x & m01, x.y & m01, x.z & m23, x.w & m23, b01, b23);
       }
       __syncwarp();
-      if (lane == 0) {
-        const int lim = min(n, 2 * (ci + 1) + ST);
-        for (; issued < lim; ++issued) {
-          issue_unit(issued, istage);
-          istage = istage + 1 == ST ? 0 : istage + 1;
-        }
-      }
+      issue_units(min(n, 2 * (ci + 1) + ST));
     }
     write_partial<D, NVG>(a, st, ml_base, 1.f);
     item_done(b, h, nv);
