@@ -5,9 +5,10 @@
 // order:
 //   1. flush:    one CTA per (key group, kv head, sequence).  It gathers the G
 //                tokens of the group (old ones from the fp16 ring, new ones
-//                from the input), quantises keys per channel and values per
-//                token with the reference quantizer (kivi_cache.cu:92-124) and
-//                writes the group's pages with coalesced 32-bit stores.
+//                from the input with cp.async), quantises keys per channel and
+//                values per token with the reference quantizer
+//                (kivi_cache.cu:92-124) and writes the group's pages with
+//                coalesced 32- and 128-bit stores.
 //   2. residual: copies the new tokens that stay in fp16 into the ring.
 // Running the flush before the residual write keeps ring slots that are read
 // by (1) from being overwritten by (2) in the same call.
@@ -47,31 +48,76 @@ __device__ __forceinline__ bool append_lengths_ok(const AppendArgs& a, int L, in
          (int64_t)L + (c1 - c0) <= (int64_t)a.max_blocks * kPage;
 }
 
-constexpr int kFlushThreads = 256;
-constexpr int kMaxG = 128, kMaxD = 128;
+constexpr int kFlushThreads = 128;
 
-// Shared memory of the flush kernel: fp16 tiles with a padded row stride
-// (D + 2 halves) so the per-token value scans hit distinct banks, plus 1-byte
-// code matrices and the fp16 meta.
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src_gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst_smem)),
+               "l"(src_gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+}
+
+__device__ __forceinline__ float h2f(uint16_t h) {
+  return __half2float(*reinterpret_cast<const __half*>(&h));
+}
+
+// Sequential-scan extremes of the reference quantizer (kivi_cache.cu:92-124:
+// gmin/gmax seeded with +/-FLT_MAX, strict compares, so NaN never enters and
+// the first of equal values wins) from the packed-f16 min/max of the same
+// values (min.f16x2 / max.f16x2 skip NaN).  The only equal values with
+// different bits are +0 and -0: when an extreme is zero, its sign is that of
+// the first zero in scan order, supplied by `first_zero_sign` (rare path).
+template <typename FirstZero>
+__device__ __forceinline__ void scan_extremes(__half hmn, __half hmx, float& gmin, float& gmax,
+                                              FirstZero first_zero_sign) {
+  gmin = __half2float(hmn);
+  gmax = __half2float(hmx);
+  if (gmin == INFINITY) gmin = FLT_MAX;      // no value below the seed
+  if (gmax == -INFINITY) gmax = -FLT_MAX;
+  if (gmin == 0.f || gmax == 0.f) {
+    const float z = first_zero_sign();
+    if (gmin == 0.f) gmin = z;
+    if (gmax == 0.f) gmax = z;
+  }
+}
+
+// Shared memory of the flush kernel: the group's fp16 K and V tiles with
+// rows padded by 8 halves (the fragment-order value reads then hit distinct
+// banks), per-channel / per-token quantisation parameters and meta words.
+template <int D, int G>
 struct FlushSmem {
-  uint16_t kt[kMaxG * (kMaxD + 2)];
-  uint16_t vt[kMaxG * (kMaxD + 2)];
-  uint8_t kq[kMaxG * kMaxD];
-  uint8_t vq[kMaxG * kMaxD];
-  uint32_t kmeta[kMaxD];          // (step | zero << 16) per channel
-  uint32_t vmeta[kMaxG * 8];      // (step | zero << 16) per token and value group
+  static constexpr int TS = D + 8;               // row stride in halves
+  static constexpr int NVG = D > G ? D / G : 1;  // value groups per token
+  uint16_t kt[G * TS];
+  uint16_t vt[G * TS];
+  float2 kp[D];          // (gmin, scale) per channel
+  float2 vp[G * NVG];    // (gmin, scale) per token and value group
+  uint32_t kmeta[D];     // step | zero << 16
+  uint32_t vmeta[G * NVG];
+  int phys[G / kPage];   // the group's pages
 };
 
+// One CTA per (key group, kv head, sequence): gathers the G tokens of the
+// group (old ones from the fp16 ring, new ones from the input with 16-byte
+// cp.async), rounds bf16 input to fp16, computes the key parameters per
+// channel and the value parameters per token (and value group), then packs
+// and stores the group's pages.
+template <int D, int BITS, int G>
 __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs a) {
+  using S_t = FlushSmem<D, G>;
+  constexpr int TS = S_t::TS, NVG = S_t::NVG, QMAX = (1 << BITS) - 1;
+  constexpr int VG_CH = D > G ? G : D;  // channels per value group
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  FlushSmem& S = *reinterpret_cast<FlushSmem*>(smem_raw);
+  S_t& S = *reinterpret_cast<S_t*>(smem_raw);
+  const int tid = threadIdx.x;
   const int b = blockIdx.z, h = blockIdx.y, gi = blockIdx.x;
-  const int D = a.head_dim, G = a.group, TS = D + 2;
   const int L = a.lens_old[b];
   const int c0 = a.cu_new[b], c1 = a.cu_new[b + 1];
   const int T = c1 - c0;
   if (!append_lengths_ok(a, L, c0, c1)) {
-    if (threadIdx.x == 0 && gi == 0 && h == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
+    if (tid == 0 && gi == 0 && h == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
     return;
   }
   const int L2 = L + T;
@@ -80,183 +126,233 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
   if (t0 >= nq1) return;
   const int row = a.seq_slots ? a.seq_slots[b] : b;
   if (t0 < L && (row < 0 || row >= a.max_seqs)) {
-    if (threadIdx.x == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
+    if (tid == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
     return;
   }
   const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
-  const int qmax = (1 << a.bits) - 1;
+  const int n_old = min(max(L - t0, 0), G);  // tile rows [0, n_old) come from the ring
 
-  // ---- gather the G x D tiles (fp16 values) --------------------------------
-  // Old tokens come from ring chunks (fragment order, 16-byte vectors); new
-  // tokens from input rows [cu_new[b] + (t - L)][h][0:D].
-  const int vec_per_row = D / 8;  // 16-byte vectors per token row
-  for (int i = threadIdx.x; i < G * vec_per_row; i += kFlushThreads) {
-    const int t = i / vec_per_row, v = i % vec_per_row;
-    const int tok = t0 + t;
-    if (tok < L) continue;  // old token: gathered from its ring chunk below
-    const int64_t in_row = ((int64_t)a.cu_new[b] + (tok - L)) * a.n_kv_heads + h;
-    const int64_t e0 = in_row * D + v * 8;
-    uint4 kw = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.k_new) + e0);
-    uint4 vw = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.v_new) + e0);
-    const uint16_t* ks = reinterpret_cast<const uint16_t*>(&kw);
-    const uint16_t* vs = reinterpret_cast<const uint16_t*>(&vw);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      uint16_t kh = ks[j], vh = vs[j];
-      if (a.in_bf16) {
-        __half k16 = __float2half_rn(__bfloat162float(*reinterpret_cast<__nv_bfloat16*>(&kh)));
-        __half v16 = __float2half_rn(__bfloat162float(*reinterpret_cast<__nv_bfloat16*>(&vh)));
-        kh = *reinterpret_cast<uint16_t*>(&k16);
-        vh = *reinterpret_cast<uint16_t*>(&v16);
-      }
-      S.kt[t * TS + v * 8 + j] = kh;
-      S.vt[t * TS + v * 8 + j] = vh;
-    }
+  // ---- gather ---------------------------------------------------------------
+  // New tokens: input rows [cu_new[b] + (tok - L)][h][0:D], 16-byte vectors
+  // (the entry point requires 16-byte aligned inputs).
+  constexpr int VPR = D / 8;  // vectors per token row
+  for (int i = n_old * VPR + tid; i < G * VPR; i += kFlushThreads) {
+    const int t = i / VPR, v = i - t * VPR;
+    const int64_t e0 = (((int64_t)c0 + (t0 + t - L)) * a.n_kv_heads + h) * D + v * 8;
+    cp_async16(&S.kt[t * TS + v * 8], static_cast<const uint16_t*>(a.k_new) + e0);
+    cp_async16(&S.vt[t * TS + v * 8], static_cast<const uint16_t*>(a.v_new) + e0);
   }
-  // Ring chunks: handled chunk-wise so each 16-byte vector is read once.
-  {
-    const int first_chunk_tok = t0, last_tok = min(t0 + G, L);
-    const int vecs_per_chunk = kPage * D / 8;
-    const int n_chunks = last_tok > first_chunk_tok ? (last_tok - first_chunk_tok + kPage - 1) / kPage : 0;
-    for (int i = threadIdx.x; i < n_chunks * vecs_per_chunk; i += kFlushThreads) {
-      const int ch = i / vecs_per_chunk, v = i % vecs_per_chunk;
-      const int ctok = t0 + ch * kPage;  // chunk's first token (t0 is a multiple of 16)
-      const uint16_t* kc = ring_chunk(a, row, h, ctok, 0);
-      const uint16_t* vc = ring_chunk(a, row, h, ctok, 1);
-      uint4 kw = reinterpret_cast<const uint4*>(kc)[v];
-      uint4 vw = reinterpret_cast<const uint4*>(vc)[v];
+  if (tid < G / kPage) {
+    const int ph = bt[t0 / kPage + tid];
+    S.phys[tid] = ph;
+    if (ph < 0 || ph >= a.num_pages) set_err(a.err, TKV_ERR_BAD_PAGE);
+  }
+  // Old tokens: ring chunks (fragment order), each 16-byte vector read once.
+  if (n_old > 0) {
+    constexpr int VPC = kPage * D / 8;  // vectors per chunk block
+    const int n_chunks = (n_old + kPage - 1) / kPage;
+    for (int i = tid; i < n_chunks * VPC; i += kFlushThreads) {
+      const int ch = i / VPC, v = i - ch * VPC;
+      const int ctok = t0 + ch * kPage;  // t0 is a multiple of 16
+      const uint4 kw = reinterpret_cast<const uint4*>(ring_chunk(a, row, h, ctok, 0))[v];
+      const uint4 vw = reinterpret_cast<const uint4*>(ring_chunk(a, row, h, ctok, 1))[v];
       const uint16_t* ks = reinterpret_cast<const uint16_t*>(&kw);
       const uint16_t* vs = reinterpret_cast<const uint16_t*>(&vw);
-      // vector v = (block index bi, lane l): bi = v / 32, l = v % 32
-      const int bi = v >> 5, l = v & 31;
+      const int bi = v >> 5, l = v & 31, g = l >> 2, tig = l & 3;
 #pragma unroll
       for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          // K block: lane l = 4*g + tig; r = 2*hi + th; element (t = g + 8 th, c = 16 bi + 2 tig + 8 hi + e)
-          {
-            const int g = l >> 2, tig = l & 3, hi = r >> 1, th = r & 1;
-            const int t = g + 8 * th, c = 16 * bi + 2 * tig + 8 * hi + e;
-            const int tt = ch * kPage + t;
-            if (ctok + t < L) S.kt[tt * TS + c] = ks[2 * r + e];
+          {  // K block: r = 2*hi + th -> (t = g + 8 th, c = 16 bi + 2 tig + 8 hi + e)
+            const int t = ch * kPage + g + 8 * (r & 1), c = 16 * bi + 2 * tig + 8 * (r >> 1) + e;
+            if (t < n_old) S.kt[t * TS + c] = ks[2 * r + e];
           }
-          // V block: lane l = 4*g + tig; r = 2*th + rh; element (t = 8 th + 2 tig + e, c = 16 bi + g + 8 rh)
-          {
-            const int g = l >> 2, tig = l & 3, th = r >> 1, rh = r & 1;
-            const int t = 8 * th + 2 * tig + e, c = 16 * bi + g + 8 * rh;
-            const int tt = ch * kPage + t;
-            if (ctok + t < L) S.vt[tt * TS + c] = vs[2 * r + e];
+          {  // V block: r = 2*th + rh -> (t = 8 th + 2 tig + e, c = 16 bi + g + 8 rh)
+            const int t = ch * kPage + 8 * (r >> 1) + 2 * tig + e, c = 16 * bi + g + 8 * (r & 1);
+            if (t < n_old) S.vt[t * TS + c] = vs[2 * r + e];
           }
         }
     }
   }
+  cp_async_wait_all();
   __syncthreads();
+  // bf16 input -> fp16 (RN) in place, rows of new tokens
+  if (a.in_bf16) {
+    for (int i = n_old * VPR + tid; i < G * VPR; i += kFlushThreads) {
+      const int t = i / VPR, v = i - t * VPR;
+#pragma unroll
+      for (int kv = 0; kv < 2; ++kv) {
+        uint4* p = reinterpret_cast<uint4*>(&(kv ? S.vt : S.kt)[t * TS + v * 8]);
+        uint4 x = *p;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&x);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xffff0000u);
+          const __half2 hh = __floats2half2_rn(lo, hi);
+          w[j] = *reinterpret_cast<const uint32_t*>(&hh);
+        }
+        *p = x;
+      }
+    }
+    __syncthreads();
+  }
 
-  // ---- quantise: keys per channel over G tokens, values per token over G channels
-  const int nv = G * a.n_vgroups;
-  for (int i = threadIdx.x; i < D + nv; i += kFlushThreads) {
-    if (i < D) {
-      const int c = i;
-      float gmin = FLT_MAX, gmax = -FLT_MAX;
+  // ---- pass 1: quantisation parameters -------------------------------------
+  if (tid < 64) {
+    // keys: channels 2 tid, 2 tid + 1 over the G tokens
+    if (2 * tid < D) {
+      __half2 mn = __half2half2(__ushort_as_half(0x7c00u)), mx = __half2half2(__ushort_as_half(0xfc00u));
+#pragma unroll 8
       for (int t = 0; t < G; ++t) {
-        float x = __half2float(*reinterpret_cast<const __half*>(&S.kt[t * TS + c]));
-        if (x < gmin) gmin = x;
-        if (x > gmax) gmax = x;
+        const __half2 x = *reinterpret_cast<const __half2*>(&S.kt[t * TS + 2 * tid]);
+        mn = __hmin2(mn, x);
+        mx = __hmax2(mx, x);
       }
-      QParams qp = quant_params(gmin, gmax, qmax);
-      for (int t = 0; t < G; ++t) {
-        float x = __half2float(*reinterpret_cast<const __half*>(&S.kt[t * TS + c]));
-        S.kq[t * D + c] = static_cast<uint8_t>(quant_code(x, qp, qmax));
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int c = 2 * tid + e;
+        float gmin, gmax;
+        scan_extremes(e ? __high2half(mn) : __low2half(mn), e ? __high2half(mx) : __low2half(mx),
+                      gmin, gmax, [&]() {
+                        for (int t = 0; t < G; ++t) {
+                          const float x = h2f(S.kt[t * TS + c]);
+                          if (x == 0.f) return x;
+                        }
+                        return 0.f;
+                      });
+        const QParams qp = quant_params(gmin, gmax, QMAX);
+        S.kp[c] = make_float2(qp.gmin, qp.scale);
+        S.kmeta[c] = (uint32_t)qp.hstep | ((uint32_t)qp.hzero << 16);
       }
-      S.kmeta[c] = (uint32_t)qp.hstep | ((uint32_t)qp.hzero << 16);
-    } else {
-      const int j = i - D, t = j / a.n_vgroups, vg = j % a.n_vgroups;
-      const int c0 = vg * G, c1 = min(D, c0 + G);
-      float gmin = FLT_MAX, gmax = -FLT_MAX;
-      for (int c = c0; c < c1; ++c) {
-        float x = __half2float(*reinterpret_cast<const __half*>(&S.vt[t * TS + c]));
-        if (x < gmin) gmin = x;
-        if (x > gmax) gmax = x;
+    }
+  } else {
+    // values: per token, per group of VG_CH channels
+    for (int j = tid - 64; j < G * NVG; j += kFlushThreads - 64) {
+      const int t = j / NVG, vg = j - t * NVG;
+      const uint16_t* rowp = &S.vt[t * TS + vg * VG_CH];
+      __half2 mn = __half2half2(__ushort_as_half(0x7c00u)), mx = __half2half2(__ushort_as_half(0xfc00u));
+#pragma unroll
+      for (int c = 0; c < VG_CH; c += 8) {
+        const uint4 x = *reinterpret_cast<const uint4*>(rowp + c);
+        const __half2* hx = reinterpret_cast<const __half2*>(&x);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          mn = __hmin2(mn, hx[k]);
+          mx = __hmax2(mx, hx[k]);
+        }
       }
-      QParams qp = quant_params(gmin, gmax, qmax);
-      for (int c = c0; c < c1; ++c) {
-        float x = __half2float(*reinterpret_cast<const __half*>(&S.vt[t * TS + c]));
-        S.vq[t * D + c] = static_cast<uint8_t>(quant_code(x, qp, qmax));
-      }
-      S.vmeta[t * a.n_vgroups + vg] = (uint32_t)qp.hstep | ((uint32_t)qp.hzero << 16);
+      float gmin, gmax;
+      scan_extremes(__hmin(__low2half(mn), __high2half(mn)), __hmax(__low2half(mx), __high2half(mx)),
+                    gmin, gmax, [&]() {
+                      for (int c = 0; c < VG_CH; ++c) {
+                        const float x = h2f(rowp[c]);
+                        if (x == 0.f) return x;
+                      }
+                      return 0.f;
+                    });
+      const QParams qp = quant_params(gmin, gmax, QMAX);
+      S.vp[j] = make_float2(qp.gmin, qp.scale);
+      S.vmeta[j] = (uint32_t)qp.hstep | ((uint32_t)qp.hzero << 16);
     }
   }
   __syncthreads();
 
-  // ---- pack and store the group's pages, one 32-bit word per thread step ---
-  const int pages = G / kPage;
-  const int rb = D * a.bits / 8;            // K code bytes per token row
-  const int kwords = kPage * rb / 4;        // K code words per page
-  const int W = D * a.bits / 64;            // V code words per lane
-  const int VW = W < 4 ? W : 4;
-  const int vwords = 32 * W;                // V code words per page
-  const int vmwords = kPage * a.n_vgroups;  // V meta words per page
-  const int kmwords = a.k_meta_slice / 4;   // K meta words per page
-  const int per_page = kwords + vwords + vmwords + kmwords;
-  for (int i = threadIdx.x; i < pages * per_page; i += kFlushThreads) {
-    const int pi = i / per_page;
-    int j = i % per_page;
-    const int phys = bt[(t0 / kPage) + pi];
-    if (phys < 0 || phys >= a.num_pages) {
-      set_err(a.err, TKV_ERR_BAD_PAGE);
-      continue;
-    }
-    uint8_t* blk = a.pool + ((int64_t)phys * a.n_kv_heads + h) * a.page_bytes;
-    const int tb = pi * kPage;  // first token row of this page inside the tile
-    if (j < kwords) {
-      const int t = j / (rb / 4), wj = j % (rb / 4);
-      const uint8_t* q = &S.kq[(tb + t) * D];
-      uint32_t w = 0;
-      if (a.bits == 4) {
+  auto code = [&](float x, float2 p) {
+    int q = __float2int_rn(__fmul_rn(__fsub_rn(x, p.x), p.y));
+    q = q < 0 ? 0 : q;
+    return static_cast<uint32_t>(q > QMAX ? QMAX : q);
+  };
+  auto page_base = [&](int pi) -> uint8_t* {
+    const int ph = S.phys[pi];
+    return (ph < 0 || ph >= a.num_pages)
+               ? nullptr
+               : a.pool + ((int64_t)ph * a.n_kv_heads + h) * a.page_bytes;
+  };
+
+  // ---- pass 2a: key codes, row-major [16 tokens][D * BITS / 8 bytes] --------
+  {
+    constexpr int CPW = 32 / BITS;     // channels per 32-bit word
+    constexpr int NWR = D / CPW;       // words per token row
+    constexpr int TSTEP = kFlushThreads / NWR;
+    const int w = tid % NWR;
+    float2 p[CPW];
 #pragma unroll
-        for (int n = 0; n < 8; ++n) w |= (uint32_t)q[8 * wj + n] << (4 * n);
-      } else {
+    for (int n = 0; n < CPW; ++n) p[n] = S.kp[w * CPW + n];
+    for (int t = tid / NWR; t < G; t += TSTEP) {
+      uint32_t word = 0;
 #pragma unroll
-        for (int n = 0; n < 16; ++n) w |= (uint32_t)q[16 * wj + n] << (2 * n);
+      for (int n8 = 0; n8 < CPW; n8 += 8) {
+        const uint4 x = *reinterpret_cast<const uint4*>(&S.kt[t * TS + w * CPW + n8]);
+        const uint16_t* hx = reinterpret_cast<const uint16_t*>(&x);
+#pragma unroll
+        for (int n = 0; n < 8; ++n) word |= code(h2f(hx[n]), p[n8 + n]) << (BITS * (n8 + n));
       }
-      reinterpret_cast<uint32_t*>(blk + a.k_codes_off)[t * (rb / 4) + wj] = w;
-      continue;
+      uint8_t* blk = page_base(t / kPage);
+      if (blk)
+        reinterpret_cast<uint32_t*>(blk + a.k_codes_off)[(t % kPage) * NWR + w] = word;
     }
-    j -= kwords;
-    if (j < vwords) {
-      const int l = j / W, wv = j % W;
-      const int g = l >> 2, tig = l & 3;
-      uint32_t w = 0;
+  }
+
+  // ---- pass 2b: value codes in mma A-fragment order --------------------------
+  {
+    constexpr int W = D * BITS / 64;  // words per lane
+    constexpr int VW = W < 4 ? W : 4;
+    for (int pl = tid; pl < (G / kPage) * 32; pl += kFlushThreads) {
+      const int pi = pl >> 5, l = pl & 31, g = l >> 2, tig = l & 3;
+      const int tb = pi * kPage;
+      uint8_t* blk = page_base(pi);
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
+      for (int q = 0; q < W / VW; ++q) {
+        uint32_t words[VW];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int rh = k >> 1, th = k & 1;
-          const int t = 8 * th + 2 * tig + e;
-          if (a.bits == 4) {
-            const int c = 16 * wv + g + 8 * rh;
-            w |= (uint32_t)S.vq[(tb + t) * D + c] << (4 * (k + 4 * e));
-          } else {
+        for (int u = 0; u < VW; ++u) {
+          const int wv = q * VW + u;
+          uint32_t wd = 0;
 #pragma unroll
-            for (int mbi = 0; mbi < 2; ++mbi) {
-              const int c = 16 * (2 * wv + mbi) + g + 8 * rh;
-              w |= (uint32_t)S.vq[(tb + t) * D + c] << (2 * (4 * mbi + k + 8 * e));
+          for (int k = 0; k < 4; ++k)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int rh = k >> 1, th = k & 1;
+              const int t = tb + 8 * th + 2 * tig + e;
+              if (BITS == 4) {
+                const int c = 16 * wv + g + 8 * rh;
+                wd |= code(h2f(S.vt[t * TS + c]), S.vp[t * NVG + c / VG_CH]) << (4 * (k + 4 * e));
+              } else {
+#pragma unroll
+                for (int mbi = 0; mbi < 2; ++mbi) {
+                  const int c = 16 * (2 * wv + mbi) + g + 8 * rh;
+                  wd |= code(h2f(S.vt[t * TS + c]), S.vp[t * NVG + c / VG_CH])
+                        << (2 * (4 * mbi + k + 8 * e));
+                }
+              }
             }
-          }
+          words[u] = wd;
         }
-      const int off = ((wv / VW) * 32 + l) * (4 * VW) + (wv % VW) * 4;
-      *reinterpret_cast<uint32_t*>(blk + a.v_codes_off + off) = w;
-      continue;
+        if (blk) {
+          uint8_t* dst = blk + a.v_codes_off + (q * 32 + l) * (4 * VW);
+          if (VW == 4)
+            *reinterpret_cast<uint4*>(dst) = make_uint4(words[0], words[VW > 1 ? 1 : 0],
+                                                        words[VW > 2 ? 2 : 0], words[VW > 3 ? 3 : 0]);
+          else
+            *reinterpret_cast<uint2*>(dst) = make_uint2(words[0], words[VW > 1 ? 1 : 0]);
+        }
+      }
     }
-    j -= vwords;
-    if (j < vmwords) {
-      const int t = j / a.n_vgroups, vg = j % a.n_vgroups;
-      reinterpret_cast<uint32_t*>(blk + a.v_meta_off)[j] = S.vmeta[(tb + t) * a.n_vgroups + vg];
-      continue;
+  }
+
+  // ---- pass 2c: value meta [16 tokens][NVG] and key meta slices per page -----
+  {
+    constexpr int VMW = kPage * NVG;   // value meta words per page
+    constexpr int KMW = D * kPage / G; // key meta words per page (= k_meta_slice / 4)
+    for (int i = tid; i < (G / kPage) * (VMW + KMW); i += kFlushThreads) {
+      const int pi = i / (VMW + KMW), j = i - pi * (VMW + KMW);
+      uint8_t* blk = page_base(pi);
+      if (!blk) continue;
+      if (j < VMW)
+        reinterpret_cast<uint32_t*>(blk + a.v_meta_off)[j] = S.vmeta[pi * VMW + j];
+      else
+        reinterpret_cast<uint32_t*>(blk + a.k_meta_off)[j - VMW] = S.kmeta[pi * KMW + (j - VMW)];
     }
-    j -= vmwords;
-    // K meta slice pi: words [pi * kmwords, (pi+1) * kmwords) of kmeta
-    reinterpret_cast<uint32_t*>(blk + a.k_meta_off)[j] = S.kmeta[pi * kmwords + j];
   }
 }
 
@@ -297,21 +393,41 @@ __global__ void __launch_bounds__(256) residual_write_kernel(AppendArgs a) {
   }
 }
 
-size_t flush_smem_bytes() { return sizeof(FlushSmem); }
-
-int launch_append(const AppendArgs& a, int num_seqs, cudaStream_t stream) {
+template <int D, int BITS, int G>
+static int launch_flush_t(const AppendArgs& a, int num_seqs, cudaStream_t stream) {
+  constexpr int smem = sizeof(FlushSmem<D, G>);
   static bool attr_set = false;
-  const size_t smem = sizeof(FlushSmem);
   if (!attr_set) {
-    if (cudaFuncSetAttribute(flush_groups_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
+    if (cudaFuncSetAttribute(flush_groups_kernel<D, BITS, G>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return TKV_BACKEND_ERROR;
     attr_set = true;
   }
-  const int max_groups = a.max_new / a.group + 1;
-  dim3 g1(max_groups, a.n_kv_heads, num_seqs);
-  flush_groups_kernel<<<g1, kFlushThreads, smem, stream>>>(a);
-  if (cudaGetLastError() != cudaSuccess) return TKV_BACKEND_ERROR;
+  dim3 grid(a.max_new / G + 1, a.n_kv_heads, num_seqs);
+  flush_groups_kernel<D, BITS, G><<<grid, kFlushThreads, smem, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
+}
+
+template <int D, int BITS>
+static int launch_flush_g(const AppendArgs& a, int num_seqs, cudaStream_t stream) {
+  switch (a.group) {
+    case 16: return launch_flush_t<D, BITS, 16>(a, num_seqs, stream);
+    case 32: return launch_flush_t<D, BITS, 32>(a, num_seqs, stream);
+    case 64: return launch_flush_t<D, BITS, 64>(a, num_seqs, stream);
+    case 128: return launch_flush_t<D, BITS, 128>(a, num_seqs, stream);
+  }
+  return TKV_NOT_IMPLEMENTED;
+}
+
+int launch_append(const AppendArgs& a, int num_seqs, cudaStream_t stream) {
+  int st = TKV_NOT_IMPLEMENTED;
+  if (a.head_dim == 128)
+    st = a.bits == 4 ? launch_flush_g<128, 4>(a, num_seqs, stream)
+                     : launch_flush_g<128, 2>(a, num_seqs, stream);
+  else if (a.head_dim == 64)
+    st = a.bits == 4 ? launch_flush_g<64, 4>(a, num_seqs, stream)
+                     : launch_flush_g<64, 2>(a, num_seqs, stream);
+  if (st != TKV_OK) return st;
   dim3 g2((a.max_new + kPage - 1) / kPage, a.n_kv_heads, num_seqs);
   if (g2.x > 0) {
     residual_write_kernel<<<g2, 256, 0, stream>>>(a);
