@@ -92,7 +92,7 @@ def test_append_bitexact_one_shot(ops, O, wl, cuda, D, G, R, bits, dtype):
     tw.assert_same_state(lengths)
 
 
-@pytest.mark.parametrize("chunks", [(1,), (7, 1, 33), (16,), (130, 2)])
+@pytest.mark.parametrize("chunks", [(1,), (7, 1, 33), (16,), (130, 2), (15, 2)])
 def test_append_bitexact_chunked(ops, O, wl, cuda, chunks):
     lengths = [300, 45, 161, 700]
     tw, bt, lengths, _ = _build(ops, O, wl, cuda, 128, 128, 128, 4, 2, lengths, "bf16",

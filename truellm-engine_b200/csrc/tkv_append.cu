@@ -3,13 +3,14 @@
 // Replaces reshape_and_cache (third_party/vllm_kernels/cache_kernels.cu:47-94,
 // host wrapper :202-232) for a KIVI cache.  Two launches per call, in stream
 // order:
-//   1. flush:    one CTA per (key group, kv head, sequence).  It gathers the G
+//   1. flush:    one CTA per (key group, K or V, kv head, sequence).  It gathers the G
 //                tokens of the group (old ones from the fp16 ring, new ones
 //                from the input with cp.async), quantises keys per channel and
 //                values per token with the reference quantizer
 //                (kivi_cache.cu:92-124) and writes the group's pages with
 //                coalesced 32- and 128-bit stores.
-//   2. residual: copies the new tokens that stay in fp16 into the ring.
+//   2. residual: copies the new tokens that stay in fp16 into the ring, whole
+//                16-byte fragment vectors for fully written 16-token chunks.
 // Running the flush before the residual write keeps ring slots that are read
 // by (1) from being overwritten by (2) in the same call.
 #include "tkv_common.cuh"
@@ -83,41 +84,42 @@ __device__ __forceinline__ void scan_extremes(__half hmn, __half hmx, float& gmi
   }
 }
 
-// Shared memory of the flush kernel: the group's fp16 K and V tiles with
-// rows padded by 8 halves (the fragment-order value reads then hit distinct
-// banks), per-channel / per-token quantisation parameters and meta words.
+// Shared memory of the flush kernel: the group's fp16 K (or V) tile with rows
+// padded by 8 halves (the fragment-order value reads then hit distinct
+// banks), the quantisation parameters and meta words, partial key extremes.
 template <int D, int G>
 struct FlushSmem {
   static constexpr int TS = D + 8;               // row stride in halves
   static constexpr int NVG = D > G ? D / G : 1;  // value groups per token
-  uint16_t kt[G * TS];
-  uint16_t vt[G * TS];
-  float2 kp[D];          // (gmin, scale) per channel
-  float2 vp[G * NVG];    // (gmin, scale) per token and value group
-  uint32_t kmeta[D];     // step | zero << 16
-  uint32_t vmeta[G * NVG];
+  static constexpr int NPAR = D > G * NVG ? D : G * NVG;
+  static constexpr int KSPLIT = kFlushThreads / (D / 2);  // token splits of the key scan
+  uint16_t tile[G * TS];
+  float2 par[NPAR];      // (gmin, scale) per key channel or per (token, value group)
+  uint32_t meta[NPAR];   // step | zero << 16
+  __half2 kmn[KSPLIT][D / 2], kmx[KSPLIT][D / 2];
   int phys[G / kPage];   // the group's pages
 };
 
-// One CTA per (key group, kv head, sequence): gathers the G tokens of the
-// group (old ones from the fp16 ring, new ones from the input with 16-byte
-// cp.async), rounds bf16 input to fp16, computes the key parameters per
-// channel and the value parameters per token (and value group), then packs
-// and stores the group's pages.
+// One CTA per (key group, K or V, kv head, sequence): gathers the G tokens of
+// the group (old ones from the fp16 ring, new ones from the input with
+// 16-byte cp.async), rounds bf16 input to fp16, computes the quantisation
+// parameters (keys per channel, values per token and value group), then packs
+// and stores the group's K (or V) codes and meta into its pages.
 template <int D, int BITS, int G>
 __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs a) {
   using S_t = FlushSmem<D, G>;
-  constexpr int TS = S_t::TS, NVG = S_t::NVG, QMAX = (1 << BITS) - 1;
+  constexpr int TS = S_t::TS, NVG = S_t::NVG, KSPLIT = S_t::KSPLIT, QMAX = (1 << BITS) - 1;
   constexpr int VG_CH = D > G ? G : D;  // channels per value group
   extern __shared__ __align__(16) uint8_t smem_raw[];
   S_t& S = *reinterpret_cast<S_t*>(smem_raw);
   const int tid = threadIdx.x;
-  const int b = blockIdx.z, h = blockIdx.y, gi = blockIdx.x;
+  const int b = blockIdx.z, h = blockIdx.y, gi = blockIdx.x >> 1;
+  const bool is_v = blockIdx.x & 1;
   const int L = a.lens_old[b];
   const int c0 = a.cu_new[b], c1 = a.cu_new[b + 1];
   const int T = c1 - c0;
   if (!append_lengths_ok(a, L, c0, c1)) {
-    if (tid == 0 && gi == 0 && h == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
+    if (tid == 0 && blockIdx.x == 0 && h == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
     return;
   }
   const int L2 = L + T;
@@ -126,21 +128,22 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
   if (t0 >= nq1) return;
   const int row = a.seq_slots ? a.seq_slots[b] : b;
   if (t0 < L && (row < 0 || row >= a.max_seqs)) {
-    if (tid == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
+    if (tid == 0 && !is_v) set_err(a.err, TKV_ERR_BAD_SLOT);
     return;
   }
   const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
   const int n_old = min(max(L - t0, 0), G);  // tile rows [0, n_old) come from the ring
+  uint16_t* tile = S.tile;
 
   // ---- gather ---------------------------------------------------------------
   // New tokens: input rows [cu_new[b] + (tok - L)][h][0:D], 16-byte vectors
   // (the entry point requires 16-byte aligned inputs).
   constexpr int VPR = D / 8;  // vectors per token row
+  const uint16_t* src = static_cast<const uint16_t*>(is_v ? a.v_new : a.k_new);
   for (int i = n_old * VPR + tid; i < G * VPR; i += kFlushThreads) {
     const int t = i / VPR, v = i - t * VPR;
     const int64_t e0 = (((int64_t)c0 + (t0 + t - L)) * a.n_kv_heads + h) * D + v * 8;
-    cp_async16(&S.kt[t * TS + v * 8], static_cast<const uint16_t*>(a.k_new) + e0);
-    cp_async16(&S.vt[t * TS + v * 8], static_cast<const uint16_t*>(a.v_new) + e0);
+    cp_async16(&tile[t * TS + v * 8], src + e0);
   }
   if (tid < G / kPage) {
     const int ph = bt[t0 / kPage + tid];
@@ -154,23 +157,18 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
     for (int i = tid; i < n_chunks * VPC; i += kFlushThreads) {
       const int ch = i / VPC, v = i - ch * VPC;
       const int ctok = t0 + ch * kPage;  // t0 is a multiple of 16
-      const uint4 kw = reinterpret_cast<const uint4*>(ring_chunk(a, row, h, ctok, 0))[v];
-      const uint4 vw = reinterpret_cast<const uint4*>(ring_chunk(a, row, h, ctok, 1))[v];
-      const uint16_t* ks = reinterpret_cast<const uint16_t*>(&kw);
-      const uint16_t* vs = reinterpret_cast<const uint16_t*>(&vw);
+      const uint4 w = reinterpret_cast<const uint4*>(ring_chunk(a, row, h, ctok, is_v))[v];
+      const uint16_t* xs = reinterpret_cast<const uint16_t*>(&w);
       const int bi = v >> 5, l = v & 31, g = l >> 2, tig = l & 3;
 #pragma unroll
       for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          {  // K block: r = 2*hi + th -> (t = g + 8 th, c = 16 bi + 2 tig + 8 hi + e)
-            const int t = ch * kPage + g + 8 * (r & 1), c = 16 * bi + 2 * tig + 8 * (r >> 1) + e;
-            if (t < n_old) S.kt[t * TS + c] = ks[2 * r + e];
-          }
-          {  // V block: r = 2*th + rh -> (t = 8 th + 2 tig + e, c = 16 bi + g + 8 rh)
-            const int t = ch * kPage + 8 * (r >> 1) + 2 * tig + e, c = 16 * bi + g + 8 * (r & 1);
-            if (t < n_old) S.vt[t * TS + c] = vs[2 * r + e];
-          }
+          // K block: r = 2*hi + th -> (t = g + 8 th, c = 16 bi + 2 tig + 8 hi + e)
+          // V block: r = 2*th + rh -> (t = 8 th + 2 tig + e, c = 16 bi + g + 8 rh)
+          const int t = ch * kPage + (is_v ? 8 * (r >> 1) + 2 * tig + e : g + 8 * (r & 1));
+          const int c = 16 * bi + (is_v ? g + 8 * (r & 1) : 2 * tig + 8 * (r >> 1) + e);
+          if (t < n_old) tile[t * TS + c] = xs[2 * r + e];
         }
     }
   }
@@ -180,82 +178,19 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
   if (a.in_bf16) {
     for (int i = n_old * VPR + tid; i < G * VPR; i += kFlushThreads) {
       const int t = i / VPR, v = i - t * VPR;
+      uint4* p = reinterpret_cast<uint4*>(&tile[t * TS + v * 8]);
+      uint4 x = *p;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&x);
 #pragma unroll
-      for (int kv = 0; kv < 2; ++kv) {
-        uint4* p = reinterpret_cast<uint4*>(&(kv ? S.vt : S.kt)[t * TS + v * 8]);
-        uint4 x = *p;
-        uint32_t* w = reinterpret_cast<uint32_t*>(&x);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xffff0000u);
-          const __half2 hh = __floats2half2_rn(lo, hi);
-          w[j] = *reinterpret_cast<const uint32_t*>(&hh);
-        }
-        *p = x;
+      for (int j = 0; j < 4; ++j) {
+        const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xffff0000u);
+        const __half2 hh = __floats2half2_rn(lo, hi);
+        w[j] = *reinterpret_cast<const uint32_t*>(&hh);
       }
+      *p = x;
     }
     __syncthreads();
   }
-
-  // ---- pass 1: quantisation parameters -------------------------------------
-  if (tid < 64) {
-    // keys: channels 2 tid, 2 tid + 1 over the G tokens
-    if (2 * tid < D) {
-      __half2 mn = __half2half2(__ushort_as_half(0x7c00u)), mx = __half2half2(__ushort_as_half(0xfc00u));
-#pragma unroll 8
-      for (int t = 0; t < G; ++t) {
-        const __half2 x = *reinterpret_cast<const __half2*>(&S.kt[t * TS + 2 * tid]);
-        mn = __hmin2(mn, x);
-        mx = __hmax2(mx, x);
-      }
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int c = 2 * tid + e;
-        float gmin, gmax;
-        scan_extremes(e ? __high2half(mn) : __low2half(mn), e ? __high2half(mx) : __low2half(mx),
-                      gmin, gmax, [&]() {
-                        for (int t = 0; t < G; ++t) {
-                          const float x = h2f(S.kt[t * TS + c]);
-                          if (x == 0.f) return x;
-                        }
-                        return 0.f;
-                      });
-        const QParams qp = quant_params(gmin, gmax, QMAX);
-        S.kp[c] = make_float2(qp.gmin, qp.scale);
-        S.kmeta[c] = (uint32_t)qp.hstep | ((uint32_t)qp.hzero << 16);
-      }
-    }
-  } else {
-    // values: per token, per group of VG_CH channels
-    for (int j = tid - 64; j < G * NVG; j += kFlushThreads - 64) {
-      const int t = j / NVG, vg = j - t * NVG;
-      const uint16_t* rowp = &S.vt[t * TS + vg * VG_CH];
-      __half2 mn = __half2half2(__ushort_as_half(0x7c00u)), mx = __half2half2(__ushort_as_half(0xfc00u));
-#pragma unroll
-      for (int c = 0; c < VG_CH; c += 8) {
-        const uint4 x = *reinterpret_cast<const uint4*>(rowp + c);
-        const __half2* hx = reinterpret_cast<const __half2*>(&x);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          mn = __hmin2(mn, hx[k]);
-          mx = __hmax2(mx, hx[k]);
-        }
-      }
-      float gmin, gmax;
-      scan_extremes(__hmin(__low2half(mn), __high2half(mn)), __hmax(__low2half(mx), __high2half(mx)),
-                    gmin, gmax, [&]() {
-                      for (int c = 0; c < VG_CH; ++c) {
-                        const float x = h2f(rowp[c]);
-                        if (x == 0.f) return x;
-                      }
-                      return 0.f;
-                    });
-      const QParams qp = quant_params(gmin, gmax, QMAX);
-      S.vp[j] = make_float2(qp.gmin, qp.scale);
-      S.vmeta[j] = (uint32_t)qp.hstep | ((uint32_t)qp.hzero << 16);
-    }
-  }
-  __syncthreads();
 
   auto code = [&](float x, float2 p) {
     int q = __float2int_rn(__fmul_rn(__fsub_rn(x, p.x), p.y));
@@ -268,32 +203,109 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
                ? nullptr
                : a.pool + ((int64_t)ph * a.n_kv_heads + h) * a.page_bytes;
   };
+  const __half2 pinf = __half2half2(__ushort_as_half(0x7c00u));
+  const __half2 ninf = __half2half2(__ushort_as_half(0xfc00u));
 
-  // ---- pass 2a: key codes, row-major [16 tokens][D * BITS / 8 bytes] --------
-  {
-    constexpr int CPW = 32 / BITS;     // channels per 32-bit word
-    constexpr int NWR = D / CPW;       // words per token row
+  if (!is_v) {
+    // ---- keys: extremes per channel over the G tokens, KSPLIT token ranges ----
+    {
+      const int cp = tid % (D / 2), ks = tid / (D / 2);
+      __half2 mn = pinf, mx = ninf;
+#pragma unroll 8
+      for (int t = ks * (G / KSPLIT); t < (ks + 1) * (G / KSPLIT); ++t) {
+        const __half2 x = *reinterpret_cast<const __half2*>(&tile[t * TS + 2 * cp]);
+        mn = __hmin2(mn, x);
+        mx = __hmax2(mx, x);
+      }
+      S.kmn[ks][cp] = mn;
+      S.kmx[ks][cp] = mx;
+    }
+    __syncthreads();
+    if (tid < D / 2) {
+      __half2 mn = S.kmn[0][tid], mx = S.kmx[0][tid];
+#pragma unroll
+      for (int ks = 1; ks < KSPLIT; ++ks) {
+        mn = __hmin2(mn, S.kmn[ks][tid]);
+        mx = __hmax2(mx, S.kmx[ks][tid]);
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int c = 2 * tid + e;
+        float gmin, gmax;
+        scan_extremes(e ? __high2half(mn) : __low2half(mn), e ? __high2half(mx) : __low2half(mx),
+                      gmin, gmax, [&]() {
+                        for (int t = 0; t < G; ++t) {
+                          const float x = h2f(tile[t * TS + c]);
+                          if (x == 0.f) return x;
+                        }
+                        return 0.f;
+                      });
+        const QParams qp = quant_params(gmin, gmax, QMAX);
+        S.par[c] = make_float2(qp.gmin, qp.scale);
+        S.meta[c] = (uint32_t)qp.hstep | ((uint32_t)qp.hzero << 16);
+      }
+    }
+    __syncthreads();
+    // ---- key codes, row-major [16 tokens][D * BITS / 8 bytes] ----------------
+    constexpr int CPW = 32 / BITS;  // channels per 32-bit word
+    constexpr int NWR = D / CPW;    // words per token row
     constexpr int TSTEP = kFlushThreads / NWR;
     const int w = tid % NWR;
     float2 p[CPW];
 #pragma unroll
-    for (int n = 0; n < CPW; ++n) p[n] = S.kp[w * CPW + n];
+    for (int n = 0; n < CPW; ++n) p[n] = S.par[w * CPW + n];
     for (int t = tid / NWR; t < G; t += TSTEP) {
       uint32_t word = 0;
 #pragma unroll
       for (int n8 = 0; n8 < CPW; n8 += 8) {
-        const uint4 x = *reinterpret_cast<const uint4*>(&S.kt[t * TS + w * CPW + n8]);
+        const uint4 x = *reinterpret_cast<const uint4*>(&tile[t * TS + w * CPW + n8]);
         const uint16_t* hx = reinterpret_cast<const uint16_t*>(&x);
 #pragma unroll
         for (int n = 0; n < 8; ++n) word |= code(h2f(hx[n]), p[n8 + n]) << (BITS * (n8 + n));
       }
       uint8_t* blk = page_base(t / kPage);
-      if (blk)
-        reinterpret_cast<uint32_t*>(blk + a.k_codes_off)[(t % kPage) * NWR + w] = word;
+      if (blk) reinterpret_cast<uint32_t*>(blk + a.k_codes_off)[(t % kPage) * NWR + w] = word;
     }
+    // key meta slices: page pi holds channels [pi * KMW, (pi + 1) * KMW)
+    constexpr int KMW = D * kPage / G;
+    for (int i = tid; i < (G / kPage) * KMW; i += kFlushThreads) {
+      const int pi = i / KMW, j = i - pi * KMW;
+      uint8_t* blk = page_base(pi);
+      if (blk) reinterpret_cast<uint32_t*>(blk + a.k_meta_off)[j] = S.meta[i];
+    }
+    return;
   }
 
-  // ---- pass 2b: value codes in mma A-fragment order --------------------------
+  // ---- values: extremes per token and value group ---------------------------
+  for (int j = tid; j < G * NVG; j += kFlushThreads) {
+    const int t = j / NVG, vg = j - t * NVG;
+    const uint16_t* rowp = &tile[t * TS + vg * VG_CH];
+    __half2 mn = pinf, mx = ninf;
+#pragma unroll
+    for (int c = 0; c < VG_CH; c += 8) {
+      const uint4 x = *reinterpret_cast<const uint4*>(rowp + c);
+      const __half2* hx = reinterpret_cast<const __half2*>(&x);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        mn = __hmin2(mn, hx[k]);
+        mx = __hmax2(mx, hx[k]);
+      }
+    }
+    float gmin, gmax;
+    scan_extremes(__hmin(__low2half(mn), __high2half(mn)), __hmax(__low2half(mx), __high2half(mx)),
+                  gmin, gmax, [&]() {
+                    for (int c = 0; c < VG_CH; ++c) {
+                      const float x = h2f(rowp[c]);
+                      if (x == 0.f) return x;
+                    }
+                    return 0.f;
+                  });
+    const QParams qp = quant_params(gmin, gmax, QMAX);
+    S.par[j] = make_float2(qp.gmin, qp.scale);
+    S.meta[j] = (uint32_t)qp.hstep | ((uint32_t)qp.hzero << 16);
+  }
+  __syncthreads();
+  // ---- value codes in mma A-fragment order ----------------------------------
   {
     constexpr int W = D * BITS / 64;  // words per lane
     constexpr int VW = W < 4 ? W : 4;
@@ -316,12 +328,12 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
               const int t = tb + 8 * th + 2 * tig + e;
               if (BITS == 4) {
                 const int c = 16 * wv + g + 8 * rh;
-                wd |= code(h2f(S.vt[t * TS + c]), S.vp[t * NVG + c / VG_CH]) << (4 * (k + 4 * e));
+                wd |= code(h2f(tile[t * TS + c]), S.par[t * NVG + c / VG_CH]) << (4 * (k + 4 * e));
               } else {
 #pragma unroll
                 for (int mbi = 0; mbi < 2; ++mbi) {
                   const int c = 16 * (2 * wv + mbi) + g + 8 * rh;
-                  wd |= code(h2f(S.vt[t * TS + c]), S.vp[t * NVG + c / VG_CH])
+                  wd |= code(h2f(tile[t * TS + c]), S.par[t * NVG + c / VG_CH])
                         << (2 * (4 * mbi + k + 8 * e));
                 }
               }
@@ -339,57 +351,92 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
       }
     }
   }
-
-  // ---- pass 2c: value meta [16 tokens][NVG] and key meta slices per page -----
-  {
-    constexpr int VMW = kPage * NVG;   // value meta words per page
-    constexpr int KMW = D * kPage / G; // key meta words per page (= k_meta_slice / 4)
-    for (int i = tid; i < (G / kPage) * (VMW + KMW); i += kFlushThreads) {
-      const int pi = i / (VMW + KMW), j = i - pi * (VMW + KMW);
-      uint8_t* blk = page_base(pi);
-      if (!blk) continue;
-      if (j < VMW)
-        reinterpret_cast<uint32_t*>(blk + a.v_meta_off)[j] = S.vmeta[pi * VMW + j];
-      else
-        reinterpret_cast<uint32_t*>(blk + a.k_meta_off)[j - VMW] = S.kmeta[pi * KMW + (j - VMW)];
-    }
+  // value meta [16 tokens][NVG] per page
+  constexpr int VMW = kPage * NVG;
+  for (int i = tid; i < (G / kPage) * VMW; i += kFlushThreads) {
+    const int pi = i / VMW, j = i - pi * VMW;
+    uint8_t* blk = page_base(pi);
+    if (blk) reinterpret_cast<uint32_t*>(blk + a.v_meta_off)[j] = S.meta[i];
   }
 }
 
 // New tokens that stay in fp16: t in [max(nq1, L), L + T) -> ring slot t % C.
-__global__ void __launch_bounds__(256) residual_write_kernel(AppendArgs a) {
-  const int b = blockIdx.z, h = blockIdx.y;
-  const int D = a.head_dim;
+// One CTA per (16-token ring chunk, kv head, sequence); chunk q of the
+// sequence covers tokens [16 q, 16 q + 16).  A chunk whose 16 tokens are all
+// written here is staged through shared memory and stored as whole 16-byte
+// fragment vectors; a partly written chunk (e.g. one decode token) is written
+// element by element so the slots of older tokens stay untouched.
+constexpr int kResThreads = 128;
+
+template <int D>
+__global__ void __launch_bounds__(kResThreads) residual_write_kernel(AppendArgs a) {
+  constexpr int TS = D + 8, VPR = D / 8;
+  __shared__ __align__(16) uint16_t st[2][kPage * TS];
+  const int b = blockIdx.z, h = blockIdx.y, tid = threadIdx.x;
   const int L = a.lens_old[b];
-  const int T = a.cu_new[b + 1] - a.cu_new[b];
-  if (!append_lengths_ok(a, L, a.cu_new[b], a.cu_new[b + 1])) return;
-  const int L2 = L + T;
+  const int c0 = a.cu_new[b], c1 = a.cu_new[b + 1];
+  if (!append_lengths_ok(a, L, c0, c1)) return;
+  const int L2 = L + (c1 - c0);
   const int nq1 = nq_of(L2, a.residual, a.group);
   const int start = nq1 > L ? nq1 : L;
-  const int i0 = blockIdx.x * kPage;  // new-token index range [i0, i0 + 16)
-  if (L + i0 + kPage <= start || i0 >= T) return;
+  const int q = start / kPage + blockIdx.x;
+  const int lo = max(q * kPage, start), hi = min(q * kPage + kPage, L2);
+  if (lo >= hi) return;
   const int row = a.seq_slots ? a.seq_slots[b] : b;
   if (row < 0 || row >= a.max_seqs) {
-    if (threadIdx.x == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
+    if (tid == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
     return;
   }
-  for (int i = threadIdx.x; i < kPage * D; i += blockDim.x) {
-    const int ti = i / D, c = i % D;
-    const int n = i0 + ti;
-    const int tok = L + n;
-    if (n >= T || tok < start) continue;
-    const int64_t e0 = (((int64_t)a.cu_new[b] + n) * a.n_kv_heads + h) * D + c;
-    uint16_t kh = static_cast<const uint16_t*>(a.k_new)[e0];
-    uint16_t vh = static_cast<const uint16_t*>(a.v_new)[e0];
-    if (a.in_bf16) {
-      __half k16 = __float2half_rn(__bfloat162float(*reinterpret_cast<__nv_bfloat16*>(&kh)));
-      __half v16 = __float2half_rn(__bfloat162float(*reinterpret_cast<__nv_bfloat16*>(&vh)));
-      kh = *reinterpret_cast<uint16_t*>(&k16);
-      vh = *reinterpret_cast<uint16_t*>(&v16);
+  auto in_elem = [&](const void* base, int tok, int c) -> const uint16_t* {
+    return static_cast<const uint16_t*>(base) + (((int64_t)c0 + (tok - L)) * a.n_kv_heads + h) * D + c;
+  };
+  auto to_f16 = [&](uint16_t x) -> uint16_t {
+    if (!a.in_bf16) return x;
+    const __half y = __float2half_rn(__uint_as_float((uint32_t)x << 16));
+    return __half_as_ushort(y);
+  };
+  uint16_t* kc = ring_chunk(a, row, h, q * kPage, 0);
+  uint16_t* vc = ring_chunk(a, row, h, q * kPage, 1);
+  if (hi - lo < kPage) {
+    for (int i = tid; i < (hi - lo) * D; i += kResThreads) {
+      const int tok = lo + i / D, c = i % D, t = tok % kPage;
+      kc[ring_k_off(c, t)] = to_f16(*in_elem(a.k_new, tok, c));
+      vc[ring_v_off(c, t)] = to_f16(*in_elem(a.v_new, tok, c));
     }
-    const int t = (tok % a.ring_cap) % kPage;
-    ring_chunk(a, row, h, tok, 0)[ring_k_off(c, t)] = kh;
-    ring_chunk(a, row, h, tok, 1)[ring_v_off(c, t)] = vh;
+    return;
+  }
+  // full chunk: stage the 16 input rows (16-byte aligned by the entry point)
+  for (int i = tid; i < 2 * kPage * VPR; i += kResThreads) {
+    const int kv = i / (kPage * VPR), r = i % (kPage * VPR), t = r / VPR, v = r % VPR;
+    uint4 x = *reinterpret_cast<const uint4*>(in_elem(kv ? a.v_new : a.k_new, lo + t, v * 8));
+    if (a.in_bf16) {
+      uint32_t* w = reinterpret_cast<uint32_t*>(&x);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __half2 hh = __floats2half2_rn(__uint_as_float(w[j] << 16),
+                                             __uint_as_float(w[j] & 0xffff0000u));
+        w[j] = *reinterpret_cast<const uint32_t*>(&hh);
+      }
+    }
+    *reinterpret_cast<uint4*>(&st[kv][t * TS + v * 8]) = x;
+  }
+  __syncthreads();
+  // vector v of a block = (bi = v / 32, lane l = 4 g + tig), halves 2 r + e:
+  //   K: (t = g + 8 (r & 1), c = 16 bi + 2 tig + 8 (r >> 1) + e)
+  //   V: (t = 8 (r >> 1) + 2 tig + e, c = 16 bi + g + 8 (r & 1))
+  for (int i = tid; i < 2 * kPage * VPR; i += kResThreads) {
+    const int kv = i / (kPage * VPR), v = i % (kPage * VPR);
+    const int bi = v >> 5, l = v & 31, g = l >> 2, tig = l & 3;
+    uint16_t x[8];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = kv ? 8 * (r >> 1) + 2 * tig + e : g + 8 * (r & 1);
+        const int c = 16 * bi + (kv ? g + 8 * (r & 1) : 2 * tig + 8 * (r >> 1) + e);
+        x[2 * r + e] = st[kv][t * TS + c];
+      }
+    reinterpret_cast<uint4*>(kv ? vc : kc)[v] = *reinterpret_cast<const uint4*>(x);
   }
 }
 
@@ -403,7 +450,7 @@ static int launch_flush_t(const AppendArgs& a, int num_seqs, cudaStream_t stream
       return TKV_BACKEND_ERROR;
     attr_set = true;
   }
-  dim3 grid(a.max_new / G + 1, a.n_kv_heads, num_seqs);
+  dim3 grid(2 * (a.max_new / G + 1), a.n_kv_heads, num_seqs);  // x: (group, K or V)
   flush_groups_kernel<D, BITS, G><<<grid, kFlushThreads, smem, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
 }
@@ -428,9 +475,16 @@ int launch_append(const AppendArgs& a, int num_seqs, cudaStream_t stream) {
     st = a.bits == 4 ? launch_flush_g<64, 4>(a, num_seqs, stream)
                      : launch_flush_g<64, 2>(a, num_seqs, stream);
   if (st != TKV_OK) return st;
-  dim3 g2((a.max_new + kPage - 1) / kPage, a.n_kv_heads, num_seqs);
-  if (g2.x > 0) {
-    residual_write_kernel<<<g2, 256, 0, stream>>>(a);
+  // written tokens [start, L2): at most min(max_new, R + G - 1) of them (the
+  // rest is quantised), from any offset, so they span at most that many
+  // + 14, / 16, + 1 ring chunks
+  const int span = min(a.max_new, a.residual + a.group - 1);
+  dim3 g2((span + 2 * kPage - 2) / kPage, a.n_kv_heads, num_seqs);
+  if (a.max_new > 0) {
+    if (a.head_dim == 128)
+      residual_write_kernel<128><<<g2, kResThreads, 0, stream>>>(a);
+    else
+      residual_write_kernel<64><<<g2, kResThreads, 0, stream>>>(a);
     if (cudaGetLastError() != cudaSuccess) return TKV_BACKEND_ERROR;
   }
   return TKV_OK;
