@@ -10,6 +10,10 @@ over a shared pool, KIVI INT4 with G=R=128, bf16 q, synthetic seeded data
 data path).  A step = one decode-attention call for all sequences of one
 layer.  metric = sequence-tokens/s (B / step time), whole job.
 
+--workload config3 measures the other half of the path, quantize-on-append
+64 sequences x 2048-token bf16 chunk per GPU appended to
+empty sequences, metric = appended tokens/s.
+
 --impl reference times the reference's CPU path for the same workload: the
 CPU restatement of the reference algorithm (oracle/, the reference has no CPU
 implementation of this path) on all host threads, over a bounded sample of the
@@ -33,6 +37,8 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "KIVI-INT4 paged decode-attn seq-tokens/s (HBM GB/s and % of peak in roofline)"
 UNIT = "seq-tokens/s"
+APPEND_METRIC = "KIVI-INT4 quantize-on-append appended tokens/s (config 3)"
+APPEND_UNIT = "tokens/s"
 
 
 def parse():
@@ -40,7 +46,8 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="config2", choices=["config2", "config4", "config5"])
+    ap.add_argument("--workload", default="config2",
+                    choices=["config2", "config3", "config4", "config5"])
     ap.add_argument("--impl", default="kivi", choices=["kivi", "reference"])
     ap.add_argument("--cpu-sample", type=int, default=8, help="sequences in the CPU sample")
     return ap.parse_args()
@@ -55,6 +62,8 @@ def peaks():
 
 
 def make_workload(wl, name: str, rank: int):
+    if name == "config3":
+        return wl.config3(seed=3000 + rank)
     if name == "config2":
         return wl.config2(seed=1000 + rank)
     if name == "config4":
@@ -385,8 +394,204 @@ def run_kivi(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# config 3: quantize-on-append
+# ---------------------------------------------------------------------------
+def append_inputs(wl, w, torch, dev):
+    """Seeded bf16 K/V [B*T, Hkv, D] (keys N(0,1) with outlier channels x8)."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(w.seed)
+    k = torch.randn((w.B * w.T, w.Hkv, w.D), generator=gen, device=dev, dtype=torch.float32)
+    v = torch.randn((w.B * w.T, w.Hkv, w.D), generator=gen, device=dev, dtype=torch.float32)
+    oc = torch.from_numpy(np.asarray(w.outlier_channels, np.int64)).to(dev)
+    k[:, :, oc] *= w.outlier_scale
+    return k.to(torch.bfloat16), v.to(torch.bfloat16)
+
+
+def cpu_append_time(O, wl, w, sample, reps=1):
+    """Oracle append of the first `sample` sequences' chunks (single thread)."""
+    rng = np.random.default_rng(w.seed)
+    T = sample * w.T
+    k = wl.f32_to_bf16_bits(rng.standard_normal((T, w.Hkv, w.D)).astype(np.float32))
+    v = wl.f32_to_bf16_bits(rng.standard_normal((T, w.Hkv, w.D)).astype(np.float32))
+    cu = (np.arange(sample + 1) * w.T).astype(np.int32)
+    bt = np.ascontiguousarray(w.block_tables[:sample])
+    best = None
+    for _ in range(reps):
+        st = O.PagedState(w.D, w.group, w.residual, w.bits, w.Hkv, w.num_pages, sample)
+        t0 = time.perf_counter()
+        st.append(k, v, True, cu, np.zeros(sample, np.int32), bt)
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+    return best
+
+
+def run_append_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+    O.build()
+    wl = importlib.import_module("truellm-engine_b200.workloads")
+    w = make_workload(wl, "config3", 0)
+    sample = max(1, min(args.cpu_sample // 2, w.B))
+    times = [cpu_append_time(O, wl, w, sample) for _ in range(max(1, min(args.steps, 3)))]
+    t = float(np.mean(times))
+    value = sample * w.T / t
+    line = {
+        "impl": "reference", "metric": APPEND_METRIC, "value": value, "unit": APPEND_UNIT,
+        "n_gpus": args.gpus, "steps": len(times), "warmup": 0, "ms_per_step": t * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8/f32",
+        "data": "synthetic",
+        "config": {"workload": f"config3: sample of {sample} sequences x {w.T} tokens"},
+        "cpu_baseline": {"value": value, "unit": APPEND_UNIT, "cores": 1, "kind": "port",
+                         "sample": f"{sample} of the {w.B} 2048-token chunks, CPU restatement "
+                                   "of the reference quantizer and page packing, one thread"},
+        "e2e": {"value": value, "unit": APPEND_UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def run_append(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    ops = importlib.import_module("truellm-engine_b200.ops")
+    wl = importlib.import_module("truellm-engine_b200.workloads")
+    w = make_workload(wl, "config3", rank)
+    fmt = ops.KiviFormat(w.D, w.group, w.residual, w.bits, w.Hkv)
+    cache = ops.KiviPagedCache(fmt, w.num_pages, w.B, dev)
+    bt = torch.from_numpy(w.block_tables).to(dev)
+    k, v = append_inputs(wl, w, torch, dev)
+    cu = (torch.arange(w.B + 1, dtype=torch.int32) * w.T).to(dev)
+    lens0 = torch.zeros(w.B, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(kk, vv):
+        # one call = flush kernel + residual-ring kernel (2 launches); the
+        # sequences start empty every call, so each call redoes the same work
+        ops.paged_append(cache, kk, vv, cu, lens0, bt, max_new_tokens=w.T, err=err,
+                         stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(3, args.warmup)):
+        step(k, v)
+    barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            step(k, v)
+            evs[i][1].record(stream)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    clocks = clk.summary()
+    if int(err.item()) != 0:
+        raise RuntimeError(f"device error flag {int(err.item()):#x}")
+    t_step = start.elapsed_time(stop) / 1e3 / args.steps
+    t_call = float(np.mean([a.elapsed_time(b) for a, b in evs])) / 1e3
+    times = torch.tensor([t_step, t_call], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    t_step, t_call = float(times[0]), float(times[1])
+
+    # ---- end to end: K/V from pinned host memory, error word read back ----
+    k_host = k.cpu().pin_memory()
+    v_host = v.cpu().pin_memory()
+    err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+    k_dev, v_dev = torch.empty_like(k), torch.empty_like(v)
+    n_e2e = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        k_dev.copy_(k_host, non_blocking=True)
+        v_dev.copy_(v_host, non_blocking=True)
+        step(k_dev, v_dev)
+        err_host.copy_(err, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n_e2e):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_e2e = torch.tensor([e0.elapsed_time(e1) / 1e3 / n_e2e], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_e2e, op=dist.ReduceOp.MAX)
+    t_e2e = float(t_e2e[0])
+
+    alg = wl.append_algorithmic_bytes(w)
+    peak, peak_kind = peaks()
+    achieved = alg / t_call / 1e9
+    tp = ROOT / "profiles" / "append_config3.json"
+    traffic = json.loads(tp.read_text()).get("dram_bytes_per_call") if tp.exists() else None
+    if rank == 0:
+        cpu = None
+        if world == 1:
+            try:
+                from oracle import oracle as O
+                O.build()
+                sample = max(1, min(args.cpu_sample // 2, w.B))
+                tc = cpu_append_time(O, wl, w, sample)
+                cpu = {"value": sample * w.T / tc, "unit": APPEND_UNIT, "cores": 1,
+                       "kind": "port",
+                       "sample": f"{sample} of the {w.B} 2048-token chunks, CPU restatement of "
+                                 "the reference quantizer and page packing, one thread"}
+            except Exception as e:  # the baseline is reported, never required
+                cpu = {"value": None, "unit": APPEND_UNIT, "cores": 1, "kind": "port",
+                       "sample": f"failed: {e!r}"[:200]}
+        line = {
+            "metric": APPEND_METRIC, "value": world * w.B * w.T / t_step, "unit": APPEND_UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
+            "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16->int4",
+            "data": "synthetic (seeded N(0,1) K/V, 3 key outlier channels x8)",
+            "config": {"workload": f"config3: B={w.B}/GPU x {w.T}-token bf16 chunk, Hkv={w.Hkv} "
+                                   f"D={w.D} G={w.group} R={w.residual} INT{w.bits}",
+                       "global_batch": world * w.B, "parallelism": f"sequence-sharded x{world}",
+                       "l2": "inputs larger than L2 (%.0f MB per call)" % (alg / 1e6)},
+            "gpu_launches": 2 * args.steps,
+            "e2e": {"value": world * w.B * w.T / t_e2e, "unit": APPEND_UNIT,
+                    "h2d_bytes_per_step": 2 * k.numel() * 2, "d2h_bytes_per_step": 4},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
+                         "kernel": "flush_groups_kernel<128,4,128> + residual_write_kernel<128>",
+                         "alg_bytes_per_launch": alg, "kernel_ms": t_call * 1e3},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "config3":
+        return run_append_reference(args) if args.impl == "reference" else run_append(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_kivi(args)

@@ -192,10 +192,10 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
     __syncthreads();
   }
 
+  // clamp(rint(y), 0, QMAX) of the reference: the unsigned round-to-nearest
+  // conversion saturates negatives (and NaN) to 0, the min caps the top
   auto code = [&](float x, float2 p) {
-    int q = __float2int_rn(__fmul_rn(__fsub_rn(x, p.x), p.y));
-    q = q < 0 ? 0 : q;
-    return static_cast<uint32_t>(q > QMAX ? QMAX : q);
+    return min(__float2uint_rn(__fmul_rn(__fsub_rn(x, p.x), p.y)), static_cast<uint32_t>(QMAX));
   };
   auto page_base = [&](int pi) -> uint8_t* {
     const int ph = S.phys[pi];
@@ -306,12 +306,24 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
   }
   __syncthreads();
   // ---- value codes in mma A-fragment order ----------------------------------
+  // Lane l = 4 g + tig of page pi packs, per word, tokens 2 tig + e + 8 th
+  // and channels g + 8 rh (+ 16 per m-block): offsets from the lane's base
+  // element are compile-time constants.
   {
     constexpr int W = D * BITS / 64;  // words per lane
     constexpr int VW = W < 4 ? W : 4;
     for (int pl = tid; pl < (G / kPage) * 32; pl += kFlushThreads) {
       const int pi = pl >> 5, l = pl & 31, g = l >> 2, tig = l & 3;
-      const int tb = pi * kPage;
+      const int tb = pi * kPage + 2 * tig;  // token of (th, e) = (0, 0)
+      const uint16_t* base = &tile[tb * TS + g];
+      // parameters of the lane's tokens (th, e), per value group
+      float2 pv[2][2][NVG];
+#pragma unroll
+      for (int th = 0; th < 2; ++th)
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+#pragma unroll
+          for (int vg = 0; vg < NVG; ++vg) pv[th][e][vg] = S.par[(tb + 8 * th + e) * NVG + vg];
       uint8_t* blk = page_base(pi);
 #pragma unroll
       for (int q = 0; q < W / VW; ++q) {
@@ -325,15 +337,15 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const int rh = k >> 1, th = k & 1;
-              const int t = tb + 8 * th + 2 * tig + e;
+              const int ro = (8 * th + e) * TS;  // row offset of token (th, e)
               if (BITS == 4) {
-                const int c = 16 * wv + g + 8 * rh;
-                wd |= code(h2f(tile[t * TS + c]), S.par[t * NVG + c / VG_CH]) << (4 * (k + 4 * e));
+                const int c = 16 * wv + 8 * rh;  // channel minus g (g < 8 stays in the group)
+                wd |= code(h2f(base[ro + c]), pv[th][e][c / VG_CH]) << (4 * (k + 4 * e));
               } else {
 #pragma unroll
                 for (int mbi = 0; mbi < 2; ++mbi) {
-                  const int c = 16 * (2 * wv + mbi) + g + 8 * rh;
-                  wd |= code(h2f(tile[t * TS + c]), S.par[t * NVG + c / VG_CH])
+                  const int c = 16 * (2 * wv + mbi) + 8 * rh;
+                  wd |= code(h2f(base[ro + c]), pv[th][e][c / VG_CH])
                         << (2 * (4 * mbi + k + 8 * e));
                 }
               }

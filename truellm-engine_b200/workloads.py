@@ -136,6 +136,48 @@ def config5(seed: int = 5, B: int = 256, bits: int = 4) -> DecodeWorkload:
                           "bf16", "bf16", seed, oc, 8.0)
 
 
+@dataclass
+class AppendWorkload:
+    """A batch of prompt chunks appended to empty sequences."""
+    name: str
+    B: int
+    T: int            # tokens appended per sequence
+    Hkv: int
+    D: int
+    group: int
+    residual: int
+    bits: int
+    block_tables: np.ndarray  # [B, T / 16] int32
+    num_pages: int
+    outlier_channels: np.ndarray
+    outlier_scale: float
+    seed: int
+
+
+def config3(seed: int = 3, B: int = 64, T: int = 2048) -> AppendWorkload:
+    """64 sequences x 2048-token bf16 chunk, Hkv=8, D=128, G=R=128 INT4: per
+    sequence-head 1920 quantised + 128 residual tokens; pages drawn from a
+    shared pool (+10% slack) in random order."""
+    rng = np.random.default_rng(seed)
+    lengths = np.full(B, T, np.int32)
+    num_pages = int(B * (T // PAGE) * 1.1) + 1
+    bt = random_block_tables(lengths, num_pages, rng)
+    outl = np.sort(rng.choice(128, size=3, replace=False))
+    return AppendWorkload("config3", B, T, 8, 128, 128, 128, 4, bt, num_pages, outl, 8.0, seed)
+
+
+def append_algorithmic_bytes(w: AppendWorkload) -> int:
+    """HBM bytes one append call must move: the K/V input (2 B per element),
+    the packed pages of the quantised tokens (codes, value meta, key meta) and
+    the fp16 residual tokens written to the ring."""
+    D, G, R, b, H, T = w.D, w.group, w.residual, w.bits, w.Hkv, w.T
+    nvg = -(-D // G)
+    nq = G * ((T - R) // G) if T > R else 0
+    nr = T - nq
+    per_head = 2 * T * D * 2 + nq * (2 * D * b // 8 + 4 * nvg) + (nq // G) * 4 * D + nr * 4 * D
+    return w.B * H * per_head
+
+
 def decode_algorithmic_bytes(w: DecodeWorkload) -> int:
     """HBM bytes one decode step must move (per-unit figures in DESIGN.md):
     per quantised token-head  2*D*b/8 codes + 4*ceil(D/G) value meta + 4*D/G key
