@@ -47,7 +47,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="config2",
-                    choices=["config2", "config3", "config4", "config5"])
+                    choices=["config2", "config3", "config4", "config4b", "config5"])
     ap.add_argument("--impl", default="kivi", choices=["kivi", "reference"])
     ap.add_argument("--cpu-sample", type=int, default=8, help="sequences in the CPU sample")
     return ap.parse_args()
@@ -66,8 +66,8 @@ def make_workload(wl, name: str, rank: int):
         return wl.config3(seed=3000 + rank)
     if name == "config2":
         return wl.config2(seed=1000 + rank)
-    if name == "config4":
-        return wl.config4(seed=4000 + rank)
+    if name in ("config4", "config4b"):
+        return wl.config4(seed=4000 + rank, B=1 if name == "config4b" else 8)
     return wl.config5(seed=5000 + rank)
 
 
@@ -157,9 +157,9 @@ class ClockSampler:
 
 
 def ncu_traffic(workload: str):
-    """Per-launch DRAM traffic of the split kernel from the committed ncu
-    summary (profiles/decode_split_<workload>.json), or None."""
-    p = ROOT / "profiles" / f"decode_split_{workload}.json"
+    """Per-launch DRAM traffic of the decode kernel from the committed ncu
+    summary (profiles/decode_warp_<workload>.json), or None."""
+    p = ROOT / "profiles" / f"decode_warp_{workload}.json"
     if not p.exists():
         return None
     d = json.loads(p.read_text())
@@ -169,6 +169,16 @@ def ncu_traffic(workload: str):
 # ---------------------------------------------------------------------------
 # CPU timing of the reference algorithm (oracle restatement)
 # ---------------------------------------------------------------------------
+def cpu_sample_size(lengths, cap: int, token_budget: int = 40000) -> int:
+    """Leading sequences of the CPU sample: at most `cap`, at most about
+    `token_budget` context tokens (long-context workloads), at least one."""
+    n, tok = 0, 0
+    for L in lengths[:cap]:
+        if n and tok + int(L) > token_budget:
+            break
+        n, tok = n + 1, tok + int(L)
+    return max(1, n)
+
 def cpu_reference_time(O, w, pool_np, ring_np, q_f32, sample, n_threads, repeats=1):
     st = O.PagedState(w.D, w.group, w.residual, w.bits, w.Hkv, w.num_pages, w.B)
     st.pool = pool_np
@@ -207,7 +217,7 @@ def run_reference(args):
     O.build()
     wl = importlib.import_module("truellm-engine_b200.workloads")
     w = make_workload(wl, args.workload, 0)
-    sample = min(args.cpu_sample, w.B)
+    sample = cpu_sample_size(w.lengths, args.cpu_sample)
     st = host_cache_for_reference(O, wl, w, sample)
     rng = np.random.default_rng(w.seed + 1)
     q = wl.bits_to_f32(wl.f32_to_bf16_bits(rng.standard_normal((w.B, w.Hq, w.D))), "bf16")
@@ -243,6 +253,64 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+class DecodePart:
+    """One decode call of a rank's step: a cache, its q/out and tables."""
+
+    def __init__(self, ops, wl, torch, w, dev, label):
+        self.w, self.label = w, label
+        self.cache, self.bt = build_gpu_cache(ops, w, dev, torch)
+        self.lens = torch.from_numpy(w.lengths).to(dev)
+        rng = np.random.default_rng(w.seed + 1)
+        self.q_np = wl.f32_to_bf16_bits(rng.standard_normal((w.B, w.Hq, w.D)))
+        self.q = torch.from_numpy(self.q_np.view(np.int16)).view(torch.bfloat16).to(dev)
+        self.out = torch.empty_like(self.q)
+        self.max_ctx = int(w.lengths.max())
+        self.scale = 1.0 / math.sqrt(w.D)
+        # workspace: split partials + counters, zeroed once (calls leave counters zero)
+        self.ws = torch.zeros(ops.decode_workspace_bytes(w.B, w.Hq, w.D, self.max_ctx),
+                              dtype=torch.uint8, device=dev)
+        self.q_host = torch.from_numpy(self.q_np.view(np.int16)).view(torch.bfloat16).pin_memory()
+        self.lens_host = torch.from_numpy(w.lengths.copy()).pin_memory()
+        self.out_host = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+        self.q_dev = torch.empty_like(self.q)
+        self.lens_dev = torch.empty_like(self.lens)
+
+
+def decode_plan(args, wl, ops, torch, dev, rank, world):
+    """The rank's share of the workload: (parts, total sequences, scaling,
+    layout, algorithmic bytes per step on this rank, token-split decoder)."""
+    SH = importlib.import_module("truellm-engine_b200.sharding")
+    name = args.workload
+    if name == "config2":  # every rank decodes its own 64 sequences
+        w = make_workload(wl, name, rank)
+        return ([DecodePart(ops, wl, torch, w, dev, "all")], world * w.B, "weak",
+                f"sequence-sharded x{world}", wl.decode_algorithmic_bytes(w), None, w)
+    if name == "config4":  # run A: kv heads split over the ranks, same 8 sequences
+        w = make_workload(wl, name, 0)
+        kvh, qh = SH.head_shard(w.Hkv, w.Hq, world, rank)
+        sub = wl.subset(w, Hkv=len(kvh), Hq=len(qh))
+        return ([DecodePart(ops, wl, torch, sub, dev, f"kv heads {kvh.start}-{kvh.stop - 1}")],
+                w.B, "strong", f"kv-head-sharded x{world}", wl.decode_algorithmic_bytes(sub),
+                None, w)
+    if name == "config4b":  # run B: one sequence split by tokens over the ranks
+        w = wl.config4(seed=4000, B=1)
+        part = DecodePart(ops, wl, torch, w, dev, "one sequence")
+        dec = SH.TokenSplitDecoder(1, w.Hq, w.D, part.max_ctx, w.residual, w.group, dev)
+        alg = wl.token_split_bytes(w, dec.lo, dec.hi, dec.last)
+        return ([part], 1, "strong", f"token-split x{world} (all-gather of partials + merge)",
+                alg, dec, w)
+    # config5: 256 sequences balanced by tokens; sequences 0-127 INT4, 128-255 INT2
+    w = make_workload(wl, "config5", 0)
+    mine = SH.balance_sequences(w.lengths, world)[rank]
+    parts, alg = [], 0
+    for bits, sel in ((4, mine[mine < w.B // 2]), (2, mine[mine >= w.B // 2])):
+        if len(sel):
+            sub = wl.subset(w, sel, bits=bits)
+            parts.append(DecodePart(ops, wl, torch, sub, dev, f"INT{bits} x{len(sel)}"))
+            alg += wl.decode_algorithmic_bytes(sub)
+    return parts, w.B, "strong", f"token-balanced sequences x{world}", alg, None, w
+
+
 def run_kivi(args):
     import torch
     import torch.distributed as dist
@@ -252,33 +320,34 @@ def run_kivi(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
+    if world > 1 or args.workload == "config4b":
         import datetime
+        if "MASTER_ADDR" not in os.environ:  # single process: a group of one
+            os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(29500 + os.getpid() % 1000),
+                              RANK="0", WORLD_SIZE="1")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
     ops = importlib.import_module("truellm-engine_b200.ops")
     wl = importlib.import_module("truellm-engine_b200.workloads")
-    w = make_workload(wl, args.workload, rank)
-    cache, bt = build_gpu_cache(ops, w, dev, torch)
-    lens = torch.from_numpy(w.lengths).to(dev)
-    rng = np.random.default_rng(w.seed + 1)
-    q_np = wl.f32_to_bf16_bits(rng.standard_normal((w.B, w.Hq, w.D)))
-    q = torch.from_numpy(q_np.view(np.int16)).view(torch.bfloat16).to(dev)
-    out = torch.empty_like(q)
-    max_ctx = int(w.lengths.max())
-    scale = 1.0 / math.sqrt(w.D)
+    parts, total_seqs, scaling, layout, alg_bytes, dec, w = decode_plan(
+        args, wl, ops, torch, dev, rank, world)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
-    # workspace: split partials + counters, zeroed once (calls leave counters zero)
-    ws = torch.zeros(ops.decode_workspace_bytes(w.B, w.Hq, w.D, max_ctx), dtype=torch.uint8,
-                     device=dev)
     stream = torch.cuda.current_stream()
 
+    def decode(p, q, lens):
+        if dec is not None:
+            dec(p.cache, q, p.bt, lens, p.out, scale=p.scale, err=err, stream=stream)
+        else:
+            ops.paged_decode(p.cache, q, p.bt, lens, p.max_ctx, scale=p.scale, out=p.out,
+                             workspace=p.ws, err=err, stream=stream)
+
     def step(ev=None):
-        # one decode step = one launch of the split kernel (merge fused in)
+        # one decode step: one decode launch per part (split + fused merge); the
+        # token-split layout adds the all-gather of partials and the merge
         if ev is not None:
             ev[0].record(stream)
-        ops.paged_decode(cache, q, bt, lens, max_ctx, scale=scale, out=out, workspace=ws,
-                         err=err, stream=stream)
+        for p in parts:
+            decode(p, p.q, p.lens)
         if ev is not None:
             ev[1].record(stream)
 
@@ -311,18 +380,12 @@ def run_kivi(args):
     t_step, t_split = float(times[0]), float(times[1])
 
     # ---- end to end through the public API with host buffers ----
-    q_host = torch.from_numpy(q_np.view(np.int16)).view(torch.bfloat16).pin_memory()
-    lens_host = torch.from_numpy(w.lengths.copy()).pin_memory()
-    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    q_dev = torch.empty_like(q)
-    lens_dev = torch.empty_like(lens)
-
     def e2e_step():
-        q_dev.copy_(q_host, non_blocking=True)
-        lens_dev.copy_(lens_host, non_blocking=True)
-        ops.paged_decode(cache, q_dev, bt, lens_dev, max_ctx, scale=scale, out=out,
-                         workspace=ws, err=err, stream=stream)
-        out_host.copy_(out, non_blocking=True)
+        for p in parts:
+            p.q_dev.copy_(p.q_host, non_blocking=True)
+            p.lens_dev.copy_(p.lens_host, non_blocking=True)
+            decode(p, p.q_dev, p.lens_dev)
+            p.out_host.copy_(p.out, non_blocking=True)
 
     for _ in range(args.warmup):
         e2e_step()
@@ -338,13 +401,13 @@ def run_kivi(args):
     if world > 1:
         dist.all_reduce(t_e2e, op=dist.ReduceOp.MAX)
     t_e2e = float(t_e2e[0])
-    h2d = q_host.numel() * 2 + lens_host.numel() * 4
-    d2h = out_host.numel() * 2
+    h2d = sum(p.q_host.numel() * 2 + p.lens_host.numel() * 4 for p in parts)
+    d2h = sum(p.out_host.numel() * 2 for p in parts)
 
-    alg_bytes = wl.decode_algorithmic_bytes(w)  # per launch of the split kernel (+ q/out)
     peak, peak_kind = peaks()
     achieved = alg_bytes / t_split / 1e9
-    traffic = ncu_traffic(args.workload)
+    traffic = ncu_traffic(args.workload) if world == 1 else None
+    n_launch = len(parts) * (2 if dec is not None else 1)
 
     line = None
     if rank == 0:
@@ -353,42 +416,50 @@ def run_kivi(args):
             try:
                 from oracle import oracle as O
                 O.build()
-                sample = min(args.cpu_sample, w.B)
-                pool_np = cache.pool.cpu().numpy()
-                ring_np = cache.ring.cpu().numpy().view(np.uint16)
-                qf = q.float().cpu().numpy()
+                p0 = parts[0]
+                sample = cpu_sample_size(p0.w.lengths, args.cpu_sample)
+                pool_np = p0.cache.pool.cpu().numpy()
+                ring_np = p0.cache.ring.cpu().numpy().view(np.uint16)
+                qf = p0.q.float().cpu().numpy()
                 threads = os.cpu_count() or 1
-                tc = cpu_reference_time(O, w, pool_np, ring_np, qf, sample, threads)
+                tc = cpu_reference_time(O, p0.w, pool_np, ring_np, qf, sample, threads)
                 cpu = {"value": sample / tc, "unit": UNIT, "cores": threads, "kind": "port",
-                       "sample": f"{sample} of the {w.B} sequences (mean context "
-                                 f"{w.lengths[:sample].mean():.0f}), CPU restatement of the "
+                       "sample": f"{sample} of the {p0.w.B} sequences (mean context "
+                                 f"{p0.w.lengths[:sample].mean():.0f}), CPU restatement of the "
                                  "reference algorithm (fp64), all host threads"}
             except Exception as e:  # the baseline is reported, never required
                 cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                        "sample": f"failed: {e!r}"[:200]}
+        desc = {"config2": f"config2: B={w.B}/GPU Hq={w.Hq} Hkv={w.Hkv} D={w.D} L~U[1024,8192]",
+                "config4": f"config4 run A: B={w.B} Hq={w.Hq} Hkv={w.Hkv} D={w.D} L=131072",
+                "config4b": f"config4 run B: B=1 Hq={w.Hq} Hkv={w.Hkv} D={w.D} L=131072",
+                "config5": f"config5: B={w.B} Hq={w.Hq} Hkv={w.Hkv} D={w.D} L~logU[128,32768] "
+                           "INT4 x128 + INT2 x128"}[args.workload]
         line = {
-            "metric": METRIC, "value": world * w.B / t_step, "unit": UNIT, "n_gpus": world,
+            "metric": METRIC, "value": total_seqs / t_step, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4/bf16",
-            "data": "synthetic (seeded N(0,1) K/V, 2% key outlier channels x8)",
-            "config": {"workload": f"{args.workload}: B={w.B}/GPU Hq={w.Hq} Hkv={w.Hkv} D={w.D} "
-                                   f"L~U[1024,8192] G={w.group} R={w.residual} INT{w.bits}",
-                       "global_batch": world * w.B, "mean_context": float(w.lengths.mean()),
-                       "parallelism": f"sequence-sharded x{world}",
-                       "l2": "inputs larger than L2 (cache %.0f MB)" % (alg_bytes / 1e6)},
-            "gpu_launches": args.steps,
-            "e2e": {"value": world * w.B / t_e2e, "unit": UNIT, "h2d_bytes_per_step": h2d,
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+            "dtype": "int4/bf16" if args.workload != "config5" else "int4+int2/bf16",
+            "data": "synthetic (seeded N(0,1) K/V, key outlier channels x8)",
+            "config": {"workload": f"{desc} G={w.group} R={w.residual}",
+                       "global_batch": total_seqs, "mean_context": float(w.lengths.mean()),
+                       "parallelism": layout, "rank0_parts": [p.label for p in parts],
+                       "l2": "inputs larger than L2 (cache %.0f MB per rank)" % (alg_bytes / 1e6)},
+            "gpu_launches": n_launch * args.steps,
+            "e2e": {"value": total_seqs / t_e2e, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": traffic, "kernel": "decode_warp_kernel<128,4,128> (split + fused merge)",
+                         "traffic": traffic,
+                         "kernel": "decode_warp_kernel<128,%d,128> (split + fused merge)%s" % (
+                             w.bits, " + all-gather + merge_kernel" if dec is not None else ""),
                          "alg_bytes_per_launch": alg_bytes,
                          "kernel_ms": t_split * 1e3},
             "cpu_baseline": cpu,
             "clocks": clocks,
         }
         print(json.dumps(line))
-    if world > 1:
+    if world > 1 or dist.is_initialized():
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -245,6 +245,28 @@ TKV_API int tkv_paged_decode_partials(const tkv_cache_t* cache, const void* q, i
                               int include_residual, float* part_ml, float* part_o, void* work,
                               int* err_flag, void* stream);
 
+/* One GPU's share of a decode whose quantised splits are spread over GPUs
+ * (one long sequence split by tokens): the quantised splits [split_lo,
+ * split_hi) of every sequence, plus the residual split when include_residual
+ * != 0, reduced on the GPU (a second, slot-parallel kernel) to ONE
+ * unnormalised partial per (sequence, q head):
+ *   out_ml [num_seqs][num_q_heads][2] f32  (m in log2 units, l)
+ *   out_o  [num_seqs][num_q_heads][D] f32
+ * i.e. one slot of the tkv_paged_decode_partials layout, so the slots of all
+ * GPUs, gathered in any order, go to tkv_merge_partials.  A (sequence, q head)
+ * with no token in the range gets m = -inf, l = 0, o = 0.  No counterpart in
+ * the reference (paged_attention_v2.cu keeps every partition on one GPU).
+ * workspace: at least tkv_decode_workspace_bytes(num_seqs, num_q_heads, D,
+ * split_hi * TKV_SPLIT_TOKENS), 16-byte aligned, zeroed once as for
+ * tkv_paged_decode (every call leaves its counters zero).  Two launches. */
+TKV_API int tkv_paged_decode_range(const tkv_cache_t* cache, const void* q, int q_dtype,
+                                   const int32_t* block_tables, int max_blocks_per_seq,
+                                   const int32_t* seq_lens, const int32_t* seq_slots,
+                                   int num_seqs, int num_q_heads, float scale, int split_lo,
+                                   int split_hi, int include_residual, float* out_ml,
+                                   float* out_o, void* workspace, size_t workspace_bytes,
+                                   int* err_flag, void* stream);
+
 /* Log-sum-exp merge of n_slots partial sets laid out as above
  * (paged_attention_v2.cu:132-170) into out [num_seqs, num_q_heads, D]. */
 TKV_API int tkv_merge_partials(const float* part_ml, const float* part_o, int n_slots, int num_seqs,

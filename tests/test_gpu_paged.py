@@ -169,6 +169,42 @@ def test_long_context_split_partials_merge(ops, O, wl, cuda):
     check_close(full.cpu().numpy(), ref)
 
 
+def test_range_decode_reduces_to_one_slot_per_rank(ops, O, wl, cuda):
+    """Token split over three emulated ranks: each range is computed and
+    reduced in one launch to one partial per (sequence, q head)
+    (tkv_paged_decode_range); the three one-slot partials merged with
+    tkv_merge_partials equal the single-call decode.  The 1-token sequence has
+    no quantised split, so its first two ranges are empty (m = -inf)."""
+    lengths = [4 * 512 * 2 + 300, 1, 900]
+    tw, bt, lengths, rng = _build(ops, O, wl, cuda, 128, 128, 128, 4, 8, lengths, "bf16",
+                                  seed=23)
+    B, Hq, D = len(lengths), 64, 128
+    q = bits_to_torch(wl.f32_to_bf16_bits(rng.standard_normal((B, Hq, D))), "bf16", cuda)
+    scale = 1 / math.sqrt(D)
+    bt_d, lens_d = i32(bt, cuda), i32(lengths, cuda)
+    max_ctx = int(lengths.max())
+    full = ops.paged_decode(tw.gpu, q, bt_d, lens_d, max_ctx, scale=scale,
+                            out_dtype=torch.float32)
+    n_split = (tw.fmt.quantized_len(max_ctx) + 511) // 512
+    cuts = [0, 3, 5, n_split]
+    ml = torch.empty((3, B, Hq, 2), dtype=torch.float32, device=cuda)
+    o = torch.empty((3, B, Hq, D), dtype=torch.float32, device=cuda)
+    wss = [torch.zeros(ops.decode_workspace_bytes(B, Hq, D, b * 512), dtype=torch.uint8,
+                       device=cuda) for b in cuts[1:]]
+    for _ in range(2):  # the second call reuses the workspaces (counters reset)
+        for r, (a, b) in enumerate(zip(cuts[:-1], cuts[1:])):
+            ops.paged_decode_range(tw.gpu, q, bt_d, lens_d, a, b, r == 2, ml[r], o[r], wss[r],
+                                   scale=scale, err=tw.err)
+        merged = ops.merge_partials(ml, o, torch.empty((B, Hq, D), dtype=torch.float32,
+                                                       device=cuda))
+        torch.cuda.synchronize()
+        assert int(tw.err.item()) == 0
+        assert torch.isinf(ml[0, 1, :, 0]).all() and torch.isinf(ml[1, 1, :, 0]).all()
+        assert torch.allclose(merged, full, atol=1e-5, rtol=1e-5)
+    check_close(merged.cpu().numpy(), tw.cpu.decode(q.float().cpu().numpy(), bt, lengths, scale,
+                                                    n_threads=8))
+
+
 def test_fused_merge_equals_split_kernel_plus_merge_kernel(ops, O, wl, cuda):
     """tkv_paged_decode merges the split partials inside its one launch (the
     warp that finishes a (sequence, kv head) pair's last split).  Its output

@@ -80,6 +80,9 @@ SIGNATURES = {
     "tkv_paged_decode_partials": (_i32, [C.POINTER(TkvCache), _vp, _i32, _vp, _i32, _vp, _vp,
                                          _i32, _i32, _f32, _i32, _i32, _i32, _vp, _vp, _vp,
                                          _vp, _vp]),
+    "tkv_paged_decode_range": (_i32, [C.POINTER(TkvCache), _vp, _i32, _vp, _i32, _vp, _vp,
+                                      _i32, _i32, _f32, _i32, _i32, _i32, _vp, _vp, _vp, _sz,
+                                      _vp, _vp]),
     "tkv_merge_partials": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _i32, _vp]),
     "truellm_kernel_init": (C.POINTER(TruellmKernelManifest), []),
     "tkv_cache_kernel_manifest": (C.POINTER(TruellmKernelManifest), []),

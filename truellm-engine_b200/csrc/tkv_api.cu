@@ -315,6 +315,36 @@ int tkv_paged_decode_partials(const tkv_cache_t* cache, const void* q, int q_dty
                               err_flag, as_stream(stream));
 }
 
+int tkv_paged_decode_range(const tkv_cache_t* cache, const void* q, int q_dtype,
+                           const int32_t* block_tables, int max_blocks_per_seq,
+                           const int32_t* seq_lens, const int32_t* seq_slots, int num_seqs,
+                           int num_q_heads, float scale, int split_lo, int split_hi,
+                           int include_residual, float* out_ml, float* out_o, void* workspace,
+                           size_t workspace_bytes, int* err_flag, void* stream) {
+  if (!cache_ok(cache) || !out_ml || !out_o || !workspace || !aligned16(workspace))
+    return TKV_INVALID_ARGUMENT;
+  if (num_seqs <= 0 || num_q_heads <= 0 || split_lo < 0 || split_hi < split_lo)
+    return TKV_INVALID_ARGUMENT;
+  const int D = cache->fmt.head_dim;
+  const int slots = (split_hi - split_lo) + (include_residual ? 1 : 0);
+  const size_t n = (size_t)slots * num_seqs * num_q_heads;
+  const size_t need = kWorkBytes + pair_counter_bytes(num_seqs, num_q_heads) +
+                      n * 2 * sizeof(float) + n * (size_t)D * sizeof(float);
+  if (workspace_bytes < need) return TKV_INVALID_ARGUMENT;
+  if (slots == 0) return TKV_INVALID_ARGUMENT;  // nothing would write out_ml / out_o
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* part_ml =
+      reinterpret_cast<float*>(ws + kWorkBytes + pair_counter_bytes(num_seqs, num_q_heads));
+  float* part_o = part_ml + 2 * n;
+  const cudaStream_t s = as_stream(stream);
+  const int st = decode_partials_impl(cache, q, q_dtype, block_tables, max_blocks_per_seq,
+                                      seq_lens, seq_slots, num_seqs, num_q_heads, scale, split_lo,
+                                      split_hi, include_residual, part_ml, part_o, ws, nullptr,
+                                      nullptr, 0, err_flag, s);
+  if (st != TKV_OK) return st;
+  return launch_reduce(part_ml, part_o, slots, num_seqs, num_q_heads, D, out_ml, out_o, s);
+}
+
 int tkv_merge_partials(const float* part_ml, const float* part_o, int n_slots, int num_seqs,
                        int num_q_heads, int head_dim, void* out, int out_dtype, void* stream) {
   if (!part_ml || !part_o || !out || n_slots <= 0 || num_seqs <= 0 || num_seqs > 65535 ||

@@ -262,6 +262,8 @@ int launch_ref_kivi(int mode, const void* in, void* out, int n_vecs, int head_di
                     int group_size, cudaStream_t stream);
 int launch_append(const AppendArgs& a, int num_seqs, cudaStream_t stream);
 int launch_decode_splits(DecodeArgs a, int head_dim, int bits, int n_vgroups, cudaStream_t stream);
+int launch_reduce(const float* part_ml, const float* part_o, int n_slots, int num_seqs,
+                  int num_q_heads, int head_dim, float* out_ml, float* out_o, cudaStream_t stream);
 int launch_merge(const float* part_ml, const float* part_o, int n_slots, int num_seqs,
                  int num_q_heads, int head_dim, void* out, int out_dtype, cudaStream_t stream);
 

@@ -345,11 +345,13 @@ __device__ __forceinline__ void write_partial(const DecodeArgs& a, WarpState<D, 
 // latency is exposed.  Partials are read with ld.global.cg: other CTAs of the
 // same launch may have written them.
 // ---------------------------------------------------------------------------
-template <int H>
+// Output rows are oi0 + j (j < nh).  RED: write the combined unnormalised
+// partial, (M, L) to red_ml and O to out (f32), instead of O / L.
+template <int H, bool RED = false>
 __device__ __forceinline__ void merge_heads(const float* part_ml, const float* part_o,
                                             int n_slots, int nv, int cnt, int64_t stride,
                                             int64_t i0, int nh, int D, void* out, int out_dtype,
-                                            int lane) {
+                                            int lane, int64_t oi0, float* red_ml = nullptr) {
   constexpr int CPL = 4, UB = 16 / H;
   static_assert(H == 1 || H == 2 || H == 4, "heads per merge pass");
   for (int j0 = 0; j0 < nh; j0 += H) {
@@ -433,13 +435,25 @@ __device__ __forceinline__ void merge_heads(const float* part_ml, const float* p
 #pragma unroll
       for (int q = 0; q < H; ++q) {
         if (j0 + q >= nh) continue;
+        if (RED) {
+          if (cb == 0 && lane == 0) {
+            red_ml[(oi0 + j0 + q) * 2 + 0] = M[q];
+            red_ml[(oi0 + j0 + q) * 2 + 1] = L[q];
+          }
+#pragma unroll
+          for (int k = 0; k < CPL; ++k) {
+            const int c = cb + lane + 32 * k;
+            if (c < D) static_cast<float*>(out)[(oi0 + j0 + q) * D + c] = O[q][k];
+          }
+          continue;
+        }
         const float inv = L[q] > 0.f ? 1.f / L[q] : 0.f;
 #pragma unroll
         for (int k = 0; k < CPL; ++k) {
           const int c = cb + lane + 32 * k;
           if (c >= D) continue;
           const float v = O[q][k] * inv;
-          const int64_t oi = (i0 + j0 + q) * D + c;
+          const int64_t oi = (oi0 + j0 + q) * D + c;
           if (out_dtype == TKV_F32)
             static_cast<float*>(out)[oi] = v;
           else if (out_dtype == TKV_BF16)
@@ -502,9 +516,10 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
     if (old != static_cast<unsigned int>(nv)) return;
     __threadfence();  // every other warp's partial of this pair is visible now
     if (lane == 0) a.bh_count[b * a.n_kv_heads + h] = 0u;
+    const int64_t i0 = (int64_t)b * a.num_q_heads + h * a.grp;
     merge_heads<4>(a.part_ml, a.part_o, a.n_slots, nv, nv + 1,
-                   (int64_t)a.num_seqs * a.num_q_heads, (int64_t)b * a.num_q_heads + h * a.grp,
-                   a.grp, D, a.out, a.out_dtype, lane);
+                   (int64_t)a.num_seqs * a.num_q_heads, i0, a.grp, D, a.out, a.out_dtype, lane,
+                   i0);
   };
 
   for (;;) {
@@ -549,6 +564,7 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
       }
     }
     if (n_units <= 0) {
+      // the fused merge reads only written slots, the standalone merge every slot
       if (lane < a.grp && (real || !a.fuse_merge)) {
         a.part_ml[(ml_base + lane) * 2 + 0] = -INFINITY;
         a.part_ml[(ml_base + lane) * 2 + 1] = 0.f;
@@ -806,9 +822,53 @@ __global__ void __launch_bounds__(32) merge_kernel(const float* __restrict__ par
                                                    const float* __restrict__ part_o, int n_slots,
                                                    int num_seqs, int num_q_heads, int D,
                                                    void* __restrict__ out, int out_dtype) {
-  merge_heads<1>(part_ml, part_o, n_slots, n_slots, n_slots, (int64_t)num_seqs * num_q_heads,
-                 (int64_t)blockIdx.y * num_q_heads + blockIdx.x, 1, D, out, out_dtype,
-                 threadIdx.x);
+  const int64_t i0 = (int64_t)blockIdx.y * num_q_heads + blockIdx.x;
+  merge_heads<1>(part_ml, part_o, n_slots, n_slots, n_slots, (int64_t)num_seqs * num_q_heads, i0,
+                 1, D, out, out_dtype, threadIdx.x, i0);
+}
+
+// Reduction of n_slots partials to one unnormalised partial per (sequence,
+// q head): one CTA of kReduceWarps warps per (q head, sequence), warp w takes
+// a contiguous block of slots (merge_heads with RED), then the warps' partials
+// are combined with the same log-sum-exp rule in shared memory.
+constexpr int kReduceWarps = 8;
+
+__global__ void __launch_bounds__(32 * kReduceWarps) reduce_kernel(
+    const float* __restrict__ part_ml, const float* __restrict__ part_o, int n_slots,
+    int num_seqs, int num_q_heads, int D, float* __restrict__ out_ml, float* __restrict__ out_o) {
+  __shared__ float s_ml[kReduceWarps][2];
+  __shared__ float s_o[kReduceWarps][128];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)num_seqs * num_q_heads;
+  const int64_t i0 = (int64_t)blockIdx.y * num_q_heads + blockIdx.x;
+  const int per = (n_slots + kReduceWarps - 1) / kReduceWarps;
+  const int s0 = min(n_slots, warp * per), cnt = min(n_slots, s0 + per) - s0;
+  if (cnt > 0) {
+    // slots s0 .. s0+cnt-1 as a block of their own: shift the base pointers
+    merge_heads<1, true>(part_ml + s0 * stride * 2, part_o + s0 * stride * D, cnt, cnt, cnt,
+                         stride, i0, 1, D, &s_o[warp][0], TKV_F32, lane, 0, &s_ml[warp][0]);
+  } else if (lane == 0) {
+    s_ml[warp][0] = -INFINITY;
+    s_ml[warp][1] = 0.f;
+  }
+  __syncthreads();
+  float M = -INFINITY;
+  for (int w = 0; w < kReduceWarps; ++w) M = fmaxf(M, s_ml[w][0]);
+  for (int c = threadIdx.x; c < D + 1; c += blockDim.x) {
+    float acc = 0.f;  // c < D: o[c]; c == D: l
+    for (int w = 0; w < kReduceWarps; ++w) {
+      const float m = s_ml[w][0];
+      if (m == -INFINITY || (w * per >= n_slots)) continue;
+      const float x = c < D ? s_o[w][c] : s_ml[w][1];
+      acc = fmaf(x, fast_exp2(m - M), acc);
+    }
+    if (c < D)
+      out_o[i0 * D + c] = acc;
+    else {
+      out_ml[i0 * 2 + 0] = M;
+      out_ml[i0 * 2 + 1] = acc;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -854,6 +914,16 @@ int launch_decode_splits(DecodeArgs a, int head_dim, int bits, int, cudaStream_t
   if (head_dim == 64)
     return bits == 4 ? launch_warp_g<64, 4>(a, stream) : launch_warp_g<64, 2>(a, stream);
   return TKV_NOT_IMPLEMENTED;
+}
+
+int launch_reduce(const float* part_ml, const float* part_o, int n_slots, int num_seqs,
+                  int num_q_heads, int head_dim, float* out_ml, float* out_o,
+                  cudaStream_t stream) {
+  if (head_dim > 128) return TKV_NOT_IMPLEMENTED;
+  dim3 grid(num_q_heads, num_seqs);
+  reduce_kernel<<<grid, 32 * kReduceWarps, 0, stream>>>(part_ml, part_o, n_slots, num_seqs,
+                                                        num_q_heads, head_dim, out_ml, out_o);
+  return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
 }
 
 int launch_merge(const float* part_ml, const float* part_o, int n_slots, int num_seqs,

@@ -235,6 +235,30 @@ def paged_decode_partials(cache: KiviPagedCache, q: torch.Tensor, block_tables: 
         _ptr(work), _ptr(err), C.c_void_p(_stream(stream))))
 
 
+def paged_decode_range(cache: KiviPagedCache, q: torch.Tensor, block_tables: torch.Tensor,
+                       seq_lens: torch.Tensor, split_lo: int, split_hi: int,
+                       include_residual: bool, out_ml: torch.Tensor, out_o: torch.Tensor,
+                       workspace: torch.Tensor, scale: Optional[float] = None,
+                       seq_slots: Optional[torch.Tensor] = None,
+                       err: Optional[torch.Tensor] = None, stream=None) -> None:
+    """One GPU's share of a token-split decode: quantised splits [split_lo,
+    split_hi) (+ the residual split) reduced in the launch to one partial per
+    (sequence, q head): out_ml [B, Hq, 2], out_o [B, Hq, D] fp32.  workspace:
+    zeroed uint8 device tensor of at least
+    decode_workspace_bytes(B, Hq, D, split_hi * 512) bytes, reused across calls."""
+    _need_cuda(q, block_tables, seq_lens, out_ml, out_o, workspace)
+    B, Hq, D = q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    c = cache.c_struct()
+    L.check("tkv_paged_decode_range", L.lib().tkv_paged_decode_range(
+        C.byref(c), _ptr(q.contiguous()), _DT[q.dtype], _ptr(block_tables),
+        int(block_tables.shape[1]), _ptr(seq_lens), _ptr(seq_slots), B, Hq, float(scale),
+        int(split_lo), int(split_hi), int(bool(include_residual)), _ptr(out_ml), _ptr(out_o),
+        _ptr(workspace), int(workspace.numel() * workspace.element_size()), _ptr(err),
+        C.c_void_p(_stream(stream))))
+
+
 def merge_partials(part_ml: torch.Tensor, part_o: torch.Tensor, out: torch.Tensor,
                    stream=None) -> torch.Tensor:
     """LSE merge (paged_attention_v2.cu:132-170).  part_ml: [S, B, Hq, 2],

@@ -1,0 +1,151 @@
+"""Multi-GPU layouts of the paged KIVI decode path (one process per GPU).
+
+The path shards three ways (no collective inside a decode step except where
+the work of one sequence is split by tokens):
+
+* by sequence -- each rank owns whole sequences.  `balance_sequences` assigns
+  them by greedy token balancing (longest first, to the least-loaded rank),
+  the continuous-batching layout;
+* by kv head -- each rank owns `Hkv / N` kv heads and their q-head group
+  (`head_shard`); every rank sees every sequence, outputs are disjoint head
+  slices of `[B, Hq, D]`;
+* by tokens of one sequence (long context) -- each rank owns a contiguous
+  range of the 512-token quantised splits (`split_ranges`; the fp16 residual
+  window belongs to the last rank).  Each rank computes its range and reduces
+  it to one unnormalised partial per q head in the same launch
+  (`tkv_paged_decode_range`), the one-slot partials are all-gathered, and
+  every rank merges them with the log-sum-exp rule of paged_attention_v2.cu
+  :132-170 (`tkv_merge_partials`).  The exchange is `(m, l)` plus `o[D]` fp32
+  per q head per rank: kilobytes per step.
+
+The functions here are plain host logic over torch tensors and
+`torch.distributed`; `TokenSplitDecoder` calls the CUDA entry points and
+therefore needs the library and CUDA tensors, while `gather_slots` and the
+planning helpers also run on CPU tensors with the gloo backend.
+"""
+from __future__ import annotations
+
+import importlib
+from typing import List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+SPLIT_TOKENS = 512  # tokens per quantised split (TKV_SPLIT_TOKENS)
+
+
+# ---------------------------------------------------------------------------
+# planning
+# ---------------------------------------------------------------------------
+def balance_sequences(lengths: Sequence[int], world: int) -> List[np.ndarray]:
+    """Greedy token balancing: sequences in decreasing length (ties: lower
+    index first) go to the rank with the fewest tokens so far (ties: lower
+    rank).  Returns each rank's sequence indices in increasing order."""
+    lengths = np.asarray(lengths, np.int64)
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    order = sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
+    load = [0] * world
+    owned: List[List[int]] = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda k: (load[k], k))
+        owned[r].append(i)
+        load[r] += int(lengths[i])
+    return [np.asarray(sorted(o), np.int64) for o in owned]
+
+
+def split_ranges(n_splits: int, world: int) -> List[Tuple[int, int]]:
+    """Contiguous quantised-split ranges [lo, hi) per rank covering
+    [0, n_splits): the first n_splits % world ranks get one split more."""
+    if world < 1 or n_splits < 0:
+        raise ValueError("bad split plan")
+    base, extra = divmod(n_splits, world)
+    out, lo = [], 0
+    for r in range(world):
+        hi = lo + base + (1 if r < extra else 0)
+        out.append((lo, hi))
+        lo = hi
+    return out
+
+
+def head_shard(n_kv_heads: int, n_q_heads: int, world: int, rank: int) -> Tuple[range, range]:
+    """kv heads and q heads owned by `rank` when kv heads are split evenly."""
+    if n_kv_heads % world or n_q_heads % n_kv_heads:
+        raise ValueError(f"{n_kv_heads} kv heads do not split over {world} ranks")
+    per = n_kv_heads // world
+    grp = n_q_heads // n_kv_heads
+    kv = range(rank * per, (rank + 1) * per)
+    return kv, range(kv.start * grp, kv.stop * grp)
+
+
+def quantized_splits(max_context_len: int, residual: int, group: int) -> int:
+    """Quantised splits a decode over contexts up to max_context_len needs."""
+    x = max_context_len - residual
+    nq = group * (x // group) if x > 0 else 0
+    return (nq + SPLIT_TOKENS - 1) // SPLIT_TOKENS
+
+
+# ---------------------------------------------------------------------------
+# exchange
+# ---------------------------------------------------------------------------
+def gather_slots(part_ml: torch.Tensor, part_o: torch.Tensor,
+                 group: Optional[dist.ProcessGroup] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """All-gathers every rank's slot block ([S_local, B, Hq, 2] and
+    [S_local, B, Hq, D], the same S_local on all ranks) into
+    [world * S_local, ...] in rank order."""
+    world = dist.get_world_size(group)
+    ml = torch.empty((world * part_ml.shape[0],) + tuple(part_ml.shape[1:]), dtype=part_ml.dtype,
+                     device=part_ml.device)
+    o = torch.empty((world * part_o.shape[0],) + tuple(part_o.shape[1:]), dtype=part_o.dtype,
+                    device=part_o.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(ml, part_ml.contiguous(), group=group)
+        dist.all_gather_into_tensor(o, part_o.contiguous(), group=group)
+    else:
+        dist.all_gather(list(ml.chunk(world)), part_ml.contiguous(), group=group)
+        dist.all_gather(list(o.chunk(world)), part_o.contiguous(), group=group)
+    return ml, o
+
+
+class TokenSplitDecoder:
+    """Decode of sequences whose quantised splits are spread over the ranks
+    of `group` by `split_ranges` (each rank's cache must hold the pages of its
+    range; the last rank also holds the fp16 residual window).
+
+    Every rank computes its range and reduces it inside the same launch to one
+    partial per (sequence, q head) (`tkv_paged_decode_range`); the one-slot
+    partials of all ranks are all-gathered (`(2 + D) * 4` bytes per q head per
+    rank) and every rank merges them into `out` (`tkv_merge_partials`).
+    Buffers are allocated once per (batch, heads, context) shape.
+    """
+
+    def __init__(self, batch: int, n_q_heads: int, head_dim: int, max_context_len: int,
+                 residual: int, group_size: int, device,
+                 group: Optional[dist.ProcessGroup] = None):
+        self.ops = importlib.import_module("truellm-engine_b200.ops")
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        n = quantized_splits(max_context_len, residual, group_size)
+        self.lo, self.hi = split_ranges(n, self.world)[self.rank]
+        self.last = self.rank == self.world - 1
+        self.active = self.hi > self.lo or self.last
+        shape = (1, batch, n_q_heads)
+        self.part_ml = torch.empty(shape + (2,), dtype=torch.float32, device=device)
+        self.part_o = torch.zeros(shape + (head_dim,), dtype=torch.float32, device=device)
+        self.part_ml[..., 0] = float("-inf")  # a rank without splits contributes nothing
+        self.part_ml[..., 1] = 0.0
+        self.ws = torch.zeros(self.ops.decode_workspace_bytes(
+            batch, n_q_heads, head_dim, self.hi * SPLIT_TOKENS), dtype=torch.uint8,
+            device=device)
+
+    def __call__(self, cache, q: torch.Tensor, block_tables: torch.Tensor,
+                 seq_lens: torch.Tensor, out: torch.Tensor, scale: Optional[float] = None,
+                 err: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        if self.active:
+            self.ops.paged_decode_range(
+                cache, q, block_tables, seq_lens, self.lo, self.hi, self.last,
+                self.part_ml[0], self.part_o[0], self.ws, scale=scale, err=err, stream=stream)
+        all_ml, all_o = gather_slots(self.part_ml, self.part_o, self.group)
+        return self.ops.merge_partials(all_ml, all_o, out, stream=stream)

@@ -136,6 +136,36 @@ def config5(seed: int = 5, B: int = 256, bits: int = 4) -> DecodeWorkload:
                           "bf16", "bf16", seed, oc, 8.0)
 
 
+def subset(w: DecodeWorkload, seqs=None, Hkv: int = None, Hq: int = None,
+           bits: int = None) -> DecodeWorkload:
+    """The same workload restricted to sequences `seqs` (their block-table
+    rows; the page pool keeps its size), `Hkv` kv heads / `Hq` q heads, or
+    another bit width."""
+    idx = np.arange(w.B) if seqs is None else np.asarray(seqs, np.int64)
+    return DecodeWorkload(w.name, len(idx), Hq or w.Hq, Hkv or w.Hkv, w.D, w.group, w.residual,
+                          bits or w.bits, np.ascontiguousarray(w.lengths[idx]),
+                          np.ascontiguousarray(w.block_tables[idx]), w.num_pages, w.q_dtype,
+                          w.kv_dtype, w.seed + 7919 * (1 + (int(idx[0]) if len(idx) else 0)),
+                          w.outlier_channels, w.outlier_scale)
+
+
+def token_split_bytes(w: DecodeWorkload, split_lo: int, split_hi: int, residual: bool) -> int:
+    """HBM bytes of a decode restricted to quantised splits [split_lo,
+    split_hi) (512 tokens each) and, if `residual`, the fp16 window, plus q,
+    out and the block tables: the per-rank share of a token-split decode."""
+    D, G, R, b, H = w.D, w.group, w.residual, w.bits, w.Hkv
+    nvg = -(-D // G)
+    per_tok = 2 * D * b // 8 + 4 * nvg + 4 * D // G
+    total = 0
+    for L in w.lengths:
+        L = int(L)
+        nq = G * ((L - R) // G) if L > R else 0
+        lo, hi = min(nq, split_lo * 512), min(nq, split_hi * 512)
+        total += H * (hi - lo) * per_tok + (H * (L - nq) * 4 * D if residual else 0)
+        total += 4 * ((L + PAGE - 1) // PAGE)
+    return total + w.B * w.Hq * w.D * 2 * 2
+
+
 @dataclass
 class AppendWorkload:
     """A batch of prompt chunks appended to empty sequences."""
