@@ -1,0 +1,174 @@
+// truellm_kivi.hpp -- C++ drop-in adapter over the truellm_kivi C ABI.
+//
+// Header-only; link libtruellm_kivi.so.  It keeps the reference's C++ entry
+// points for the KIVI path with the reference's error behaviour, so an engine
+// built against truellm's own headers can switch by changing one include and
+// one namespace:
+//
+//   * kivi_params_supported / kivi_compressed_bytes / kivi_compress /
+//     kivi_decompress  (kivi_cache.cuh:32-84): unsupported parameters or
+//     n_vecs <= 0 are a silent no-op, as in kivi_cache.cu:219-220.  A status
+//     the reference has no equivalent for (odd group_size, CUDA launch
+//     failure) throws std::runtime_error instead of computing garbage.
+//   * KvCompressionPass  (kv_compression_pass.h:38-58): same constructor,
+//     init / run / enabled.  The KIVI half maps the config exactly as
+//     kv_compression_pass.cpp:29-67 does (n_outliers = residual_length,
+//     group = bits == 4 ? 16 : 8) and is disabled, not thrown, when those
+//     parameters are unsupported.  run() rounds K and V through the reference
+//     format in place with one launch each and no scratch, so the
+//     reference's 16-token prefill limit does not apply.  The VQ half of the
+//     reference pass is not part of this library: enabled() reports KIVI only.
+//     CUDA failures throw std::runtime_error (kv_compression_pass.cpp:16-24).
+//   * PagedKiviCache -- the new paged KIVI cache (a view over caller-owned
+//     buffers, like the reference's TrueBuffer): append (the reshape_and_cache
+//     slot) and decode (the paged_attention_v1/v2 slot), throwing
+//     std::invalid_argument / std::runtime_error on a non-OK status.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include <cuda_fp16.h>
+#include <cuda_runtime_api.h>
+
+#include "truellm_kivi.h"
+
+namespace truellm {
+namespace kivi_b200 {
+
+inline void throw_on(int status, const char* what) {
+  if (status == TKV_OK) return;
+  const std::string msg = std::string(what) + ": " + tkv_status_string(status);
+  if (status == TKV_INVALID_ARGUMENT) throw std::invalid_argument(msg);
+  throw std::runtime_error(msg);
+}
+
+// ---------------------------------------------------------------- reference format
+inline bool kivi_params_supported(int head_dim, int n_outliers, int group_size) {
+  return tkv_kivi_params_supported(head_dim, n_outliers, group_size) != 0;
+}
+
+inline size_t kivi_compressed_bytes(int head_dim, int n_outliers, int group_size) {
+  return tkv_kivi_compressed_bytes(head_dim, n_outliers, group_size);
+}
+
+inline void kivi_compress(const __half* d_kv_in, uint8_t* d_out, int n_vecs, int head_dim,
+                          int n_outliers, int group_size, cudaStream_t stream) {
+  if (n_vecs <= 0 || !kivi_params_supported(head_dim, n_outliers, group_size)) return;
+  throw_on(tkv_kivi_compress(d_kv_in, d_out, n_vecs, head_dim, n_outliers, group_size, stream),
+           "kivi_compress");
+}
+
+inline void kivi_decompress(const uint8_t* d_in, __half* d_kv_out, int n_vecs, int head_dim,
+                            int n_outliers, int group_size, cudaStream_t stream) {
+  if (n_vecs <= 0 || !kivi_params_supported(head_dim, n_outliers, group_size)) return;
+  throw_on(tkv_kivi_decompress(d_in, d_kv_out, n_vecs, head_dim, n_outliers, group_size,
+                               stream),
+           "kivi_decompress");
+}
+
+// ---------------------------------------------------------------- compression pass
+class KvCompressionPass {
+ public:
+  // Config: truellm::CompressionConfig (config_schema.h:144-159) or any type
+  // with kv_kivi.{enabled, bits, residual_length}.
+  template <class Config>
+  KvCompressionPass(const Config& cfg, int n_layers, int n_kv_heads, int head_dim,
+                    int block_size)
+      : kivi_enabled_(cfg.kv_kivi.enabled),
+        n_layers_(n_layers),
+        n_kv_heads_(n_kv_heads),
+        head_dim_(head_dim),
+        block_size_(block_size),
+        n_outliers_(cfg.kv_kivi.residual_length),
+        group_size_(cfg.kv_kivi.bits == 4 ? 16 : 8) {
+    if (kivi_enabled_ && !kivi_params_supported(head_dim_, n_outliers_, group_size_))
+      kivi_enabled_ = false;
+  }
+
+  // No scratch to allocate: kept for call-site compatibility.
+  template <class Allocator>
+  void init(Allocator* /*allocator*/, cudaStream_t /*stream*/) {}
+
+  void run(int /*layer_idx*/, int seq_len, void* k_ptr, void* v_ptr, cudaStream_t stream) {
+    if (!kivi_enabled_ || seq_len <= 0) return;
+    const int n_vecs = seq_len * n_kv_heads_;
+    throw_on(tkv_kivi_roundtrip_inplace(k_ptr, n_vecs, head_dim_, n_outliers_, group_size_,
+                                        stream),
+             "KvCompressionPass::run (K)");
+    throw_on(tkv_kivi_roundtrip_inplace(v_ptr, n_vecs, head_dim_, n_outliers_, group_size_,
+                                        stream),
+             "KvCompressionPass::run (V)");
+  }
+
+  bool enabled() const { return kivi_enabled_; }
+  int n_outliers() const { return n_outliers_; }
+  int group_size() const { return group_size_; }
+
+ private:
+  bool kivi_enabled_;
+  int n_layers_, n_kv_heads_, head_dim_, block_size_;
+  int n_outliers_, group_size_;
+};
+
+// ---------------------------------------------------------------- paged cache
+class PagedKiviCache {
+ public:
+  // pool: num_pages * n_kv_heads * page_bytes() bytes; ring: ring_bytes()
+  // bytes, zeroed before first use; both 16-byte aligned, owned by the caller.
+  PagedKiviCache(void* pool, void* ring, int num_pages, int max_seqs, int head_dim,
+                 int group_size, int residual, int bits, int n_kv_heads) {
+    throw_on(tkv_format_init(&c_.fmt, head_dim, group_size, residual, bits, n_kv_heads),
+             "PagedKiviCache format");
+    c_.pool = pool;
+    c_.ring = ring;
+    c_.num_pages = num_pages;
+    c_.max_seqs = max_seqs;
+  }
+
+  static tkv_format_t format(int head_dim, int group_size, int residual, int bits,
+                             int n_kv_heads) {
+    tkv_format_t f{};
+    throw_on(tkv_format_init(&f, head_dim, group_size, residual, bits, n_kv_heads), "format");
+    return f;
+  }
+  int64_t page_bytes() const { return c_.fmt.page_bytes; }
+  int64_t pool_bytes() const { return c_.fmt.page_bytes * c_.fmt.n_kv_heads * c_.num_pages; }
+  int64_t ring_bytes() const { return tkv_ring_bytes(&c_.fmt, c_.max_seqs); }
+  const tkv_cache_t& c_struct() const { return c_; }
+
+  // The reshape_and_cache slot (cache_kernels.cu:47-94): quantize-on-append.
+  void append(const void* k_new, const void* v_new, int in_dtype, const int32_t* cu_new,
+              const int32_t* seq_lens_old, const int32_t* block_tables, int max_blocks_per_seq,
+              const int32_t* seq_slots, int num_seqs, int total_new_tokens, int max_new_tokens,
+              int* err_flag, cudaStream_t stream) const {
+    throw_on(tkv_paged_append(&c_, k_new, v_new, in_dtype, cu_new, seq_lens_old, block_tables,
+                              max_blocks_per_seq, seq_slots, num_seqs, total_new_tokens,
+                              max_new_tokens, err_flag, stream),
+             "PagedKiviCache::append");
+  }
+
+  static size_t decode_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
+                                       int max_context_len) {
+    return tkv_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, max_context_len);
+  }
+
+  // The paged_attention_v1/v2 slot (cuda_engine.cpp:1137-1159).
+  void decode(const void* q, int q_dtype, void* out, int out_dtype, const int32_t* block_tables,
+              int max_blocks_per_seq, const int32_t* seq_lens, const int32_t* seq_slots,
+              int num_seqs, int num_q_heads, float scale, int max_context_len, void* workspace,
+              size_t workspace_bytes, int* err_flag, cudaStream_t stream) const {
+    throw_on(tkv_paged_decode(&c_, q, q_dtype, out, out_dtype, block_tables, max_blocks_per_seq,
+                              seq_lens, seq_slots, num_seqs, num_q_heads, scale, max_context_len,
+                              workspace, workspace_bytes, err_flag, stream),
+             "PagedKiviCache::decode");
+  }
+
+ private:
+  tkv_cache_t c_{};
+};
+
+}  // namespace kivi_b200
+}  // namespace truellm

@@ -1,0 +1,99 @@
+"""The C++ drop-in adapter (include/truellm_kivi.hpp) compiles with g++ against
+the C ABI and keeps the reference's host-side behaviour, checked without a
+GPU: KvCompressionPass maps the config like kv_compression_pass.cpp:29-67 and
+disables itself on unsupported parameters, the reference-format calls are
+silent no-ops on unsupported parameters (kivi_cache.cu:219-220), and a bad
+paged call throws instead of returning an unchecked status.
+"""
+import os
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+PKG = ROOT / "truellm-engine_b200"
+CUDA_INC = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "include"
+
+PROGRAM = r"""
+#include <cstdio>
+#include <stdexcept>
+#include "truellm_kivi.hpp"
+
+namespace kb = truellm::kivi_b200;
+
+// stand-ins with the field names of truellm::CompressionConfig (config_schema.h:121-159)
+struct KiviConfig { bool enabled = false; int bits = 8; int residual_length = 128; };
+struct CompressionConfig { bool enabled = false; KiviConfig kv_kivi; };
+struct CudaAllocator {};
+
+#define CHECK(x) do { if (!(x)) { std::printf("FAIL %s:%d %s\n", __FILE__, __LINE__, #x); return 1; } } while (0)
+
+int main() {
+  CompressionConfig cfg;
+  cfg.kv_kivi.enabled = true;
+  cfg.kv_kivi.bits = 4;
+  cfg.kv_kivi.residual_length = 32;
+  kb::KvCompressionPass pass(cfg, 32, 8, 128, 16);
+  CHECK(pass.enabled());
+  CHECK(pass.n_outliers() == 32 && pass.group_size() == 16);   // bits 4 -> group 16
+  CudaAllocator alloc;
+  pass.init(&alloc, nullptr);
+  pass.run(0, 0, nullptr, nullptr, nullptr);                     // seq_len 0: no-op
+
+  cfg.kv_kivi.bits = 8;
+  kb::KvCompressionPass pass8(cfg, 32, 8, 128, 16);
+  CHECK(pass8.group_size() == 8);
+  kb::KvCompressionPass wide(cfg, 32, 8, 256, 16);                // head_dim > 128: disabled
+  CHECK(!wide.enabled());
+  wide.run(0, 4, nullptr, nullptr, nullptr);                      // disabled: no-op
+  cfg.kv_kivi.enabled = false;
+  CHECK(!kb::KvCompressionPass(cfg, 32, 8, 128, 16).enabled());
+
+  CHECK(kb::kivi_params_supported(64, 32, 16));
+  CHECK(!kb::kivi_params_supported(64, 0, 0));
+  CHECK(kb::kivi_compressed_bytes(128, 0, 128) == 68);
+  kb::kivi_compress(nullptr, nullptr, 0, 64, 0, 32, nullptr);     // n_vecs 0: no-op
+  kb::kivi_compress(nullptr, nullptr, 10, 64, 0, 0, nullptr);     // unsupported: no-op
+  kb::kivi_decompress(nullptr, nullptr, 10, 300, 0, 32, nullptr); // unsupported: no-op
+
+  tkv_format_t f = kb::PagedKiviCache::format(128, 128, 128, 4, 8);
+  CHECK(f.page_bytes == 2176);
+  kb::PagedKiviCache cache(nullptr, nullptr, 16, 4, 128, 128, 128, 4, 8);
+  CHECK(cache.pool_bytes() == 2176LL * 8 * 16);
+  bool threw = false;
+  try {  // null pool: rejected before any launch
+    cache.decode(nullptr, TKV_BF16, nullptr, TKV_BF16, nullptr, 1, nullptr, nullptr, 1, 32,
+                 0.1f, 16, nullptr, 0, nullptr, nullptr);
+  } catch (const std::invalid_argument&) {
+    threw = true;
+  }
+  CHECK(threw);
+  threw = false;
+  try {
+    kb::PagedKiviCache::format(96, 128, 128, 4, 8);
+  } catch (const std::exception&) {
+    threw = true;
+  }
+  CHECK(threw);
+  std::printf("ok\n");
+  return 0;
+}
+"""
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="g++ not installed")
+def test_cpp_adapter_compiles_and_keeps_reference_behaviour(tmp_path):
+    lib = PKG / "libtruellm_kivi.so"
+    assert lib.exists(), "build the library first (truellm-engine_b200/build.py)"
+    src = tmp_path / "adapter_test.cpp"
+    src.write_text(PROGRAM)
+    exe = tmp_path / "adapter_test"
+    cmd = ["g++", "-std=c++17", "-O1", "-Wall", "-Werror", f"-I{ROOT / 'include'}",
+           f"-I{CUDA_INC}", str(src), f"-L{PKG}", "-ltruellm_kivi", f"-Wl,-rpath,{PKG}",
+           "-o", str(exe)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0 and run.stdout.strip() == "ok", run.stdout + run.stderr
