@@ -51,14 +51,6 @@ __device__ __forceinline__ bool append_lengths_ok(const AppendArgs& a, int L, in
 
 constexpr int kFlushThreads = 128;
 
-__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src_gmem) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst_smem)),
-               "l"(src_gmem)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.wait_all;\n" ::: "memory");
-}
 
 __device__ __forceinline__ float h2f(uint16_t h) {
   return __half2float(*reinterpret_cast<const __half*>(&h));

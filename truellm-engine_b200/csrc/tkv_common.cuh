@@ -87,6 +87,22 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
       : "memory");
 }
 
+// Per-thread asynchronous copies global -> shared (cp.async), completed by
+// cp_async_wait_all (all of this thread's outstanding copies).
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src_gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst_smem)),
+               "l"(src_gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst_smem, const void* src_gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(dst_smem)),
+               "l"(src_gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+}
+
 // L2 policy for data read once per launch (cache pages): evict it first, so
 // lines that are read again soon (split partials) stay in L2.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
