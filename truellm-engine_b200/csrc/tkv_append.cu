@@ -186,8 +186,11 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
 
   // clamp(rint(y), 0, QMAX) of the reference: the unsigned round-to-nearest
   // conversion saturates negatives (and NaN) to 0, the min caps the top
+  // clamp(rint((x - gmin) * scale), 0, QMAX) of the reference with
+  // p = (-gmin, scale): x - gmin as x + (-gmin); the unsigned round-to-nearest
+  // conversion saturates negatives (and NaN) to 0, the min caps the top
   auto code = [&](float x, float2 p) {
-    return min(__float2uint_rn(__fmul_rn(__fsub_rn(x, p.x), p.y)), static_cast<uint32_t>(QMAX));
+    return min(__float2uint_rn(__fmul_rn(__fadd_rn(x, p.x), p.y)), static_cast<uint32_t>(QMAX));
   };
   auto page_base = [&](int pi) -> uint8_t* {
     const int ph = S.phys[pi];
@@ -203,9 +206,10 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
     {
       const int cp = tid % (D / 2), ks = tid / (D / 2);
       __half2 mn = pinf, mx = ninf;
-#pragma unroll 8
-      for (int t = ks * (G / KSPLIT); t < (ks + 1) * (G / KSPLIT); ++t) {
-        const __half2 x = *reinterpret_cast<const __half2*>(&tile[t * TS + 2 * cp]);
+      const __half2* col = reinterpret_cast<const __half2*>(&tile[ks * (G / KSPLIT) * TS + 2 * cp]);
+#pragma unroll 16
+      for (int t = 0; t < G / KSPLIT; ++t) {
+        const __half2 x = col[t * (TS / 2)];
         mn = __hmin2(mn, x);
         mx = __hmax2(mx, x);
       }
@@ -233,7 +237,7 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
                         return 0.f;
                       });
         const QParams qp = quant_params(gmin, gmax, QMAX);
-        S.par[c] = make_float2(qp.gmin, qp.scale);
+        S.par[c] = make_float2(-qp.gmin, qp.scale);
         S.meta[c] = (uint32_t)qp.hstep | ((uint32_t)qp.hzero << 16);
       }
     }
@@ -246,7 +250,13 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
     float2 p[CPW];
 #pragma unroll
     for (int n = 0; n < CPW; ++n) p[n] = S.par[w * CPW + n];
-    for (int t = tid / NWR; t < G; t += TSTEP) {
+    // fully unrolled: the page and row of each step are compile-time
+    // functions of the thread's first row
+    const int t_first = tid / NWR;
+#pragma unroll
+    for (int k = 0; k < (G + TSTEP - 1) / TSTEP; ++k) {
+      const int t = t_first + k * TSTEP;
+      if (TSTEP * (k + 1) > G && t >= G) break;
       uint32_t word = 0;
 #pragma unroll
       for (int n8 = 0; n8 < CPW; n8 += 8) {
@@ -293,7 +303,7 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
                     return 0.f;
                   });
     const QParams qp = quant_params(gmin, gmax, QMAX);
-    S.par[j] = make_float2(qp.gmin, qp.scale);
+    S.par[j] = make_float2(-qp.gmin, qp.scale);
     S.meta[j] = (uint32_t)qp.hstep | ((uint32_t)qp.hzero << 16);
   }
   __syncthreads();
@@ -304,7 +314,10 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
   {
     constexpr int W = D * BITS / 64;  // words per lane
     constexpr int VW = W < 4 ? W : 4;
-    for (int pl = tid; pl < (G / kPage) * 32; pl += kFlushThreads) {
+#pragma unroll
+    for (int k = 0; k < ((G / kPage) * 32 + kFlushThreads - 1) / kFlushThreads; ++k) {
+      const int pl = tid + k * kFlushThreads;
+      if (pl >= (G / kPage) * 32) break;
       const int pi = pl >> 5, l = pl & 31, g = l >> 2, tig = l & 3;
       const int tb = pi * kPage + 2 * tig;  // token of (th, e) = (0, 0)
       const uint16_t* base = &tile[tb * TS + g];
@@ -325,23 +338,22 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
           const int wv = q * VW + u;
           uint32_t wd = 0;
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
+          for (int k = 0; k < 4; ++k) {
+            const int rh = k >> 1, th = k & 1;
+            const int r0 = 8 * th * TS, r1 = (8 * th + 1) * TS;  // rows of tokens (th, e = 0, 1)
+            if (BITS == 4) {
+              const int c = 16 * wv + 8 * rh;  // channel minus g (g < 8 stays in the group)
+              wd |= code(h2f(base[r0 + c]), pv[th][0][c / VG_CH]) << (4 * k);
+              wd |= code(h2f(base[r1 + c]), pv[th][1][c / VG_CH]) << (4 * (k + 4));
+            } else {
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int rh = k >> 1, th = k & 1;
-              const int ro = (8 * th + e) * TS;  // row offset of token (th, e)
-              if (BITS == 4) {
-                const int c = 16 * wv + 8 * rh;  // channel minus g (g < 8 stays in the group)
-                wd |= code(h2f(base[ro + c]), pv[th][e][c / VG_CH]) << (4 * (k + 4 * e));
-              } else {
-#pragma unroll
-                for (int mbi = 0; mbi < 2; ++mbi) {
-                  const int c = 16 * (2 * wv + mbi) + 8 * rh;
-                  wd |= code(h2f(base[ro + c]), pv[th][e][c / VG_CH])
-                        << (2 * (4 * mbi + k + 8 * e));
-                }
+              for (int mbi = 0; mbi < 2; ++mbi) {
+                const int c = 16 * (2 * wv + mbi) + 8 * rh;
+                wd |= code(h2f(base[r0 + c]), pv[th][0][c / VG_CH]) << (2 * (4 * mbi + k));
+                wd |= code(h2f(base[r1 + c]), pv[th][1][c / VG_CH]) << (2 * (4 * mbi + k + 8));
               }
             }
+          }
           words[u] = wd;
         }
         if (blk) {
