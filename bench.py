@@ -407,7 +407,10 @@ def run_kivi(args):
     peak, peak_kind = peaks()
     achieved = alg_bytes / t_split / 1e9
     traffic = ncu_traffic(args.workload) if world == 1 else None
-    n_launch = len(parts) * (2 if dec is not None else 1)
+    # launches per step: the token split makes two (range + reduce) plus the
+    # merge; otherwise one or two per decode call (ops.decode_launches)
+    n_launch = (3 if dec is not None else
+                sum(ops.decode_launches(p.w.B, p.w.Hq, p.max_ctx) for p in parts))
 
     line = None
     if rank == 0:

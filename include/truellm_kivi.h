@@ -189,9 +189,19 @@ TKV_API int tkv_decode_num_splits(int max_context_len);
 /* Workspace bytes for tkv_paged_decode: work counters, per-(sequence, kv head)
  * completion counters and the split partials.  Zero the whole workspace once
  * when it is allocated; every call leaves the counters zero again.  Calls that
- * share a workspace must not overlap on the GPU. */
+ * share a workspace must not overlap on the GPU.  Launches with few work items
+ * (num_seqs * num_q_heads * splits small: long single sequences, few kv heads)
+ * use 128-token splits internally; the size accounts for that. */
 TKV_API size_t tkv_decode_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
                                   int max_context_len);
+/* Kernel launches tkv_paged_decode makes for these sizes: 1 (merge fused into
+ * the decode launch) or 2 (contexts beyond 64K tokens: a separate
+ * slot-parallel merge). */
+TKV_API int tkv_decode_launches(int num_seqs, int num_q_heads, int max_context_len);
+/* Workspace bytes for tkv_paged_decode_range over splits [split_lo, split_hi)
+ * (with the finer internal splits the range may use). */
+TKV_API size_t tkv_decode_range_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
+                                                int split_lo, int split_hi);
 
 /* Replaces paged_attention_v1/v2 (cuda_engine.cpp:51-62,
  * paged_attention_v1.cu:177-213, paged_attention_v2.cu:176-251) for the KIVI
@@ -200,7 +210,9 @@ TKV_API size_t tkv_decode_workspace_bytes(int num_seqs, int num_q_heads, int hea
  * (megakernel.cu:270-277).  q, out: [num_seqs, num_q_heads, D]; q is fp16 or
  * bf16, out is fp16, bf16 or f32.  Split-KV over TKV_SPLIT_TOKENS-token splits
  * plus a log-sum-exp merge (paged_attention_v2.cu:132-170), done by the warp
- * that finishes the last split of each (sequence, kv head).  One launch. */
+ * that finishes the last split of each (sequence, kv head): one launch.
+ * Contexts beyond 64K tokens merge in a second, slot-parallel launch
+ * (tkv_decode_launches). */
 TKV_API int tkv_paged_decode(const tkv_cache_t* cache, const void* q, int q_dtype, void* out,
                      int out_dtype, const int32_t* block_tables, int max_blocks_per_seq,
                      const int32_t* seq_lens, const int32_t* seq_slots, int num_seqs,
@@ -256,9 +268,11 @@ TKV_API int tkv_paged_decode_partials(const tkv_cache_t* cache, const void* q, i
  * GPUs, gathered in any order, go to tkv_merge_partials.  A (sequence, q head)
  * with no token in the range gets m = -inf, l = 0, o = 0.  No counterpart in
  * the reference (paged_attention_v2.cu keeps every partition on one GPU).
- * workspace: at least tkv_decode_workspace_bytes(num_seqs, num_q_heads, D,
- * split_hi * TKV_SPLIT_TOKENS), 16-byte aligned, zeroed once as for
- * tkv_paged_decode (every call leaves its counters zero).  Two launches. */
+ * workspace: tkv_decode_range_workspace_bytes(num_seqs, num_q_heads, D,
+ * split_lo, split_hi) bytes (a smaller one of at least the 512-token-split
+ * size makes the launch keep 512-token splits), 16-byte aligned, zeroed once
+ * as for tkv_paged_decode (every call leaves its counters zero).  Two
+ * launches. */
 TKV_API int tkv_paged_decode_range(const tkv_cache_t* cache, const void* q, int q_dtype,
                                    const int32_t* block_tables, int max_blocks_per_seq,
                                    const int32_t* seq_lens, const int32_t* seq_slots,

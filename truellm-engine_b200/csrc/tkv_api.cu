@@ -232,13 +232,49 @@ static size_t pair_counter_bytes(int num_seqs, int num_q_heads) {
   return ((size_t)num_seqs * (size_t)num_q_heads * 4 + 255) / 256 * 256;
 }
 
-size_t tkv_decode_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
-                                  int max_context_len) {
-  if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || max_context_len < 0) return 0;
-  const size_t slots = (size_t)tkv_decode_num_splits(max_context_len);
+// Split granularity of a decode launch over n_coarse 512-token splits: 128-token
+// splits when even num_seqs * num_q_heads * n_coarse (an upper bound of the
+// 512-token work items, reached at one q head per kv head) is below 8 items
+// per resident warp, i.e. when the 512-token items certainly leave resident
+// warps idle; decided from the call's sizes alone (the same rule in the
+// workspace queries and the launches), with the B200 count of 148 SMs x 12
+// resident warps.
+static int split_pages_for(int num_seqs, int num_q_heads, int n_coarse) {
+  constexpr long long kResidentWarps = 148LL * 12;
+  const long long units = (long long)num_seqs * num_q_heads * n_coarse;
+  return units < 8 * kResidentWarps ? kFineSplitPages : kSplitPages;
+}
+
+static size_t workspace_bytes_for(int num_seqs, int num_q_heads, int head_dim, size_t slots) {
   const size_t n = slots * (size_t)num_seqs * (size_t)num_q_heads;
   return kWorkBytes + pair_counter_bytes(num_seqs, num_q_heads) + n * 2 * sizeof(float) +
          n * (size_t)head_dim * sizeof(float);
+}
+
+size_t tkv_decode_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
+                                  int max_context_len) {
+  if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || max_context_len < 0) return 0;
+  const int n_coarse = tkv_decode_num_splits(max_context_len) - 1;
+  const int sp = split_pages_for(num_seqs, num_q_heads, n_coarse);
+  return workspace_bytes_for(num_seqs, num_q_heads, head_dim,
+                             (size_t)n_coarse * (kSplitPages / sp) + 1);
+}
+
+int tkv_decode_launches(int num_seqs, int num_q_heads, int max_context_len) {
+  if (num_seqs <= 0 || num_q_heads <= 0 || max_context_len < 0) return 0;
+  const int n_coarse = tkv_decode_num_splits(max_context_len) - 1;
+  const int sp = split_pages_for(num_seqs, num_q_heads, n_coarse);
+  return n_coarse * (kSplitPages / sp) + 1 > kWideMergeSlots ? 2 : 1;
+}
+
+size_t tkv_decode_range_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
+                                        int split_lo, int split_hi) {
+  if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || split_lo < 0 ||
+      split_hi < split_lo)
+    return 0;
+  const int sp = split_pages_for(num_seqs, num_q_heads, split_hi - split_lo);
+  return workspace_bytes_for(num_seqs, num_q_heads, head_dim,
+                             (size_t)(split_hi - split_lo) * (kSplitPages / sp) + 1);
 }
 
 static int decode_partials_impl(const tkv_cache_t* cache, const void* q, int q_dtype,
@@ -247,7 +283,8 @@ static int decode_partials_impl(const tkv_cache_t* cache, const void* q, int q_d
                                 int num_q_heads, float scale, int split_lo, int split_hi,
                                 int include_residual, float* part_ml, float* part_o,
                                 void* work, unsigned int* bh_count, void* out, int out_dtype,
-                                int* err_flag, cudaStream_t stream) {
+                                int* err_flag, cudaStream_t stream,
+                                int split_pages = kSplitPages) {
   if (!cache_ok(cache)) return TKV_INVALID_ARGUMENT;
   const tkv_format_t& f = cache->fmt;
   if (q_dtype != TKV_F16 && q_dtype != TKV_BF16) return TKV_NOT_IMPLEMENTED;
@@ -289,6 +326,7 @@ static int decode_partials_impl(const tkv_cache_t* cache, const void* q, int q_d
   a.alpha = scale * 1.4426950408889634f;
   a.split_lo = split_lo;
   a.split_hi = split_hi;
+  a.split_pages = split_pages;
   a.include_residual = include_residual ? 1 : 0;
   a.n_slots = (split_hi - split_lo) + a.include_residual;
   a.part_ml = part_ml;
@@ -326,11 +364,19 @@ int tkv_paged_decode_range(const tkv_cache_t* cache, const void* q, int q_dtype,
   if (num_seqs <= 0 || num_q_heads <= 0 || split_lo < 0 || split_hi < split_lo)
     return TKV_INVALID_ARGUMENT;
   const int D = cache->fmt.head_dim;
+  // finer splits when the range has few items and the workspace holds them
+  int sp = split_pages_for(num_seqs, num_q_heads, split_hi - split_lo);
+  auto need_for = [&](int pages) {
+    const size_t sl = (size_t)(split_hi - split_lo) * (kSplitPages / pages) + 1;
+    return workspace_bytes_for(num_seqs, num_q_heads, D, sl);
+  };
+  if (workspace_bytes < need_for(sp)) sp = kSplitPages;
+  if (workspace_bytes < need_for(sp)) return TKV_INVALID_ARGUMENT;
+  const int mult = kSplitPages / sp;
+  split_lo *= mult;
+  split_hi *= mult;
   const int slots = (split_hi - split_lo) + (include_residual ? 1 : 0);
   const size_t n = (size_t)slots * num_seqs * num_q_heads;
-  const size_t need = kWorkBytes + pair_counter_bytes(num_seqs, num_q_heads) +
-                      n * 2 * sizeof(float) + n * (size_t)D * sizeof(float);
-  if (workspace_bytes < need) return TKV_INVALID_ARGUMENT;
   if (slots == 0) return TKV_INVALID_ARGUMENT;  // nothing would write out_ml / out_o
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   float* part_ml =
@@ -340,7 +386,7 @@ int tkv_paged_decode_range(const tkv_cache_t* cache, const void* q, int q_dtype,
   const int st = decode_partials_impl(cache, q, q_dtype, block_tables, max_blocks_per_seq,
                                       seq_lens, seq_slots, num_seqs, num_q_heads, scale, split_lo,
                                       split_hi, include_residual, part_ml, part_o, ws, nullptr,
-                                      nullptr, 0, err_flag, s);
+                                      nullptr, 0, err_flag, s, sp);
   if (st != TKV_OK) return st;
   return launch_reduce(part_ml, part_o, slots, num_seqs, num_q_heads, D, out_ml, out_o, s);
 }
@@ -368,7 +414,9 @@ int tkv_paged_decode(const tkv_cache_t* cache, const void* q, int q_dtype, void*
   if (workspace_bytes < need || !aligned16(workspace)) return TKV_INVALID_ARGUMENT;
   if (out_dtype != TKV_F32 && out_dtype != TKV_F16 && out_dtype != TKV_BF16)
     return TKV_NOT_IMPLEMENTED;
-  const int slots = tkv_decode_num_splits(max_context_len);
+  const int n_coarse = tkv_decode_num_splits(max_context_len) - 1;
+  const int sp = split_pages_for(num_seqs, num_q_heads, n_coarse);
+  const int slots = n_coarse * (kSplitPages / sp) + 1;
   const size_t n = (size_t)slots * num_seqs * num_q_heads;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   void* work = ws;
@@ -376,12 +424,22 @@ int tkv_paged_decode(const tkv_cache_t* cache, const void* q, int q_dtype, void*
   float* part_ml =
       reinterpret_cast<float*>(ws + kWorkBytes + pair_counter_bytes(num_seqs, num_q_heads));
   float* part_o = part_ml + 2 * n;
+  const cudaStream_t st = as_stream(stream);
+  if (slots > kWideMergeSlots) {
+    // long contexts: the split kernel, then a slot-parallel merge (a single
+    // warp merging hundreds of slots would be the launch's tail)
+    const int r = decode_partials_impl(cache, q, q_dtype, block_tables, max_blocks_per_seq,
+                                       seq_lens, seq_slots, num_seqs, num_q_heads, scale, 0,
+                                       slots - 1, 1, part_ml, part_o, work, nullptr, nullptr, 0,
+                                       err_flag, st, sp);
+    if (r != TKV_OK) return r;
+    return launch_merge(part_ml, part_o, slots, num_seqs, num_q_heads, D, out, out_dtype, st);
+  }
   // one launch: the split kernel merges each (sequence, kv head) when its last
   // split finishes
   return decode_partials_impl(cache, q, q_dtype, block_tables, max_blocks_per_seq, seq_lens,
                               seq_slots, num_seqs, num_q_heads, scale, 0, slots - 1, 1, part_ml,
-                              part_o, work, bh_count, out, out_dtype, err_flag,
-                              as_stream(stream));
+                              part_o, work, bh_count, out, out_dtype, err_flag, st, sp);
 }
 
 // ---------------------------------------------------------------------------

@@ -17,6 +17,16 @@ namespace tkv {
 constexpr int kPage = TKV_PAGE_SIZE;
 constexpr int kSplitTokens = TKV_SPLIT_TOKENS;
 constexpr int kSplitPages = kSplitTokens / kPage;  // 32
+// Pages per split for launches whose 512-token items would not give every
+// resident warp ~2 items (one long sequence, few kv heads): 128 tokens, a
+// multiple of every key group (G <= 128).
+constexpr int kFineSplitPages = 8;
+static_assert(kSplitPages % kFineSplitPages == 0, "fine splits tile the coarse ones");
+// Above this many split slots per sequence (contexts beyond 64K tokens at
+// 512-token splits) the merge runs as its own slot-parallel kernel instead of
+// in the decode launch's last warp per (sequence, kv head), whose serial merge
+// of that many slots would be the launch's tail.
+constexpr int kWideMergeSlots = 129;
 // A bounded mbarrier wait gives up after this many try_wait polls, each of
 // which suspends the thread for at most kSuspendNs while the phase is still
 // open (about 2 s in total), then reports TKV_ERR_TIMEOUT instead of
@@ -262,7 +272,8 @@ struct DecodeArgs {
   const int32_t* seq_slots;
   int num_seqs, num_q_heads, grp;
   float alpha;  // scale * log2(e)
-  int split_lo, split_hi, include_residual, n_slots;
+  int split_lo, split_hi, include_residual, n_slots;  // splits of split_pages pages
+  int split_pages;          // kSplitPages, or kFineSplitPages for launches with few items
   int n_items;              // n_slots * num_seqs * n_kv_heads
   unsigned int* work;       // [0] next work item, [1] finished warps; zero between launches
   unsigned int* bh_count;   // [num_seqs * n_kv_heads] finished slots; zero between launches

@@ -541,13 +541,13 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
     // quantised splits of this sequence that hold pages; the fused merge
     // counts and reads only those and the residual slot
     const int nv =
-        max(0, min(n_qsplit, (nq / kPage + kSplitPages - 1) / kSplitPages - a.split_lo));
+        max(0, min(n_qsplit, (nq / kPage + a.split_pages - 1) / a.split_pages - a.split_lo));
     const bool real = is_res || slot < nv;
 
     int n_units = 0, page_lo = 0, row = 0, my_phys = 0;
     if (len_ok && !is_res) {
-      page_lo = (a.split_lo + slot) * kSplitPages;
-      n_units = min(kSplitPages, nq / kPage - page_lo);  // pages, a multiple of PPG
+      page_lo = (a.split_lo + slot) * a.split_pages;
+      n_units = min(a.split_pages, nq / kPage - page_lo);  // pages, a multiple of PPG
       if (n_units > 0) {
         my_phys = lane < n_units ? bt[page_lo + lane] : 0;
         if (__any_sync(0xffffffffu, my_phys < 0 || my_phys >= a.num_pages)) {
@@ -827,15 +827,17 @@ __global__ void __launch_bounds__(32) merge_kernel(const float* __restrict__ par
                  1, D, out, out_dtype, threadIdx.x, i0);
 }
 
-// Reduction of n_slots partials to one unnormalised partial per (sequence,
-// q head): one CTA of kReduceWarps warps per (q head, sequence), warp w takes
-// a contiguous block of slots (merge_heads with RED), then the warps' partials
-// are combined with the same log-sum-exp rule in shared memory.
+// Merge of many partial slots, one CTA of kReduceWarps warps per (q head,
+// sequence): warp w combines a contiguous block of slots (merge_heads with
+// RED), then the warps' partials are combined in shared memory with the same
+// log-sum-exp rule.  out_ml != nullptr: the combined unnormalised partial
+// (M, L) to out_ml and O to out (f32); otherwise O / L to out in out_dtype.
 constexpr int kReduceWarps = 8;
 
-__global__ void __launch_bounds__(32 * kReduceWarps) reduce_kernel(
+__global__ void __launch_bounds__(32 * kReduceWarps) wide_merge_kernel(
     const float* __restrict__ part_ml, const float* __restrict__ part_o, int n_slots,
-    int num_seqs, int num_q_heads, int D, float* __restrict__ out_ml, float* __restrict__ out_o) {
+    int num_seqs, int num_q_heads, int D, void* __restrict__ out, int out_dtype,
+    float* __restrict__ out_ml) {
   __shared__ float s_ml[kReduceWarps][2];
   __shared__ float s_o[kReduceWarps][128];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -854,20 +856,34 @@ __global__ void __launch_bounds__(32 * kReduceWarps) reduce_kernel(
   __syncthreads();
   float M = -INFINITY;
   for (int w = 0; w < kReduceWarps; ++w) M = fmaxf(M, s_ml[w][0]);
-  for (int c = threadIdx.x; c < D + 1; c += blockDim.x) {
-    float acc = 0.f;  // c < D: o[c]; c == D: l
+  float L = 0.f;
+  for (int w = 0; w < kReduceWarps; ++w) {
+    const float m = s_ml[w][0];
+    if (m != -INFINITY) L = fmaf(s_ml[w][1], fast_exp2(m - M), L);
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float acc = 0.f;
     for (int w = 0; w < kReduceWarps; ++w) {
       const float m = s_ml[w][0];
-      if (m == -INFINITY || (w * per >= n_slots)) continue;
-      const float x = c < D ? s_o[w][c] : s_ml[w][1];
-      acc = fmaf(x, fast_exp2(m - M), acc);
+      if (m != -INFINITY) acc = fmaf(s_o[w][c], fast_exp2(m - M), acc);
     }
-    if (c < D)
-      out_o[i0 * D + c] = acc;
-    else {
-      out_ml[i0 * 2 + 0] = M;
-      out_ml[i0 * 2 + 1] = acc;
+    const int64_t oi = i0 * D + c;
+    if (out_ml) {
+      static_cast<float*>(out)[oi] = acc;
+    } else {
+      const float v = acc * inv;
+      if (out_dtype == TKV_F32)
+        static_cast<float*>(out)[oi] = v;
+      else if (out_dtype == TKV_BF16)
+        static_cast<__nv_bfloat16*>(out)[oi] = __float2bfloat16_rn(v);
+      else
+        static_cast<__half*>(out)[oi] = __float2half_rn(v);
     }
+  }
+  if (out_ml && threadIdx.x == 0) {
+    out_ml[i0 * 2 + 0] = M;
+    out_ml[i0 * 2 + 1] = L;
   }
 }
 
@@ -921,13 +937,19 @@ int launch_reduce(const float* part_ml, const float* part_o, int n_slots, int nu
                   cudaStream_t stream) {
   if (head_dim > 128) return TKV_NOT_IMPLEMENTED;
   dim3 grid(num_q_heads, num_seqs);
-  reduce_kernel<<<grid, 32 * kReduceWarps, 0, stream>>>(part_ml, part_o, n_slots, num_seqs,
-                                                        num_q_heads, head_dim, out_ml, out_o);
+  wide_merge_kernel<<<grid, 32 * kReduceWarps, 0, stream>>>(
+      part_ml, part_o, n_slots, num_seqs, num_q_heads, head_dim, out_o, TKV_F32, out_ml);
   return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
 }
 
 int launch_merge(const float* part_ml, const float* part_o, int n_slots, int num_seqs,
                  int num_q_heads, int head_dim, void* out, int out_dtype, cudaStream_t stream) {
+  if (n_slots > kWideMergeSlots && head_dim <= 128) {  // many slots: 8 warps per q head
+    dim3 grid(num_q_heads, num_seqs);
+    wide_merge_kernel<<<grid, 32 * kReduceWarps, 0, stream>>>(
+        part_ml, part_o, n_slots, num_seqs, num_q_heads, head_dim, out, out_dtype, nullptr);
+    return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
+  }
   dim3 grid(num_q_heads, num_seqs);
   merge_kernel<<<grid, 32, 0, stream>>>(part_ml, part_o, n_slots, num_seqs, num_q_heads,
                                          head_dim, out, out_dtype);

@@ -178,6 +178,17 @@ def decode_workspace_bytes(num_seqs: int, num_q_heads: int, head_dim: int,
                                                   max_context_len))
 
 
+def decode_range_workspace_bytes(num_seqs: int, num_q_heads: int, head_dim: int,
+                                 split_lo: int, split_hi: int) -> int:
+    return int(L.lib().tkv_decode_range_workspace_bytes(num_seqs, num_q_heads, head_dim,
+                                                        split_lo, split_hi))
+
+
+def decode_launches(num_seqs: int, num_q_heads: int, max_context_len: int) -> int:
+    """Kernel launches one paged_decode call makes (1, or 2 beyond 64K tokens)."""
+    return int(L.lib().tkv_decode_launches(num_seqs, num_q_heads, max_context_len))
+
+
 def decode_num_splits(max_context_len: int) -> int:
     return int(L.lib().tkv_decode_num_splits(max_context_len))
 
@@ -244,8 +255,8 @@ def paged_decode_range(cache: KiviPagedCache, q: torch.Tensor, block_tables: tor
     """One GPU's share of a token-split decode: quantised splits [split_lo,
     split_hi) (+ the residual split) reduced in the launch to one partial per
     (sequence, q head): out_ml [B, Hq, 2], out_o [B, Hq, D] fp32.  workspace:
-    zeroed uint8 device tensor of at least
-    decode_workspace_bytes(B, Hq, D, split_hi * 512) bytes, reused across calls."""
+    zeroed uint8 device tensor of decode_range_workspace_bytes(B, Hq, D,
+    split_lo, split_hi) bytes, reused across calls."""
     _need_cuda(q, block_tables, seq_lens, out_ml, out_o, workspace)
     B, Hq, D = q.shape
     if scale is None:

@@ -136,9 +136,8 @@ class TokenSplitDecoder:
         self.part_o = torch.zeros(shape + (head_dim,), dtype=torch.float32, device=device)
         self.part_ml[..., 0] = float("-inf")  # a rank without splits contributes nothing
         self.part_ml[..., 1] = 0.0
-        self.ws = torch.zeros(self.ops.decode_workspace_bytes(
-            batch, n_q_heads, head_dim, self.hi * SPLIT_TOKENS), dtype=torch.uint8,
-            device=device)
+        self.ws = torch.zeros(max(16, self.ops.decode_range_workspace_bytes(
+            batch, n_q_heads, head_dim, self.lo, self.hi)), dtype=torch.uint8, device=device)
 
     def __call__(self, cache, q: torch.Tensor, block_tables: torch.Tensor,
                  seq_lens: torch.Tensor, out: torch.Tensor, scale: Optional[float] = None,
