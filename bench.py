@@ -333,9 +333,25 @@ def run_kivi(args):
         args, wl, ops, torch, dev, rank, world)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
+    # the token split is launch-bound (range decode, reduce, two all-gathers,
+    # merge per step): its step is captured once in a CUDA graph and replayed
+    graph = None
+    if dec is not None:
+        p0 = parts[0]
+        try:
+            graph = dec.capture(p0.cache, p0.q, p0.bt, p0.lens, p0.out, scale=p0.scale, err=err)
+        except Exception as e:  # capture not supported here: eager calls
+            print(f"rank {rank}: CUDA graph capture failed ({e!r}); eager token split",
+                  file=sys.stderr)
+        stream = torch.cuda.current_stream()
 
     def decode(p, q, lens):
-        if dec is not None:
+        if graph is not None:  # captured over p.q / p.lens
+            if q is not p.q:
+                p.q.copy_(q, non_blocking=True)
+                p.lens.copy_(lens, non_blocking=True)
+            graph.replay()
+        elif dec is not None:
             dec(p.cache, q, p.bt, lens, p.out, scale=p.scale, err=err, stream=stream)
         else:
             ops.paged_decode(p.cache, q, p.bt, lens, p.max_ctx, scale=p.scale, out=p.out,
@@ -407,8 +423,9 @@ def run_kivi(args):
     peak, peak_kind = peaks()
     achieved = alg_bytes / t_split / 1e9
     traffic = ncu_traffic(args.workload) if world == 1 else None
-    # launches per step: the token split makes two (range + reduce) plus the
-    # merge; otherwise one or two per decode call (ops.decode_launches)
+    # our kernel launches per step: the token split runs three (split kernel
+    # and reduce of the range, merge) besides NCCL's all-gathers; otherwise one
+    # or two per decode call (ops.decode_launches)
     n_launch = (3 if dec is not None else
                 sum(ops.decode_launches(p.w.B, p.w.Hq, p.max_ctx) for p in parts))
 
@@ -462,6 +479,9 @@ def run_kivi(args):
             "clocks": clocks,
         }
         print(json.dumps(line))
+    if graph is not None:  # a graph holding NCCL calls goes before the group
+        torch.cuda.synchronize()
+        del graph
     if world > 1 or dist.is_initialized():
         dist.barrier()
         dist.destroy_process_group()

@@ -90,15 +90,19 @@ def quantized_splits(max_context_len: int, residual: int, group: int) -> int:
 # exchange
 # ---------------------------------------------------------------------------
 def gather_slots(part_ml: torch.Tensor, part_o: torch.Tensor,
-                 group: Optional[dist.ProcessGroup] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+                 group: Optional[dist.ProcessGroup] = None,
+                 out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
+                 ) -> Tuple[torch.Tensor, torch.Tensor]:
     """All-gathers every rank's slot block ([S_local, B, Hq, 2] and
     [S_local, B, Hq, D], the same S_local on all ranks) into
-    [world * S_local, ...] in rank order."""
+    [world * S_local, ...] in rank order (into `out` when given)."""
     world = dist.get_world_size(group)
-    ml = torch.empty((world * part_ml.shape[0],) + tuple(part_ml.shape[1:]), dtype=part_ml.dtype,
-                     device=part_ml.device)
-    o = torch.empty((world * part_o.shape[0],) + tuple(part_o.shape[1:]), dtype=part_o.dtype,
-                    device=part_o.device)
+    if out is None:
+        out = (torch.empty((world * part_ml.shape[0],) + tuple(part_ml.shape[1:]),
+                           dtype=part_ml.dtype, device=part_ml.device),
+               torch.empty((world * part_o.shape[0],) + tuple(part_o.shape[1:]),
+                           dtype=part_o.dtype, device=part_o.device))
+    ml, o = out
     if dist.get_backend(group) == "nccl":
         dist.all_gather_into_tensor(ml, part_ml.contiguous(), group=group)
         dist.all_gather_into_tensor(o, part_o.contiguous(), group=group)
@@ -138,6 +142,10 @@ class TokenSplitDecoder:
         self.part_ml[..., 1] = 0.0
         self.ws = torch.zeros(max(16, self.ops.decode_range_workspace_bytes(
             batch, n_q_heads, head_dim, self.lo, self.hi)), dtype=torch.uint8, device=device)
+        self.all_ml = torch.empty((self.world,) + shape[1:] + (2,), dtype=torch.float32,
+                                  device=device)
+        self.all_o = torch.empty((self.world,) + shape[1:] + (head_dim,), dtype=torch.float32,
+                                 device=device)
 
     def __call__(self, cache, q: torch.Tensor, block_tables: torch.Tensor,
                  seq_lens: torch.Tensor, out: torch.Tensor, scale: Optional[float] = None,
@@ -146,5 +154,26 @@ class TokenSplitDecoder:
             self.ops.paged_decode_range(
                 cache, q, block_tables, seq_lens, self.lo, self.hi, self.last,
                 self.part_ml[0], self.part_o[0], self.ws, scale=scale, err=err, stream=stream)
-        all_ml, all_o = gather_slots(self.part_ml, self.part_o, self.group)
-        return self.ops.merge_partials(all_ml, all_o, out, stream=stream)
+        gather_slots(self.part_ml, self.part_o, self.group, out=(self.all_ml, self.all_o))
+        return self.ops.merge_partials(self.all_ml, self.all_o, out, stream=stream)
+
+    def capture(self, cache, q: torch.Tensor, block_tables: torch.Tensor,
+                seq_lens: torch.Tensor, out: torch.Tensor, scale: Optional[float] = None,
+                err: Optional[torch.Tensor] = None) -> "torch.cuda.CUDAGraph":
+        """Records one call (range decode, reduce, all-gather, merge) over these
+        fixed buffers in a CUDA graph; `graph.replay()` reruns it with one host
+        launch.  Every rank of the group must capture (the graph holds the
+        collectives); release the graph before destroying the group."""
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):  # first call eagerly: communicator set-up
+            self(cache, q, block_tables, seq_lens, out, scale=scale, err=err,
+                 stream=torch.cuda.current_stream())
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self(cache, q, block_tables, seq_lens, out, scale=scale, err=err,
+                 stream=torch.cuda.current_stream())
+        return graph
+
