@@ -345,25 +345,41 @@ def run_kivi(args):
                   file=sys.stderr)
         stream = torch.cuda.current_stream()
 
-    def decode(p, q, lens):
+    def decode(p, q, lens, st):
         if graph is not None:  # captured over p.q / p.lens
             if q is not p.q:
                 p.q.copy_(q, non_blocking=True)
                 p.lens.copy_(lens, non_blocking=True)
             graph.replay()
         elif dec is not None:
-            dec(p.cache, q, p.bt, lens, p.out, scale=p.scale, err=err, stream=stream)
+            dec(p.cache, q, p.bt, lens, p.out, scale=p.scale, err=err, stream=st)
         else:
             ops.paged_decode(p.cache, q, p.bt, lens, p.max_ctx, scale=p.scale, out=p.out,
-                             workspace=p.ws, err=err, stream=stream)
+                             workspace=p.ws, err=err, stream=st)
+
+    # parts of one step (config 5: the INT4 and the INT2 sequences) run on
+    # their own streams so one launch's tail overlaps the other's work
+    side = [torch.cuda.Stream() for _ in parts[1:]]
+
+    def run_parts(fn):
+        if not side:
+            fn(parts[0], stream)
+            return
+        for s_ in side:
+            s_.wait_stream(stream)
+        fn(parts[0], stream)
+        for p, s_ in zip(parts[1:], side):
+            with torch.cuda.stream(s_):
+                fn(p, s_)
+        for s_ in side:
+            stream.wait_stream(s_)
 
     def step(ev=None):
         # one decode step: one decode launch per part (split + fused merge); the
         # token-split layout adds the all-gather of partials and the merge
         if ev is not None:
             ev[0].record(stream)
-        for p in parts:
-            decode(p, p.q, p.lens)
+        run_parts(lambda p, s_: decode(p, p.q, p.lens, s_))
         if ev is not None:
             ev[1].record(stream)
 
@@ -396,12 +412,14 @@ def run_kivi(args):
     t_step, t_split = float(times[0]), float(times[1])
 
     # ---- end to end through the public API with host buffers ----
+    def e2e_part(p, st):
+        p.q_dev.copy_(p.q_host, non_blocking=True)
+        p.lens_dev.copy_(p.lens_host, non_blocking=True)
+        decode(p, p.q_dev, p.lens_dev, st)
+        p.out_host.copy_(p.out, non_blocking=True)
+
     def e2e_step():
-        for p in parts:
-            p.q_dev.copy_(p.q_host, non_blocking=True)
-            p.lens_dev.copy_(p.lens_host, non_blocking=True)
-            decode(p, p.q_dev, p.lens_dev)
-            p.out_host.copy_(p.out, non_blocking=True)
+        run_parts(e2e_part)
 
     for _ in range(args.warmup):
         e2e_step()
