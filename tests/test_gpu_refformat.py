@@ -147,3 +147,26 @@ def test_reference_roundtrip_tolerances_on_gpu(ops, cuda):
     assert np.abs(rt(x, 4, 16) - x).max() <= 0.1
     x = np.full((1, 32), 2.5, np.float32)
     assert np.abs(rt(x, 0, 16) - 2.5).max() <= 1e-2
+
+
+def test_compression_pass_mirror_matches_oracle(O, cuda):
+    """KvCompressionPass (the reference class's call sequence) rounds the K and
+    V of a 37-token prefill through the reference format in place: every
+    vector equals the oracle's decompress(compress(x)); the reference skipped
+    prefills longer than its 16-token scratch (kv_compression_pass.cpp:184-200)."""
+    import importlib
+    CF = importlib.import_module("truellm-engine_b200.config")
+    cfg = CF.parse("[inference.compression.kv_kivi]\nenabled = true\nbits = 4\n"
+                   "residual_length = 8\n")
+    p = CF.KvCompressionPass(cfg, 32, 8, 128, 16)
+    assert p.enabled()
+    seq_len = 37
+    xk = _inputs(128, seq_len * 8, 71)
+    xv = _inputs(128, seq_len * 8, 72)
+    k, v = _t(xk, cuda), _t(xv, cuda)
+    p.init()
+    p.run(0, seq_len, k, v)
+    torch.cuda.synchronize()
+    for got, x in ((k, xk), (v, xv)):
+        want = O.kivi_decompress(O.kivi_compress(x, 8, 16), 128, 8, 16)
+        assert np.array_equal(got.cpu().numpy().view(np.uint16).reshape(-1, 128), want)
