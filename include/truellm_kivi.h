@@ -287,6 +287,114 @@ TKV_API int tkv_merge_partials(const float* part_ml, const float* part_o, int n_
                        int num_q_heads, int head_dim, void* out, int out_dtype, void* stream);
 
 /* ---------------------------------------------------------------- */
+/* Page allocator (host)                                              */
+/* ---------------------------------------------------------------- */
+/* Replaces the bookkeeping of CudaAllocator
+ * (src/inference/backends/cuda/cuda_allocator.{h,cpp}) for the KIVI cache:
+ * a free list of page ids (lowest id handed out first,
+ * cuda_allocator.cpp:97-99), per-page reference counts for shared pages
+ * (copy_sequence, cuda_allocator.cpp:205-217), per-sequence block tables with
+ * -1 padding (:231-253), and eviction bookkeeping (:318-380).  One allocator
+ * serves every layer: a page id and a ring row name the same slot in each
+ * layer's cache, as a block id does across the reference's per-layer pools.
+ *
+ * Differences the KIVI format brings:
+ *   * a sequence of length L holds n_q(L) / 16 pages (whole key groups only);
+ *     its n_r most recent tokens live in its ring row, which the allocator
+ *     also hands out (one per live sequence, max_seqs rows);
+ *   * a page is written once, when its key group is flushed, and never again,
+ *     so pages shared by tkv_allocator_fork stay valid for both sequences
+ *     without copy-on-write; the fork's ring row must be copied on the device
+ *     (tkv_copy_ring_rows) before either sequence appends again;
+ *   * the block-table width is a constructor argument (the reference caps it
+ *     at 2048 blocks = 32K tokens, cuda_allocator.cpp:76).
+ * All functions are thread-safe (one mutex, as cuda_allocator.h:14-16), touch
+ * no device memory and never block on the GPU.  Errors: TKV_INVALID_ARGUMENT
+ * (unknown / duplicate / evicted sequence, length beyond the table width),
+ * TKV_OUT_OF_MEMORY (not enough free pages or ring rows; nothing changes). */
+typedef struct tkv_allocator tkv_allocator_t;
+
+typedef struct tkv_allocator_stats {
+  int32_t pages_total, pages_used, pages_free, pages_shared; /* shared: refcount > 1 */
+  int32_t rows_total, rows_free;
+  int32_t sequences, evicted;
+  float utilization_pct; /* 100 * pages_used / pages_total (KvCacheStats) */
+} tkv_allocator_stats_t;
+
+TKV_API int tkv_allocator_create(const tkv_format_t* fmt, int num_pages, int max_seqs,
+                                 int max_blocks_per_seq, tkv_allocator_t** out);
+TKV_API void tkv_allocator_destroy(tkv_allocator_t* a);
+/* Pages for n_q(len) tokens: the block-table entries a sequence of length len uses. */
+TKV_API int tkv_allocator_pages_for(const tkv_allocator_t* a, int len);
+/* allocate_sequence (cuda_allocator.cpp:129-158): a ring row plus the pages of
+ * a sequence of num_tokens tokens.  *ring_row (may be NULL) gets the row. */
+TKV_API int tkv_allocator_add_sequence(tkv_allocator_t* a, uint64_t seq_id, int num_tokens,
+                                       int32_t* ring_row);
+/* extend_sequence (cuda_allocator.cpp:160-171), by length: makes the table
+ * cover new_len tokens (allocating the pages of every key group that the
+ * append up to new_len will flush) and records new_len as the length.
+ * *n_new (may be NULL) gets the number of pages added. */
+TKV_API int tkv_allocator_extend(tkv_allocator_t* a, uint64_t seq_id, int new_len, int* n_new);
+/* free_sequence (cuda_allocator.cpp:173-185); unknown ids are a no-op (TKV_OK). */
+TKV_API int tkv_allocator_free_sequence(tkv_allocator_t* a, uint64_t seq_id);
+/* copy_sequence (cuda_allocator.cpp:187-203): dst shares src's pages
+ * (reference counted) and length, and gets a ring row of its own.  The caller
+ * copies ring row *src_row to *dst_row in every layer (tkv_copy_ring_rows). */
+TKV_API int tkv_allocator_fork(tkv_allocator_t* a, uint64_t src_id, uint64_t dst_id,
+                               int32_t* src_row, int32_t* dst_row);
+/* Batched get_device_block_table (cuda_allocator.cpp:231-253), filled on the
+ * host: block_tables [n][max_blocks_per_seq] (-1 padded), seq_lens [n] and
+ * ring rows [n] (either may be NULL) for the sequences seq_ids[0..n). */
+TKV_API int tkv_allocator_tables(const tkv_allocator_t* a, const uint64_t* seq_ids, int n,
+                                 int32_t* block_tables, int32_t* seq_lens, int32_t* ring_rows);
+/* Length, page count, ring row (-1 when evicted) and evicted flag of one sequence. */
+TKV_API int tkv_allocator_sequence(const tkv_allocator_t* a, uint64_t seq_id, int* len,
+                                   int* n_pages, int32_t* ring_row, int* evicted);
+TKV_API int tkv_allocator_stats(const tkv_allocator_t* a, tkv_allocator_stats_t* out);
+/* evict_sequence bookkeeping (cuda_allocator.cpp:318-350): writes the
+ * sequence's pages (in table order, capacity max_blocks_per_seq) and ring row,
+ * then releases them.  The caller moves them to host memory
+ * (tkv_swap_pages / tkv_swap_ring_rows) on a stream that orders the copy
+ * before any later write to the released pages. */
+TKV_API int tkv_allocator_evict(tkv_allocator_t* a, uint64_t seq_id, int32_t* pages,
+                                int* n_pages, int32_t* ring_row);
+/* reload_sequence bookkeeping (cuda_allocator.cpp:352-378): fresh pages and a
+ * ring row for an evicted sequence, written to pages / *ring_row; the caller
+ * copies the saved images back.  Out of pages or rows: TKV_OUT_OF_MEMORY and
+ * the sequence stays evicted (the reference leaves a partial table). */
+TKV_API int tkv_allocator_reload(tkv_allocator_t* a, uint64_t seq_id, int32_t* pages,
+                                 int* n_pages, int32_t* ring_row);
+
+/* ---------------------------------------------------------------- */
+/* Page and ring-row moves (device)                                   */
+/* ---------------------------------------------------------------- */
+/* The KIVI format is position independent: a (page, kv head) block holds its
+ * codes and meta, a ring row its fp16 tokens, so pages and rows move as bytes.
+ * mapping: device int32 [n][2] = {src, dst} index pairs (destinations distinct
+ * and not sources of other pairs).  Pairs with an index out of range are
+ * skipped and flagged TKV_ERR_BAD_PAGE / TKV_ERR_BAD_SLOT in *err_flag (may be
+ * NULL).  One launch each, 16-byte loads and stores. */
+/* copy_blocks (cache_kernels.cu:107-127,234-260): pool page -> pool page. */
+TKV_API int tkv_copy_pages(const tkv_cache_t* cache, const int32_t* mapping, int n,
+                           int* err_flag, void* stream);
+/* swap_blocks (cache_kernels.cu:138-168,262-283) for pages: between the pool
+ * and `images` [capacity][n_kv_heads][page_bytes] in pinned host memory (or
+ * device memory).  direction 0: pool page src -> image dst; 1: image src ->
+ * pool page dst.  Host memory that is not page-locked is rejected with
+ * TKV_INVALID_ARGUMENT before launching. */
+TKV_API int tkv_swap_pages(const tkv_cache_t* cache, void* images, int64_t capacity,
+                           const int32_t* mapping, int n, int direction, int* err_flag,
+                           void* stream);
+/* Ring row -> ring row (the device half of tkv_allocator_fork). */
+TKV_API int tkv_copy_ring_rows(const tkv_cache_t* cache, const int32_t* mapping, int n,
+                               int* err_flag, void* stream);
+/* Ring rows between the ring and `images` [capacity][tkv_ring_bytes(fmt, 1)]
+ * bytes, directions as tkv_swap_pages. */
+TKV_API int tkv_swap_ring_rows(const tkv_cache_t* cache, void* images, int64_t capacity,
+                               const int32_t* mapping, int n, int direction, int* err_flag,
+                               void* stream);
+
+/* ---------------------------------------------------------------- */
 /* Kernel registry (include/truellm/kernel.h:23-57)                   */
 /* ---------------------------------------------------------------- */
 #ifndef TRUELLM_KERNEL_ABI_VERSION

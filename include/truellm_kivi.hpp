@@ -19,6 +19,9 @@
 //     reference's 16-token prefill limit does not apply.  The VQ half of the
 //     reference pass is not part of this library: enabled() reports KIVI only.
 //     CUDA failures throw std::runtime_error (kv_compression_pass.cpp:16-24).
+//   * KiviPageAllocator -- CudaAllocator's page bookkeeping for the KIVI
+//     cache (bool / -1 returns as in cuda_allocator.cpp), plus copy_pages /
+//     swap_pages / copy_ring_rows / swap_ring_rows (copy_blocks / swap_blocks).
 //   * PagedKiviCache -- the new paged KIVI cache (a view over caller-owned
 //     buffers, like the reference's TrueBuffer): append (the reshape_and_cache
 //     slot) and decode (the paged_attention_v1/v2 slot), throwing
@@ -169,6 +172,85 @@ class PagedKiviCache {
  private:
   tkv_cache_t c_{};
 };
+
+// ---------------------------------------------------------------- page allocator
+// CudaAllocator's bookkeeping (cuda_allocator.h:38-160) for the KIVI cache,
+// with the reference's bool / -1 returns.  Host only; the device half of
+// copy / evict / reload is copy_ring_rows / swap_pages / swap_ring_rows below.
+class KiviPageAllocator {
+ public:
+  KiviPageAllocator(const tkv_format_t& fmt, int num_pages, int max_seqs, int max_blocks_per_seq)
+      : max_blocks_(max_blocks_per_seq), num_pages_(num_pages) {
+    throw_on(tkv_allocator_create(&fmt, num_pages, max_seqs, max_blocks_per_seq, &a_),
+             "KiviPageAllocator");
+  }
+  ~KiviPageAllocator() { tkv_allocator_destroy(a_); }
+  KiviPageAllocator(const KiviPageAllocator&) = delete;
+  KiviPageAllocator& operator=(const KiviPageAllocator&) = delete;
+
+  bool allocate_sequence(uint64_t seq_id, int num_prompt_tokens, int32_t* ring_row = nullptr) {
+    return tkv_allocator_add_sequence(a_, seq_id, num_prompt_tokens, ring_row) == TKV_OK;
+  }
+  // Pages added so the table covers new_len tokens, or -1.
+  int extend_sequence(uint64_t seq_id, int new_len) {
+    int added = 0;
+    return tkv_allocator_extend(a_, seq_id, new_len, &added) == TKV_OK ? added : -1;
+  }
+  void free_sequence(uint64_t seq_id) { tkv_allocator_free_sequence(a_, seq_id); }
+  // Shares src's pages; the caller copies ring row *src_row to *dst_row.
+  bool copy_sequence(uint64_t src_id, uint64_t dst_id, int32_t* src_row = nullptr,
+                     int32_t* dst_row = nullptr) {
+    return tkv_allocator_fork(a_, src_id, dst_id, src_row, dst_row) == TKV_OK;
+  }
+  // block_tables [n][max_blocks_per_seq()] (-1 padded), seq_lens [n], ring_rows [n].
+  void block_tables(const uint64_t* seq_ids, int n, int32_t* block_tables, int32_t* seq_lens,
+                    int32_t* ring_rows) const {
+    throw_on(tkv_allocator_tables(a_, seq_ids, n, block_tables, seq_lens, ring_rows),
+             "KiviPageAllocator::block_tables");
+  }
+  // pages: capacity max_blocks_per_seq(); released on return.
+  bool evict_sequence(uint64_t seq_id, int32_t* pages, int* n_pages, int32_t* ring_row) {
+    return tkv_allocator_evict(a_, seq_id, pages, n_pages, ring_row) == TKV_OK;
+  }
+  bool reload_sequence(uint64_t seq_id, int32_t* pages, int* n_pages, int32_t* ring_row) {
+    return tkv_allocator_reload(a_, seq_id, pages, n_pages, ring_row) == TKV_OK;
+  }
+  tkv_allocator_stats_t stats() const {
+    tkv_allocator_stats_t s{};
+    throw_on(tkv_allocator_stats(a_, &s), "KiviPageAllocator::stats");
+    return s;
+  }
+  int num_free_blocks() const { return stats().pages_free; }
+  int num_total_blocks() const { return num_pages_; }
+  int block_size() const { return TKV_PAGE_SIZE; }
+  int max_blocks_per_seq() const { return max_blocks_; }
+
+ private:
+  tkv_allocator_t* a_ = nullptr;
+  int max_blocks_, num_pages_;
+};
+
+// copy_blocks / swap_blocks (cache_kernels.cu:234-283) for KIVI pages and ring rows.
+inline void copy_pages(const tkv_cache_t& c, const int32_t* mapping, int n, int* err,
+                       cudaStream_t stream) {
+  throw_on(tkv_copy_pages(&c, mapping, n, err, stream), "copy_pages");
+}
+inline void swap_pages(const tkv_cache_t& c, void* images, int64_t capacity,
+                       const int32_t* mapping, int n, int direction, int* err,
+                       cudaStream_t stream) {
+  throw_on(tkv_swap_pages(&c, images, capacity, mapping, n, direction, err, stream),
+           "swap_pages");
+}
+inline void copy_ring_rows(const tkv_cache_t& c, const int32_t* mapping, int n, int* err,
+                           cudaStream_t stream) {
+  throw_on(tkv_copy_ring_rows(&c, mapping, n, err, stream), "copy_ring_rows");
+}
+inline void swap_ring_rows(const tkv_cache_t& c, void* images, int64_t capacity,
+                           const int32_t* mapping, int n, int direction, int* err,
+                           cudaStream_t stream) {
+  throw_on(tkv_swap_ring_rows(&c, images, capacity, mapping, n, direction, err, stream),
+           "swap_ring_rows");
+}
 
 }  // namespace kivi_b200
 }  // namespace truellm

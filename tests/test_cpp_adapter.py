@@ -77,6 +77,34 @@ int main() {
     threw = true;
   }
   CHECK(threw);
+  // page allocator: reference bool / -1 returns, shared pages, -1 padded tables
+  kb::KiviPageAllocator pa(f, 32, 2, 16);
+  int32_t row = -1;
+  CHECK(pa.allocate_sequence(1, 256, &row) && row == 0);        // 8 pages
+  CHECK(!pa.allocate_sequence(1, 0));                           // duplicate
+  CHECK(pa.extend_sequence(1, 384) == 8 && pa.extend_sequence(7, 384) == -1);
+  int32_t sr = -1, dr = -1;
+  CHECK(pa.copy_sequence(1, 2, &sr, &dr) && sr == 0 && dr == 1);
+  CHECK(!pa.copy_sequence(1, 3));                               // out of ring rows
+  CHECK(pa.stats().pages_shared == 16 && pa.num_free_blocks() == 16);
+  uint64_t ids[2] = {1, 2};
+  int32_t bt[32], lens[2], rows[2];
+  pa.block_tables(ids, 2, bt, lens, rows);
+  CHECK(bt[0] == 0 && bt[15] == 15 && bt[16] == 0 && lens[1] == 384 && rows[1] == 1);
+  int32_t pages[16];
+  int np = 0;
+  CHECK(pa.evict_sequence(1, pages, &np, &row) && np == 16 && row == 0);
+  CHECK(pa.stats().pages_used == 16 && pa.stats().evicted == 1);
+  pa.free_sequence(2);
+  CHECK(pa.num_free_blocks() == 32);
+  CHECK(pa.reload_sequence(1, pages, &np, &row) && np == 16);
+  threw = false;
+  try {
+    pa.block_tables(ids, 2, bt, lens, rows);                    // 2 is gone
+  } catch (const std::invalid_argument&) {
+    threw = true;
+  }
+  CHECK(threw);
   std::printf("ok\n");
   return 0;
 }

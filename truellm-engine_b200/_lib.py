@@ -54,8 +54,17 @@ class TruellmKernelManifest(C.Structure):
     ]
 
 
+class TkvAllocatorStats(C.Structure):
+    _fields_ = [
+        ("pages_total", C.c_int32), ("pages_used", C.c_int32), ("pages_free", C.c_int32),
+        ("pages_shared", C.c_int32), ("rows_total", C.c_int32), ("rows_free", C.c_int32),
+        ("sequences", C.c_int32), ("evicted", C.c_int32), ("utilization_pct", C.c_float),
+    ]
+
+
 _vp, _i32, _i64, _sz, _f32 = C.c_void_p, C.c_int, C.c_int64, C.c_size_t, C.c_float
 _ip = C.POINTER(C.c_int)
+_u64 = C.c_uint64
 
 # name -> (restype, argtypes); every symbol the header declares.
 SIGNATURES = {
@@ -86,6 +95,22 @@ SIGNATURES = {
                                       _i32, _i32, _f32, _i32, _i32, _i32, _vp, _vp, _vp, _sz,
                                       _vp, _vp]),
     "tkv_merge_partials": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _i32, _vp]),
+    "tkv_allocator_create": (_i32, [C.POINTER(TkvFormat), _i32, _i32, _i32, C.POINTER(_vp)]),
+    "tkv_allocator_destroy": (None, [_vp]),
+    "tkv_allocator_pages_for": (_i32, [_vp, _i32]),
+    "tkv_allocator_add_sequence": (_i32, [_vp, _u64, _i32, _ip]),
+    "tkv_allocator_extend": (_i32, [_vp, _u64, _i32, _ip]),
+    "tkv_allocator_free_sequence": (_i32, [_vp, _u64]),
+    "tkv_allocator_fork": (_i32, [_vp, _u64, _u64, _ip, _ip]),
+    "tkv_allocator_tables": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp]),
+    "tkv_allocator_sequence": (_i32, [_vp, _u64, _ip, _ip, _ip, _ip]),
+    "tkv_allocator_stats": (_i32, [_vp, C.POINTER(TkvAllocatorStats)]),
+    "tkv_allocator_evict": (_i32, [_vp, _u64, _vp, _ip, _ip]),
+    "tkv_allocator_reload": (_i32, [_vp, _u64, _vp, _ip, _ip]),
+    "tkv_copy_pages": (_i32, [C.POINTER(TkvCache), _vp, _i32, _vp, _vp]),
+    "tkv_swap_pages": (_i32, [C.POINTER(TkvCache), _vp, _i64, _vp, _i32, _i32, _vp, _vp]),
+    "tkv_copy_ring_rows": (_i32, [C.POINTER(TkvCache), _vp, _i32, _vp, _vp]),
+    "tkv_swap_ring_rows": (_i32, [C.POINTER(TkvCache), _vp, _i64, _vp, _i32, _i32, _vp, _vp]),
     "truellm_kernel_init": (C.POINTER(TruellmKernelManifest), []),
     "tkv_cache_kernel_manifest": (C.POINTER(TruellmKernelManifest), []),
 }

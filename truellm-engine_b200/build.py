@@ -1,6 +1,6 @@
 """Build the sm_100a C-ABI library libtruellm_kivi.so in-tree with nvcc.
 
-Each csrc/*.cu file is compiled to an object for sm_100a (-lineinfo, -O3,
+Each csrc/*.cu (and host-only csrc/*.cpp) file is compiled to an object for sm_100a (-lineinfo, -O3,
 IEEE division and square root, no fast-math) in parallel and linked into one
 shared library with the CUDA runtime linked statically, so the library only
 needs the driver on the GPU box.  Objects go to _build/ (not committed).
@@ -35,7 +35,7 @@ def nvcc() -> str:
 
 
 def _sources() -> list[Path]:
-    return sorted(CSRC.glob("*.cu"))
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
 
 
 def _deps() -> list[Path]:

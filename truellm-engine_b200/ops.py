@@ -280,3 +280,66 @@ def merge_partials(part_ml: torch.Tensor, part_o: torch.Tensor, out: torch.Tenso
         _ptr(part_ml), _ptr(part_o), S, B, Hq, D, _ptr(out), _DT[out.dtype],
         C.c_void_p(_stream(stream))))
     return out
+
+
+# ---------------------------------------------------------------------------
+# page and ring-row moves (copy_blocks / swap_blocks, cache_kernels.cu:107-168)
+# ---------------------------------------------------------------------------
+def _mapping(mapping: torch.Tensor) -> int:
+    if mapping.dtype != torch.int32 or mapping.dim() != 2 or mapping.shape[1] != 2:
+        raise ValueError("mapping must be an int32 [n, 2] tensor of (src, dst) pairs")
+    if not (mapping.is_cuda or mapping.is_pinned()):
+        raise ValueError("mapping must be a CUDA or pinned host tensor")
+    return int(mapping.shape[0])
+
+
+def _images(images: torch.Tensor, like: torch.Tensor) -> None:
+    """images must be [capacity, *like.shape[1:]] of like's dtype, contiguous,
+    in CUDA or pinned host memory: the kernel addresses whole rows of it."""
+    if not (images.is_cuda or images.is_pinned()) or not images.is_contiguous():
+        raise ValueError("images must be a contiguous CUDA or pinned host tensor")
+    if images.dtype != like.dtype or tuple(images.shape[1:]) != tuple(like.shape[1:]):
+        raise ValueError(f"images must be [capacity, {', '.join(map(str, like.shape[1:]))}] "
+                         f"{like.dtype}")
+
+
+def copy_pages(cache: KiviPagedCache, mapping: torch.Tensor, err: Optional[torch.Tensor] = None,
+               stream=None) -> None:
+    """copy_blocks for KIVI pages: pool page mapping[i,0] -> mapping[i,1]."""
+    n = _mapping(mapping)
+    c = cache.c_struct()
+    L.check("tkv_copy_pages", L.lib().tkv_copy_pages(
+        C.byref(c), _ptr(mapping), n, _ptr(err), C.c_void_p(_stream(stream))))
+
+
+def swap_pages(cache: KiviPagedCache, images: torch.Tensor, mapping: torch.Tensor,
+               direction: int, err: Optional[torch.Tensor] = None, stream=None) -> None:
+    """swap_blocks for KIVI pages.  images: [capacity, n_kv_heads, page_bytes]
+    uint8, pinned host (or CUDA); direction 0 = pool -> images, 1 = images -> pool."""
+    n = _mapping(mapping)
+    _images(images, cache.pool)
+    c = cache.c_struct()
+    cap = int(images.shape[0])
+    L.check("tkv_swap_pages", L.lib().tkv_swap_pages(
+        C.byref(c), _ptr(images), cap, _ptr(mapping), n, int(direction), _ptr(err),
+        C.c_void_p(_stream(stream))))
+
+
+def copy_ring_rows(cache: KiviPagedCache, mapping: torch.Tensor,
+                   err: Optional[torch.Tensor] = None, stream=None) -> None:
+    """Ring row mapping[i,0] -> mapping[i,1] (the device half of a fork)."""
+    n = _mapping(mapping)
+    c = cache.c_struct()
+    L.check("tkv_copy_ring_rows", L.lib().tkv_copy_ring_rows(
+        C.byref(c), _ptr(mapping), n, _ptr(err), C.c_void_p(_stream(stream))))
+
+
+def swap_ring_rows(cache: KiviPagedCache, images: torch.Tensor, mapping: torch.Tensor,
+                   direction: int, err: Optional[torch.Tensor] = None, stream=None) -> None:
+    """Ring rows to / from images [capacity, *ring row shape] fp16 (pinned host or CUDA)."""
+    n = _mapping(mapping)
+    _images(images, cache.ring)
+    c = cache.c_struct()
+    L.check("tkv_swap_ring_rows", L.lib().tkv_swap_ring_rows(
+        C.byref(c), _ptr(images), int(images.shape[0]), _ptr(mapping), n, int(direction),
+        _ptr(err), C.c_void_p(_stream(stream))))
