@@ -281,6 +281,23 @@ TKV_API int tkv_paged_decode_range(const tkv_cache_t* cache, const void* q, int 
                                    float* out_o, void* workspace, size_t workspace_bytes,
                                    int* err_flag, void* stream);
 
+/* Chunked-prefill attention over the KIVI cache.  The reference runs its
+ * prefill attention token by token (cuda_engine.cpp:842-860); this is one
+ * launch for a batch of chunks.  For sequence s, the n_s = cu_q[s+1] - cu_q[s]
+ * query rows q[cu_q[s] .. cu_q[s+1]) are its last n_s tokens (already appended
+ * with tkv_paged_append), at positions p = seq_lens[s] - n_s + i; each
+ * attends causally to tokens [0, p] with the decode's math and kv-head
+ * mapping.  q: [total_q_tokens, num_q_heads, D] fp16 or bf16; out: same
+ * shape, fp16, bf16 or f32, 16-byte aligned.  max_q_tokens bounds n_s (it
+ * sizes the grid).  Sequences with n_s > seq_lens[s] are skipped and flagged
+ * TKV_ERR_BAD_LENGTH.  One launch, no workspace. */
+TKV_API int tkv_paged_prefill(const tkv_cache_t* cache, const void* q, int q_dtype, void* out,
+                              int out_dtype, const int32_t* cu_q, const int32_t* block_tables,
+                              int max_blocks_per_seq, const int32_t* seq_lens,
+                              const int32_t* seq_slots, int num_seqs, int num_q_heads,
+                              int total_q_tokens, int max_q_tokens, float scale, int* err_flag,
+                              void* stream);
+
 /* Log-sum-exp merge of n_slots partial sets laid out as above
  * (paged_attention_v2.cu:132-170) into out [num_seqs, num_q_heads, D]. */
 TKV_API int tkv_merge_partials(const float* part_ml, const float* part_o, int n_slots, int num_seqs,

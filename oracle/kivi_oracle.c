@@ -18,6 +18,9 @@
  *   - decode attention semantics: score = (q.k) * scale, GQA kv_head = h / (Hq/Hkv),
  *     max-subtracted softmax, out = sum p*v   (third_party/custom_kernels/megakernel.cu:267-350)
  *   - split-KV log-sum-exp merge   (third_party/vllm_kernels/paged_attention_v2.cu:132-170)
+ *   - chunked-prefill attention: the same semantics per query token with a
+ *     causal limit (the reference's prefill site, cuda_engine.cpp:842-860,
+ *     runs it token by token)
  *
  * The paged KIVI cache format (pages, key groups per channel over G tokens,
  * value groups per token over G channels, fp16 residual ring) has no reference
@@ -671,4 +674,100 @@ void or_decode(const or_fmt* f, const uint8_t* pool, const uint16_t* ring, const
   free(m);
   free(l);
   free(o);
+}
+
+/* Chunked-prefill attention over the paged cache, in fp64 (the semantics of
+ * megakernel.cu:267-350 applied per query token with a causal limit).  For
+ * sequence b, the n_b = cu_q[b+1] - cu_q[b] query rows q[cu_q[b] + i] are its
+ * last n_b tokens, at positions p = seq_lens[b] - n_b + i, each attending to
+ * the cached tokens [0, p] -- read where the cache holds them at length
+ * seq_lens[b] (pages below n_q, ring above).
+ *   q: [T, Hq, D] fp32; out: [T, Hq, D] fp64.  Rows of sequences whose n_b
+ *   exceeds seq_lens[b] are left untouched. */
+typedef struct {
+  const or_fmt* f;
+  const uint8_t* pool;
+  const uint16_t* ring;
+  const float* q;
+  const int32_t* cu_q;
+  const int32_t* block_tables;
+  int max_blocks;
+  const int32_t* seq_lens;
+  int B, Hq;
+  double scale;
+  double* out;
+  int next;
+  pthread_mutex_t mu;
+} prefill_job;
+
+static void prefill_one(prefill_job* J, int b, int h) {
+  const or_fmt* f = J->f;
+  const int D = f->head_dim, H = f->n_kv_heads, Hq = J->Hq, grp = Hq / H;
+  const int L = J->seq_lens[b], n = J->cu_q[b + 1] - J->cu_q[b];
+  if (n <= 0 || n > L) return;
+  const int nq = or_nq(f, L);
+  const int32_t* bt = J->block_tables + (long)b * J->max_blocks;
+  float* kv = (float*)malloc(sizeof(float) * 2 * D * L);
+  double* s = (double*)malloc(sizeof(double) * L);
+  for (int t = 0; t < L; ++t)
+    or_token_kv(f, J->pool, J->ring, bt, b, h, t, nq, kv + (long)t * 2 * D,
+                kv + (long)t * 2 * D + D);
+  for (int i = 0; i < n; ++i) {
+    const int p = L - n + i;
+    for (int j = 0; j < grp; ++j) {
+      const long row = (long)(J->cu_q[b] + i) * Hq + h * grp + j;
+      const float* qq = J->q + row * D;
+      double m = -INFINITY;
+      for (int t = 0; t <= p; ++t) {
+        const float* k = kv + (long)t * 2 * D;
+        double acc = 0;
+        for (int c = 0; c < D; ++c) acc += (double)qq[c] * (double)k[c];
+        s[t] = acc * J->scale;
+        if (s[t] > m) m = s[t];
+      }
+      double l = 0;
+      double* o = J->out + row * D;
+      for (int c = 0; c < D; ++c) o[c] = 0;
+      for (int t = 0; t <= p; ++t) {
+        const double w = exp(s[t] - m);
+        l += w;
+        const float* v = kv + (long)t * 2 * D + D;
+        for (int c = 0; c < D; ++c) o[c] += w * (double)v[c];
+      }
+      for (int c = 0; c < D; ++c) o[c] /= l;
+    }
+  }
+  free(s);
+  free(kv);
+}
+
+static void* prefill_worker(void* arg) {
+  prefill_job* J = (prefill_job*)arg;
+  int H = J->f->n_kv_heads, total = J->B * H;
+  for (;;) {
+    pthread_mutex_lock(&J->mu);
+    int w = J->next++;
+    pthread_mutex_unlock(&J->mu);
+    if (w >= total) break;
+    prefill_one(J, w / H, w % H);
+  }
+  return NULL;
+}
+
+void or_prefill(const or_fmt* f, const uint8_t* pool, const uint16_t* ring, const float* q,
+                const int32_t* cu_q, const int32_t* block_tables, int max_blocks,
+                const int32_t* seq_lens, int B, int Hq, double scale, double* out,
+                int n_threads) {
+  prefill_job J = {f, pool, ring, q, cu_q, block_tables, max_blocks, seq_lens, B, Hq, scale,
+                   out, 0};
+  pthread_mutex_init(&J.mu, NULL);
+  if (n_threads < 1) n_threads = 1;
+  if (n_threads > 256) n_threads = 256;
+  pthread_t th[256];
+  int started = 0;
+  for (int i = 1; i < n_threads; ++i)
+    if (pthread_create(&th[started], NULL, prefill_worker, &J) == 0) ++started;
+  prefill_worker(&J);
+  for (int i = 0; i < started; ++i) pthread_join(th[i], NULL);
+  pthread_mutex_destroy(&J.mu);
 }

@@ -73,6 +73,9 @@ def lib() -> C.CDLL:
         h.or_decode.argtypes = [C.POINTER(Fmt), P(np.uint8), P(np.uint16), P(np.float32),
                                 P(np.int32), C.c_int, P(np.int32), C.c_int, C.c_int, C.c_double,
                                 P(np.float64), C.c_int]
+        h.or_prefill.argtypes = [C.POINTER(Fmt), P(np.uint8), P(np.uint16), P(np.float32),
+                                 P(np.int32), P(np.int32), C.c_int, P(np.int32), C.c_int,
+                                 C.c_int, C.c_double, P(np.float64), C.c_int]
         _o = h
     return _o
 
@@ -185,6 +188,18 @@ class PagedState:
         out = np.zeros((B, Hq, D), dtype=np.float64)
         lib().or_decode(C.byref(self.fmt), self.pool, self.ring, q, bt, bt.shape[1],
                         _c(seq_lens, np.int32), B, Hq, float(scale), out, int(n_threads))
+        return out
+
+    def prefill(self, q_f32, cu_q, block_tables, seq_lens, scale, n_threads=1) -> np.ndarray:
+        """Causal chunked-prefill attention: q [T, Hq, D] rows of each
+        sequence's last cu_q[b+1]-cu_q[b] tokens; returns out [T, Hq, D] fp64."""
+        q = _c(q_f32, np.float32)
+        T, Hq, D = q.shape
+        bt = _c(block_tables, np.int32)
+        out = np.zeros((T, Hq, D), dtype=np.float64)
+        lib().or_prefill(C.byref(self.fmt), self.pool, self.ring, q, _c(cu_q, np.int32), bt,
+                         bt.shape[1], _c(seq_lens, np.int32), len(seq_lens), Hq, float(scale),
+                         out, int(n_threads))
         return out
 
     def decode_partial(self, q_f32, block_tables, seq_lens, scale, tok_lo, tok_hi, n_threads=1):

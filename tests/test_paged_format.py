@@ -183,3 +183,41 @@ def test_partial_merge_equals_full(O, wl):
         ms.append(m.reshape(-1)); ls.append(l.reshape(-1)); os_.append(o.reshape(-1, w.D))
     merged = O.merge(np.array(ms), np.array(ls), np.array(os_))
     assert np.allclose(merged.reshape(full.shape), full, atol=1e-12, rtol=1e-10)
+
+
+def test_prefill_oracle_against_numpy_causal_attention(O, wl):
+    """The chunked-prefill restatement: each of the last n tokens attends to
+    the cached tokens up to its own position (GQA 2)."""
+    w = wl.config1()
+    rng = np.random.default_rng(5)
+    L, n, Hq = int(w.lengths[0]), 100, 2 * w.Hkv
+    k, v = wl.kv_tokens(rng, L, w.Hkv, w.D, w.outlier_channels, w.outlier_scale)
+    st = O.PagedState(w.D, w.group, w.residual, w.bits, w.Hkv, w.num_pages, 1)
+    st.append(wl.to_bits(k, "f16"), wl.to_bits(v, "f16"), False, np.array([0, L], np.int32),
+              np.array([0], np.int32), w.block_tables)
+    q = rng.standard_normal((n, Hq, w.D)).astype(np.float16).astype(np.float32)
+    scale = 1 / np.sqrt(w.D)
+    out = st.prefill(q, np.array([0, n], np.int32), w.block_tables, w.lengths, scale)
+    for h in range(w.Hkv):
+        K, V = _dequant_numpy(O, st, w.block_tables[0], h, L)
+        for i in range(0, n, 7):
+            p = L - n + i
+            for j in range(2):
+                s = (K[:p + 1] @ q[i, 2 * h + j].astype(np.float64)) * scale
+                e = np.exp(s - s.max())
+                ref = (e @ V[:p + 1]) / e.sum()
+                assert np.allclose(out[i, 2 * h + j], ref, atol=1e-6, rtol=1e-6)
+
+
+def test_prefill_oracle_last_row_equals_decode(O, wl):
+    w = wl.config1()
+    rng = np.random.default_rng(6)
+    L = int(w.lengths[0])
+    k, v = wl.kv_tokens(rng, L, w.Hkv, w.D, w.outlier_channels, w.outlier_scale)
+    st = O.PagedState(w.D, w.group, w.residual, w.bits, w.Hkv, w.num_pages, 1)
+    st.append(wl.to_bits(k, "f16"), wl.to_bits(v, "f16"), False, np.array([0, L], np.int32),
+              np.array([0], np.int32), w.block_tables)
+    q = rng.standard_normal((3, w.Hq, w.D)).astype(np.float32)
+    pre = st.prefill(q, np.array([0, 3], np.int32), w.block_tables, w.lengths, 0.125)
+    dec = st.decode(q[2:], w.block_tables, w.lengths, 0.125)
+    assert np.array_equal(pre[2], dec[0])

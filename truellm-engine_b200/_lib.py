@@ -95,6 +95,8 @@ SIGNATURES = {
                                       _i32, _i32, _f32, _i32, _i32, _i32, _vp, _vp, _vp, _sz,
                                       _vp, _vp]),
     "tkv_merge_partials": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _i32, _vp]),
+    "tkv_paged_prefill": (_i32, [C.POINTER(TkvCache), _vp, _i32, _vp, _i32, _vp, _vp, _i32, _vp,
+                                 _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp]),
     "tkv_allocator_create": (_i32, [C.POINTER(TkvFormat), _i32, _i32, _i32, C.POINTER(_vp)]),
     "tkv_allocator_destroy": (None, [_vp]),
     "tkv_allocator_pages_for": (_i32, [_vp, _i32]),

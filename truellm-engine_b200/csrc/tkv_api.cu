@@ -391,6 +391,51 @@ int tkv_paged_decode_range(const tkv_cache_t* cache, const void* q, int q_dtype,
   return launch_reduce(part_ml, part_o, slots, num_seqs, num_q_heads, D, out_ml, out_o, s);
 }
 
+int tkv_paged_prefill(const tkv_cache_t* cache, const void* q, int q_dtype, void* out,
+                      int out_dtype, const int32_t* cu_q, const int32_t* block_tables,
+                      int max_blocks_per_seq, const int32_t* seq_lens, const int32_t* seq_slots,
+                      int num_seqs, int num_q_heads, int total_q_tokens, int max_q_tokens,
+                      float scale, int* err_flag, void* stream) {
+  if (!cache_ok(cache)) return TKV_INVALID_ARGUMENT;
+  if (q_dtype != TKV_F16 && q_dtype != TKV_BF16) return TKV_NOT_IMPLEMENTED;
+  if (out_dtype != TKV_F32 && out_dtype != TKV_F16 && out_dtype != TKV_BF16)
+    return TKV_NOT_IMPLEMENTED;
+  const tkv_format_t& f = cache->fmt;
+  if (num_seqs < 0 || num_q_heads <= 0 || num_q_heads % f.n_kv_heads != 0 ||
+      total_q_tokens < 0 || max_q_tokens < 0 || max_blocks_per_seq <= 0)
+    return TKV_INVALID_ARGUMENT;
+  if (num_seqs == 0 || max_q_tokens == 0 || total_q_tokens == 0) return TKV_OK;
+  if (!q || !out || !cu_q || !block_tables || !seq_lens || !aligned16(out))
+    return TKV_INVALID_ARGUMENT;
+  PrefillArgs a;
+  a.pool = static_cast<const uint8_t*>(cache->pool);
+  a.ring = static_cast<const uint16_t*>(cache->ring);
+  a.num_pages = cache->num_pages;
+  a.max_seqs = cache->max_seqs;
+  a.n_kv_heads = f.n_kv_heads;
+  a.residual = f.residual;
+  a.ring_cap = f.ring_cap;
+  a.q = q;
+  a.q_bf16 = q_dtype == TKV_BF16;
+  a.out = out;
+  a.out_dtype = out_dtype;
+  a.cu_q = cu_q;
+  a.block_tables = block_tables;
+  a.max_blocks = max_blocks_per_seq;
+  a.seq_lens = seq_lens;
+  a.seq_slots = seq_slots;
+  a.num_seqs = num_seqs;
+  a.num_q_heads = num_q_heads;
+  a.grp = num_q_heads / f.n_kv_heads;
+  a.total_q = total_q_tokens;
+  const int64_t rows = (int64_t)max_q_tokens * a.grp;
+  if ((rows + 15) / 16 > 0x7fffffff) return TKV_INVALID_ARGUMENT;
+  a.n_rt = (int)((rows + 15) / 16);
+  a.alpha = scale * 1.4426950408889634f;
+  a.err = err_flag;
+  return launch_prefill(a, f.head_dim, f.bits, f.group_size, as_stream(stream));
+}
+
 int tkv_merge_partials(const float* part_ml, const float* part_o, int n_slots, int num_seqs,
                        int num_q_heads, int head_dim, void* out, int out_dtype, void* stream) {
   if (!part_ml || !part_o || !out || n_slots <= 0 || num_seqs <= 0 || num_seqs > 65535 ||

@@ -285,12 +285,32 @@ struct DecodeArgs {
   int* err;
 };
 
+struct PrefillArgs {
+  const uint8_t* pool;
+  const uint16_t* ring;
+  int num_pages, max_seqs, n_kv_heads, residual, ring_cap;
+  const void* q;
+  bool q_bf16;
+  void* out;
+  int out_dtype;
+  const int32_t* cu_q;
+  const int32_t* block_tables;
+  int max_blocks;
+  const int32_t* seq_lens;
+  const int32_t* seq_slots;
+  int num_seqs, num_q_heads, grp, total_q;
+  int n_rt;     // 16-row query tiles per (sequence, kv head) for the longest chunk
+  float alpha;  // scale * log2(e)
+  int* err;
+};
+
 int launch_ref_kivi(int mode, const void* in, void* out, int n_vecs, int head_dim, int n_outliers,
                     int group_size, cudaStream_t stream);
 int launch_append(const AppendArgs& a, int num_seqs, cudaStream_t stream);
 int launch_decode_splits(DecodeArgs a, int head_dim, int bits, int n_vgroups, cudaStream_t stream);
 int launch_reduce(const float* part_ml, const float* part_o, int n_slots, int num_seqs,
                   int num_q_heads, int head_dim, float* out_ml, float* out_o, cudaStream_t stream);
+int launch_prefill(const PrefillArgs& a, int head_dim, int bits, int group, cudaStream_t stream);
 int launch_merge(const float* part_ml, const float* part_o, int n_slots, int num_seqs,
                  int num_q_heads, int head_dim, void* out, int out_dtype, cudaStream_t stream);
 

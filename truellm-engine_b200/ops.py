@@ -270,6 +270,30 @@ def paged_decode_range(cache: KiviPagedCache, q: torch.Tensor, block_tables: tor
         C.c_void_p(_stream(stream))))
 
 
+def paged_prefill(cache: KiviPagedCache, q: torch.Tensor, cu_q: torch.Tensor,
+                  block_tables: torch.Tensor, seq_lens: torch.Tensor,
+                  max_q_tokens: Optional[int] = None, scale: Optional[float] = None,
+                  out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                  seq_slots: Optional[torch.Tensor] = None, err: Optional[torch.Tensor] = None,
+                  stream=None) -> torch.Tensor:
+    """Causal chunked-prefill attention over the KIVI cache: q [T, Hq, D]
+    holds, per sequence, its last cu_q[s+1]-cu_q[s] tokens (already appended);
+    seq_lens are the lengths after the append.  Returns out [T, Hq, D]."""
+    _need_cuda(q, cu_q, block_tables, seq_lens)
+    T, Hq, D = q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty((T, Hq, D), dtype=out_dtype or q.dtype, device=q.device)
+    mq = T if max_q_tokens is None else int(max_q_tokens)
+    c = cache.c_struct()
+    L.check("tkv_paged_prefill", L.lib().tkv_paged_prefill(
+        C.byref(c), _ptr(q.contiguous()), _DT[q.dtype], _ptr(out), _DT[out.dtype], _ptr(cu_q),
+        _ptr(block_tables), int(block_tables.shape[1]), _ptr(seq_lens), _ptr(seq_slots),
+        int(seq_lens.numel()), Hq, T, mq, float(scale), _ptr(err), C.c_void_p(_stream(stream))))
+    return out
+
+
 def merge_partials(part_ml: torch.Tensor, part_o: torch.Tensor, out: torch.Tensor,
                    stream=None) -> torch.Tensor:
     """LSE merge (paged_attention_v2.cu:132-170).  part_ml: [S, B, Hq, 2],
