@@ -14,6 +14,11 @@ layer.  metric = sequence-tokens/s (B / step time), whole job.
 64 sequences x 2048-token bf16 chunk per GPU appended to
 empty sequences, metric = appended tokens/s.
 
+--workload prefill measures chunked-prefill attention over the compressed
+cache: 8 sequences per GPU with 4096 cached tokens each append a 512-token
+chunk whose query rows attend causally to the whole cache, metric = query
+tokens/s (the reference runs this attention token by token).
+
 --impl reference times the reference's CPU path for the same workload: the
 CPU restatement of the reference algorithm (oracle/, the reference has no CPU
 implementation of this path) on all host threads, over a bounded sample of the
@@ -39,6 +44,8 @@ METRIC = "KIVI-INT4 paged decode-attn seq-tokens/s (HBM GB/s and % of peak in ro
 UNIT = "seq-tokens/s"
 APPEND_METRIC = "KIVI-INT4 quantize-on-append appended tokens/s (config 3)"
 APPEND_UNIT = "tokens/s"
+PREFILL_METRIC = "KIVI-INT4 chunked-prefill attention query-tokens/s (TFLOP/s in roofline)"
+PREFILL_UNIT = "query-tokens/s"
 
 
 def parse():
@@ -47,7 +54,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="config2",
-                    choices=["config2", "config3", "config4", "config4b", "config5"])
+                    choices=["config2", "config3", "config4", "config4b", "config5", "prefill"])
     ap.add_argument("--impl", default="kivi", choices=["kivi", "reference"])
     ap.add_argument("--cpu-sample", type=int, default=8, help="sequences in the CPU sample")
     return ap.parse_args()
@@ -700,8 +707,221 @@ def run_append(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# chunked prefill over the compressed cache
+# ---------------------------------------------------------------------------
+def prefill_inputs(ops, wl, w, torch, dev):
+    """The cache after the chunk's append (history + chunk appended through the
+    public API) and the chunk's seeded bf16 query rows."""
+    fmt = ops.KiviFormat(w.D, w.group, w.residual, w.bits, w.Hkv)
+    cache = ops.KiviPagedCache(fmt, w.num_pages, w.B, dev)
+    bt = torch.from_numpy(w.block_tables).to(dev)
+    L = w.hist + w.chunk
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(w.seed)
+    k = torch.randn((w.B * L, w.Hkv, w.D), generator=gen, device=dev, dtype=torch.float32)
+    v = torch.randn((w.B * L, w.Hkv, w.D), generator=gen, device=dev, dtype=torch.float32)
+    oc = torch.from_numpy(np.asarray(w.outlier_channels, np.int64)).to(dev)
+    k[:, :, oc] *= w.outlier_scale
+    cu = (torch.arange(w.B + 1, dtype=torch.int32) * L).to(dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ops.paged_append(cache, k.to(torch.bfloat16), v.to(torch.bfloat16), cu,
+                     torch.zeros(w.B, dtype=torch.int32, device=dev), bt, max_new_tokens=L,
+                     err=err)
+    q = torch.randn((w.B * w.chunk, w.Hq, w.D), generator=gen, device=dev).to(torch.bfloat16)
+    cu_q = (torch.arange(w.B + 1, dtype=torch.int32) * w.chunk).to(dev)
+    lens = torch.full((w.B,), L, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()
+    if int(err.item()) != 0:
+        raise RuntimeError(f"device error flag {int(err.item()):#x}")
+    return cache, bt, q, cu_q, lens
+
+
+def cpu_prefill_time(O, wl, w, threads):
+    """Oracle prefill of sequence 0 (all kv heads over `threads` threads): the
+    same chunk / history shape, its own seeded inputs."""
+    rng = np.random.default_rng(w.seed)
+    L = w.hist + w.chunk
+    k = wl.f32_to_bf16_bits(rng.standard_normal((L, w.Hkv, w.D)).astype(np.float32))
+    v = wl.f32_to_bf16_bits(rng.standard_normal((L, w.Hkv, w.D)).astype(np.float32))
+    bt = np.ascontiguousarray(w.block_tables[:1])
+    st = O.PagedState(w.D, w.group, w.residual, w.bits, w.Hkv, w.num_pages, 1)
+    st.append(k, v, True, np.array([0, L], np.int32), np.zeros(1, np.int32), bt)
+    q = wl.bits_to_f32(wl.f32_to_bf16_bits(
+        rng.standard_normal((w.chunk, w.Hq, w.D)).astype(np.float32)), "bf16")
+    t0 = time.perf_counter()
+    st.prefill(q, np.array([0, w.chunk], np.int32), bt, np.array([L], np.int32),
+               1 / math.sqrt(w.D), n_threads=threads)
+    return time.perf_counter() - t0
+
+
+def run_prefill_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+    O.build()
+    wl = importlib.import_module("truellm-engine_b200.workloads")
+    w = wl.prefill(seed=6000)
+    threads = os.cpu_count() or 1
+    times = [cpu_prefill_time(O, wl, w, threads) for _ in range(max(1, min(args.steps, 2)))]
+    t = float(np.mean(times))
+    value = w.chunk / t
+    line = {
+        "impl": "reference", "metric": PREFILL_METRIC, "value": value, "unit": PREFILL_UNIT,
+        "n_gpus": args.gpus, "steps": len(times), "warmup": 0, "ms_per_step": t * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic",
+        "config": {"workload": f"prefill: sample of 1 sequence, {w.hist} cached + {w.chunk} "
+                               "chunk tokens"},
+        "cpu_baseline": {"value": value, "unit": PREFILL_UNIT, "cores": threads, "kind": "port",
+                         "sample": f"1 of the {w.B} sequences (all {w.Hkv} kv heads), CPU "
+                                   "restatement of the causal attention over the dequantised "
+                                   "cache, fp64"},
+        "e2e": {"value": value, "unit": PREFILL_UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def run_prefill(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    ops = importlib.import_module("truellm-engine_b200.ops")
+    wl = importlib.import_module("truellm-engine_b200.workloads")
+    w = wl.prefill(seed=6000 + rank)
+    cache, bt, q, cu_q, lens = prefill_inputs(ops, wl, w, torch, dev)
+    out = torch.empty_like(q)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+    T = w.B * w.chunk
+
+    def step(qq, oo):
+        ops.paged_prefill(cache, qq, cu_q, bt, lens, max_q_tokens=w.chunk, out=oo, err=err,
+                          stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(3, args.warmup)):
+        step(q, out)
+    barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            step(q, out)
+            evs[i][1].record(stream)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    clocks = clk.summary()
+    if int(err.item()) != 0:
+        raise RuntimeError(f"device error flag {int(err.item()):#x}")
+    t_step = start.elapsed_time(stop) / 1e3 / args.steps
+    t_call = float(np.mean([a.elapsed_time(b) for a, b in evs])) / 1e3
+    times = torch.tensor([t_step, t_call], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    t_step, t_call = float(times[0]), float(times[1])
+
+    # ---- end to end: q from pinned host memory, the attention output read back ----
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    q_dev, o_dev = torch.empty_like(q), torch.empty_like(out)
+    n_e2e = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        step(q_dev, o_dev)
+        out_host.copy_(o_dev, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n_e2e):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_e2e = torch.tensor([e0.elapsed_time(e1) / 1e3 / n_e2e], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_e2e, op=dist.ReduceOp.MAX)
+    t_e2e = float(t_e2e[0])
+
+    flops = wl.prefill_flops(w)
+    pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(pk.get("bf16_tflops", 1590.0))
+    peak_kind = "measured (cuBLAS bf16 burst)" if "bf16_tflops" in pk else "fallback"
+    achieved = flops / t_call / 1e12
+    tp = ROOT / "profiles" / "prefill_cta_chunk512.json"
+    traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch") if tp.exists() else None
+    if rank == 0:
+        cpu = None
+        if world == 1:
+            try:
+                from oracle import oracle as O
+                O.build()
+                threads = os.cpu_count() or 1
+                tc = cpu_prefill_time(O, wl, w, threads)
+                cpu = {"value": w.chunk / tc, "unit": PREFILL_UNIT, "cores": threads,
+                       "kind": "port",
+                       "sample": f"1 of the {w.B} sequences (all {w.Hkv} kv heads), CPU "
+                                 "restatement of the causal attention over the dequantised "
+                                 "cache, fp64"}
+            except Exception as e:  # the baseline is reported, never required
+                cpu = {"value": None, "unit": PREFILL_UNIT, "cores": 1, "kind": "port",
+                       "sample": f"failed: {e!r}"[:200]}
+        line = {
+            "metric": PREFILL_METRIC, "value": world * T / t_step, "unit": PREFILL_UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
+            "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int4/bf16 (f16 MMA, f32 accumulate)",
+            "data": "synthetic (seeded N(0,1) K/V/q, 3 key outlier channels x8)",
+            "config": {"workload": f"prefill: B={w.B}/GPU x ({w.hist} cached + {w.chunk} chunk) "
+                                   f"tokens, Hq={w.Hq} Hkv={w.Hkv} D={w.D} G={w.group} "
+                                   f"R={w.residual} INT{w.bits}",
+                       "global_batch": world * w.B, "parallelism": f"sequence-sharded x{world}",
+                       "l2": "compute-bound; the cache (%.0f MB) is read from L2 after the "
+                             "first row tile" % (w.B * w.Hkv * (w.hist + w.chunk) * 136 / 1e6)},
+            "gpu_launches": args.steps,
+            "e2e": {"value": world * T / t_e2e, "unit": PREFILL_UNIT,
+                    "h2d_bytes_per_step": q.numel() * 2, "d2h_bytes_per_step": out.numel() * 2},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": traffic, "kernel": "prefill_cta_kernel<128,4,128,4>",
+                         "flops_per_launch": flops, "kernel_ms": t_call * 1e3},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "prefill":
+        return run_prefill_reference(args) if args.impl == "reference" else run_prefill(args)
     if args.workload == "config3":
         return run_append_reference(args) if args.impl == "reference" else run_append(args)
     if args.impl == "reference":

@@ -428,9 +428,8 @@ int tkv_paged_prefill(const tkv_cache_t* cache, const void* q, int q_dtype, void
   a.num_q_heads = num_q_heads;
   a.grp = num_q_heads / f.n_kv_heads;
   a.total_q = total_q_tokens;
-  const int64_t rows = (int64_t)max_q_tokens * a.grp;
-  if ((rows + 15) / 16 > 0x7fffffff) return TKV_INVALID_ARGUMENT;
-  a.n_rt = (int)((rows + 15) / 16);
+  a.max_q = max_q_tokens;
+  a.n_rt = 0;
   a.alpha = scale * 1.4426950408889634f;
   a.err = err_flag;
   return launch_prefill(a, f.head_dim, f.bits, f.group_size, as_stream(stream));

@@ -299,7 +299,8 @@ struct PrefillArgs {
   const int32_t* seq_lens;
   const int32_t* seq_slots;
   int num_seqs, num_q_heads, grp, total_q;
-  int n_rt;     // 16-row query tiles per (sequence, kv head) for the longest chunk
+  int max_q;    // bound on the query tokens of one sequence
+  int n_rt;     // query-row tiles per (sequence, kv head), set by the launcher
   float alpha;  // scale * log2(e)
   int* err;
 };

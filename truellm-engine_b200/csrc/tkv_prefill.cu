@@ -10,24 +10,24 @@
 // score = scale * q.k, kv head = q head / (Hq/Hkv), max-subtracted softmax,
 // fp32 accumulation.
 //
-// One warp per CTA owns a tile of 16 query rows of one (sequence, kv head):
-// rows rho = i * grp + j (token i, q head j of the kv head's group), so the
-// grp q heads of one kv head share every dequantised K/V fragment.  Per page
-// the warp dequantises keys and values straight into mma.m16n8k16 fragments
-// (the decode kernel's key_frag / value_frag, with the MMA roles swapped:
-// Q is the A operand, the key and value fragments are B operands), so each
-// page's dequantisation serves 16 query rows instead of the decode's grp:
-//   * S = Q K^T: A = Q (16 rows x 16 channels, exact fp16, channels in the
-//     thread's key-code order), B = the page's key fragments (two 8-token
-//     n-tiles); exact fp16 keys as in decode;
-//   * online softmax per row in the exp2 domain, causal mask per row;
-//   * O += P V with V dequantised to fp16(code * step + zero) -- the value the
-//     reference decompress writes -- per token, so values and keys are both
-//     the reference's fp16 numbers; P moves from the S accumulator layout to
-//     the A layout without shuffles.
-// Code words are read with 16-byte loads one page ahead of use (registers),
-// the key-group meta one group ahead; no barrier waits, no shared-memory
-// staging beyond the warp's key-meta slice.
+// A CTA of 4 warps owns 64 query rows of one (sequence, kv head): rows
+// rho = i * grp + j (token i, q head j of the kv head's group), 16 per warp,
+// so the grp q heads of a kv head share every dequantised page.  Per 16-token
+// tile the CTA's threads dequantise the page's codes -- exactly, to the fp16
+// values the reference decompress writes, fp16(code * step + zero) for keys
+// (per channel) and values (per token) -- into a K tile [16][D] and a V^T
+// tile [D][16] in shared memory (double-buffered, one __syncthreads per tile);
+// each warp then runs
+//   * S = Q K^T on mma.m16n8k16 (A = its 16 query rows as exact fp16, B from
+//     the K tile by ldmatrix), causal mask per row;
+//   * online softmax per row in the exp2 domain (lazy rescale, as decode);
+//   * O += P V (P from the S accumulators without shuffles, B from the V^T
+//     tile by ldmatrix).
+// Key channels sit in the tile in the order a code word unpacks into f16
+// pairs ((c, c+4) for 4-bit words, (c, c+8) for 2-bit), and Q is loaded in the
+// same order; ring tiles (the fp16 window) are scattered into that order.
+// The next tile's code words are loaded into registers before the current
+// tile's MMAs, so their latency overlaps them.
 #include "tkv_frag.cuh"
 
 namespace tkv {
@@ -47,7 +47,7 @@ __device__ __forceinline__ void causal_mask(float (&s)[2][4], int t0, int tig, i
   }
 }
 
-template <int D, int NVG>
+template <int D>
 struct RowState {
   float m[2];          // running max (log2 units) of rows g, g+8
   float l[2];          // this lane's partial sums of p
@@ -56,8 +56,8 @@ struct RowState {
 
 // Online-softmax step for one 16-token tile; s holds raw scores on entry
 // (-inf where masked) and the unnormalised weights on return.
-template <int D, int NVG>
-__device__ __forceinline__ void row_softmax(RowState<D, NVG>& st, float (&s)[2][4], float alpha) {
+template <int D>
+__device__ __forceinline__ void row_softmax(RowState<D>& st, float (&s)[2][4], float alpha) {
   float t[2];
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
@@ -100,55 +100,6 @@ __device__ __forceinline__ float load_qv(const PrefillArgs& a, int64_t idx) {
   return __half2float(reinterpret_cast<const __half*>(a.q)[idx]);
 }
 
-// The key-code words of rows g and g+8 (this thread's channel chunk) and the
-// value-code words and per-token value meta of one page, from global memory.
-template <int D, int BITS, int NVG>
-struct PageWords {
-  uint32_t wg[D * BITS / 128], wh[D * BITS / 128];
-  uint32_t vw[D * BITS / 64];
-  uint32_t vm[4][NVG];  // (step, zero) of tokens 2tig, 2tig+1, 2tig+8, 2tig+9
-};
-
-template <int D, int BITS, int G>
-__device__ __forceinline__ void load_page(PageWords<D, BITS, Fmt<D, BITS, G>::NVG>& pw,
-                                          const uint8_t* pg, int lane) {
-  using F = Fmt<D, BITS, G>;
-  const int g = lane >> 2, tig = lane & 3;
-  constexpr int TB = F::RB / 4;  // key-code bytes per thread per row
-  if constexpr (TB == 16) {
-    const uint4 x = __ldg(reinterpret_cast<const uint4*>(pg + g * F::RB + tig * 16));
-    const uint4 y = __ldg(reinterpret_cast<const uint4*>(pg + (g + 8) * F::RB + tig * 16));
-    pw.wg[0] = x.x; pw.wg[1] = x.y; pw.wg[2] = x.z; pw.wg[3] = x.w;
-    pw.wh[0] = y.x; pw.wh[1] = y.y; pw.wh[2] = y.z; pw.wh[3] = y.w;
-  } else if constexpr (TB == 8) {
-    const uint2 x = __ldg(reinterpret_cast<const uint2*>(pg + g * F::RB + tig * 8));
-    const uint2 y = __ldg(reinterpret_cast<const uint2*>(pg + (g + 8) * F::RB + tig * 8));
-    pw.wg[0] = x.x; pw.wg[1] = x.y;
-    pw.wh[0] = y.x; pw.wh[1] = y.y;
-  } else {
-    pw.wg[0] = __ldg(reinterpret_cast<const uint32_t*>(pg + g * F::RB + tig * 4));
-    pw.wh[0] = __ldg(reinterpret_cast<const uint32_t*>(pg + (g + 8) * F::RB + tig * 4));
-  }
-  const uint8_t* vc = pg + F::V_CODES_OFF;
-#pragma unroll
-  for (int v = 0; v < F::VWN / F::VW; ++v) {
-    if constexpr (F::VW == 4) {
-      const uint4 x = __ldg(reinterpret_cast<const uint4*>(vc + (v * 32 + lane) * 16));
-      pw.vw[4 * v + 0] = x.x; pw.vw[4 * v + 1] = x.y; pw.vw[4 * v + 2] = x.z; pw.vw[4 * v + 3] = x.w;
-    } else {
-      const uint2 x = __ldg(reinterpret_cast<const uint2*>(vc + lane * 8));
-      pw.vw[0] = x.x; pw.vw[1] = x.y;
-    }
-  }
-  const uint32_t* vm = reinterpret_cast<const uint32_t*>(pg + F::V_META_OFF);
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int t = 2 * tig + (k & 1) + 8 * (k >> 1);
-#pragma unroll
-    for (int vg = 0; vg < F::NVG; ++vg) pw.vm[k][vg] = __ldg(vm + t * F::NVG + vg);
-  }
-}
-
 // value_frag() registers hold 1024 + c (tokens 2tig, 2tig+1) and 64 + c
 // (tokens 2tig+8, 2tig+9) for 4-bit codes, 1 + c/16 for 2-bit codes; one
 // HFMA2 with these f16x2 constants recovers the integer codes exactly.
@@ -162,18 +113,50 @@ template <> struct VCode<2> {
 
 }  // namespace
 
-#ifndef TKV_PREFILL_MIN_BLOCKS
-#define TKV_PREFILL_MIN_BLOCKS 8  // resident warps per SM the register budget targets
-#endif
+namespace {
 
-template <int D, int BITS, int G>
-__global__ void __launch_bounds__(32, TKV_PREFILL_MIN_BLOCKS) prefill_kernel(PrefillArgs a) {
+__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(p))
+               : "memory");
+}
+
+// Position of key channel c in the shared K tile (inverse of the unpack order).
+template <int BITS>
+__device__ __forceinline__ constexpr int kpos(int c) {
+  return BITS == 4 ? (c & ~7) + 2 * (c & 3) + ((c >> 2) & 1)
+                   : (c & ~15) + 2 * (c & 7) + ((c >> 3) & 1);
+}
+// Key channel at position p of the shared K tile.
+template <int BITS>
+__device__ __forceinline__ constexpr int kchan_at(int p) {
+  return BITS == 4 ? (p & ~7) + ((p & 7) >> 1) + 4 * (p & 1)
+                   : (p & ~15) + ((p & 15) >> 1) + 8 * (p & 1);
+}
+
+}  // namespace
+
+template <int D, int BITS, int G, int NW>
+__global__ void __launch_bounds__(32 * NW, 2) prefill_cta_kernel(PrefillArgs a) {
   using F = Fmt<D, BITS, G>;
-  constexpr int NVG = F::NVG, NKB = F::NKB;
-  __shared__ __align__(16) uint8_t meta[F::META];  // current key group's [D][step, zero]
-  const int lane = threadIdx.x, g = lane >> 2, tig = lane & 3;
+  constexpr int NT = 32 * NW, NKB = D / 16;
+  constexpr int WPR = D * BITS / 32;          // key-code words per token row
+  constexpr int CPW = 32 / BITS;              // channels per key word
+  constexpr int HP = CPW / 2;                 // f16 pairs per key word
+  constexpr int KW = kPage * WPR;             // key (and value) code words per page
+  constexpr int KPT = (KW + NT - 1) / NT;     // code words per thread
+  constexpr int MVEC = CPW / 4;               // 16-byte key-meta vectors per word's channels
+  constexpr int VMW = BITS == 4 ? 4 : 8;      // value (step, zero) words per value word
+  constexpr int RV = 2 * D;                   // 16-byte vectors per ring K (or V) block
+  constexpr int RPT = (RV + NT - 1) / NT;
+  constexpr int KS = D + 8, VS = kPage + 8;   // padded row strides (halves)
+  static_assert(NT % WPR == 0, "a thread's key words share their channels");
+  __shared__ __align__(16) __half Kt[2][kPage][KS];
+  __shared__ __align__(16) __half Vt[2][D][VS];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tig = lane & 3;
 
-  // heavy tiles first: the last row tiles of a chunk see the longest histories
   const int64_t bid = blockIdx.x;
   const int rt = a.n_rt - 1 - (int)(bid % a.n_rt);
   const int bh = (int)(bid / a.n_rt);
@@ -181,213 +164,245 @@ __global__ void __launch_bounds__(32, TKV_PREFILL_MIN_BLOCKS) prefill_kernel(Pre
   const int L = a.seq_lens[b];
   const int q0 = a.cu_q[b], n = a.cu_q[b + 1] - q0;
   if (L < 0 || L > a.max_blocks * kPage || n < 0 || n > L || q0 < 0 || q0 + n > a.total_q) {
-    if (rt == 0 && h == 0 && lane == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
+    if (rt == 0 && h == 0 && tid == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
     return;
   }
-  const int rows = n * a.grp, r0 = rt * 16;
+  const int rows = n * a.grp, r0 = rt * 16 * NW;
   if (r0 >= rows) return;
-  // this lane's rows g and g+8 of the tile: token i, q head j; padded rows
-  // (beyond the chunk) compute with q = 0 and position L-1, and write nothing
-  const int ra = r0 + g, rb = r0 + g + 8;
+  const int ra = r0 + 16 * warp + g, rb = ra + 8;
   const bool va = ra < rows, vb = rb < rows;
   const int ia = va ? ra / a.grp : n - 1, ib = vb ? rb / a.grp : n - 1;
   const int pa = L - n + ia, pb = L - n + ib;
-  const int last_row = min(rows - 1, r0 + 15);
-  const int kv_end = L - n + last_row / a.grp + 1;  // tokens [0, kv_end) are needed
+  const int kv_end = L - n + min(rows - 1, r0 + 16 * NW - 1) / a.grp + 1;
   const int64_t qa = ((int64_t)(q0 + ia) * a.num_q_heads + h * a.grp + (va ? ra % a.grp : 0)) * D;
   const int64_t qb = ((int64_t)(q0 + ib) * a.num_q_heads + h * a.grp + (vb ? rb % a.grp : 0)) * D;
   const int nq = nq_len(L, a.residual, G);
   const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
   const int n_pages = min(nq, (kv_end + kPage - 1) / kPage * kPage) / kPage;
-  const float alpha = a.alpha;
+  const int n_chunks = kv_end > nq ? (kv_end - nq + kPage - 1) / kPage : 0;
+  const int n_tiles = n_pages + n_chunks;
 
-  // every page this tile reads (its pages and the key meta of their whole
-  // groups) must be in range
+  // every page read (the tiles' pages and their groups' key meta) in range
   const int n_read = min(nq / kPage, (n_pages + F::PPG - 1) / F::PPG * F::PPG);
   bool bad = false;
-  for (int p = lane; p < n_read; p += 32) {
+  for (int p = tid; p < n_read; p += NT) {
     const int ph = bt[p];
     bad |= ph < 0 || ph >= a.num_pages;
   }
-  if (__any_sync(0xffffffffu, bad)) {
-    if (lane == 0) set_err(a.err, TKV_ERR_BAD_PAGE);
+  if (__syncthreads_or(bad)) {
+    if (tid == 0) set_err(a.err, TKV_ERR_BAD_PAGE);
     return;
   }
   int row = 0;
-  if (kv_end > nq) {
+  if (n_chunks > 0) {
     row = a.seq_slots ? a.seq_slots[b] : b;
     if (row < 0 || row >= a.max_seqs) {
-      if (lane == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
+      if (tid == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
       return;
     }
   }
 
-  RowState<D, NVG> st;
+  // A operand: this warp's rows g, g+8 as exact f16, channels in tile order
+  uint32_t aq[NKB][4];
+#pragma unroll
+  for (int kb = 0; kb < NKB; ++kb)
+#pragma unroll
+    for (int hi = 0; hi < 2; ++hi) {
+      const int c0 = kchan_at<BITS>(16 * kb + 8 * hi + 2 * tig);
+      const int c1 = kchan_at<BITS>(16 * kb + 8 * hi + 2 * tig + 1);
+      aq[kb][2 * hi + 0] = pack_h2(va ? load_qv(a, qa + c0) : 0.f, va ? load_qv(a, qa + c1) : 0.f);
+      aq[kb][2 * hi + 1] = pack_h2(vb ? load_qv(a, qb + c0) : 0.f, vb ? load_qv(a, qb + c1) : 0.f);
+    }
+
+  const uint8_t* pool_h = a.pool + (int64_t)h * F::PB;
+  const int64_t page_stride = (int64_t)a.n_kv_heads * F::PB;
+  constexpr int CHUNK = 2 * F::RBLK;
+  const uint8_t* ring_base =
+      reinterpret_cast<const uint8_t*>(a.ring) +
+      (((int64_t)row * a.n_kv_heads + h) * (a.ring_cap / kPage)) * CHUNK;
+  const int kc0 = (tid % WPR) * CPW;  // first channel of this thread's key words
+
+  // ---------------- registers of the next tile ----------------
+  uint32_t kw[KPT], vw[KPT], vm[KPT][VMW];
+  uint4 km[MVEC];
+  uint4 rk[RPT], rv[RPT];
+  auto load_tile = [&](int j) {
+    if (j < n_pages) {
+      const uint8_t* pg = pool_h + (int64_t)bt[j] * page_stride;
+#pragma unroll
+      for (int k = 0; k < KPT; ++k) {
+        const int u = tid + k * NT;
+        if (u >= KW) continue;
+        kw[k] = __ldg(reinterpret_cast<const uint32_t*>(pg) + u);
+        const int l = u & 31, w = u >> 5;
+        vw[k] = __ldg(reinterpret_cast<const uint32_t*>(
+            pg + F::V_CODES_OFF + ((w / F::VW) * 32 + l) * 4 * F::VW + (w % F::VW) * 4));
+        const uint32_t* vmp = reinterpret_cast<const uint32_t*>(pg + F::V_META_OFF);
+        const int t0 = 2 * (l & 3);
+#pragma unroll
+        for (int x = 0; x < VMW; ++x) {
+          // 4-bit: tokens t0, t0+1, t0+8, t0+9 of m-block w; 2-bit: the same
+          // for m-blocks 2w (x < 4) and 2w+1
+          const int mb = BITS == 4 ? w : 2 * w + (x >> 2);
+          const int t = t0 + (x & 1) + 8 * ((x >> 1) & 1);
+          vm[k][x] = __ldg(vmp + t * F::NVG + (16 * mb) / G);
+        }
+      }
+      if (j % F::PPG == 0 && tid < KW) {  // a new key group: this thread's channels
+        const int grp = j / F::PPG;
+#pragma unroll
+        for (int v = 0; v < MVEC; ++v) {
+          const int off = 4 * (kc0 + 4 * v);
+          const int ph = bt[grp * F::PPG + off / F::KMS];
+          km[v] = __ldg(reinterpret_cast<const uint4*>(pool_h + (int64_t)ph * page_stride +
+                                                        F::BODY + off % F::KMS));
+        }
+      }
+    } else {
+      const int t0 = nq + (j - n_pages) * kPage;
+      const uint8_t* ck = ring_base + (int64_t)((t0 % a.ring_cap) / kPage) * CHUNK;
+#pragma unroll
+      for (int k = 0; k < RPT; ++k) {
+        const int u = tid + k * NT;
+        if (u >= RV) continue;
+        rk[k] = __ldg(reinterpret_cast<const uint4*>(ck) + u);
+        rv[k] = __ldg(reinterpret_cast<const uint4*>(ck + F::RBLK) + u);
+      }
+    }
+  };
+  auto store_tile = [&](int j, int buf) {
+    if (j < n_pages) {
+      uint32_t mw[CPW];
+#pragma unroll
+      for (int v = 0; v < MVEC; ++v) {
+        mw[4 * v + 0] = km[v].x; mw[4 * v + 1] = km[v].y;
+        mw[4 * v + 2] = km[v].z; mw[4 * v + 3] = km[v].w;
+      }
+      uint32_t sp[HP], zp[HP];
+#pragma unroll
+      for (int i = 0; i < HP; ++i) {
+        sp[i] = __byte_perm(mw[i], mw[i + HP], 0x5410);
+        zp[i] = __byte_perm(mw[i], mw[i + HP], 0x7632);
+      }
+#pragma unroll
+      for (int k = 0; k < KPT; ++k) {
+        const int u = tid + k * NT;
+        if (u >= KW) continue;
+        const uint32_t x = kw[k], x8 = kw[k] >> 8;
+        uint32_t hv[HP];
+#pragma unroll
+        for (int i = 0; i < HP; ++i) {
+          uint32_t c;
+          if (BITS == 4) {
+            c = (i & 1) ? code_pair<0x00F000F0u>(i < 2 ? x : x8)
+                        : code_pair<0x000F000Fu>(i < 2 ? x : x8);
+          } else {
+            const uint32_t y = i < 4 ? x : x8;
+            c = (i & 3) == 0 ? code_pair<0x00030003u>(y)
+              : (i & 3) == 1 ? code_pair<0x000C000Cu>(y)
+              : (i & 3) == 2 ? code_pair<0x00300030u>(y)
+                             : code_pair<0x00C000C0u>(y);
+          }
+          hv[i] = hfma2(c, sp[i], zp[i]);
+        }
+        __half* dst = &Kt[buf][u / WPR][kc0];
+#pragma unroll
+        for (int q = 0; q < HP / 4; ++q)
+          reinterpret_cast<uint4*>(dst)[q] = make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2],
+                                                        hv[4 * q + 3]);
+        // value word (lane l, word w): channels 16mb+gl and 16mb+8+gl, tokens
+        // tl, tl+1, tl+8, tl+9
+        const int l = u & 31, w = u >> 5, gl = l >> 2, tl = 2 * (l & 3);
+#pragma unroll
+        for (int half = 0; half < (BITS == 4 ? 1 : 2); ++half) {
+          const int mb = BITS == 4 ? w : 2 * w + half;
+          const uint32_t* m4 = &vm[k][4 * half];
+          const uint32_t s01 = __byte_perm(m4[0], m4[1], 0x5410), z01 = __byte_perm(m4[0], m4[1], 0x7632);
+          const uint32_t s89 = __byte_perm(m4[2], m4[3], 0x5410), z89 = __byte_perm(m4[2], m4[3], 0x7632);
+          uint32_t r[4];
+          if (BITS == 4 || half == 0)
+            value_frag<BITS, 0>(&vw[k], r);
+          else
+            value_frag<BITS, (BITS == 2 ? 1 : 0)>(&vw[k], r);
+          const uint32_t v0 = hfma2(hfma2(r[0], VCode<BITS>::kMul, VCode<BITS>::kAddLo), s01, z01);
+          const uint32_t v1 = hfma2(hfma2(r[1], VCode<BITS>::kMul, VCode<BITS>::kAddLo), s01, z01);
+          const uint32_t v2 = hfma2(hfma2(r[2], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
+          const uint32_t v3 = hfma2(hfma2(r[3], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
+          *reinterpret_cast<uint32_t*>(&Vt[buf][16 * mb + gl][tl]) = v0;
+          *reinterpret_cast<uint32_t*>(&Vt[buf][16 * mb + 8 + gl][tl]) = v1;
+          *reinterpret_cast<uint32_t*>(&Vt[buf][16 * mb + gl][tl + 8]) = v2;
+          *reinterpret_cast<uint32_t*>(&Vt[buf][16 * mb + 8 + gl][tl + 8]) = v3;
+        }
+      }
+    } else {
+      const int t0 = nq + (j - n_pages) * kPage;
+#pragma unroll
+      for (int k = 0; k < RPT; ++k) {
+        const int u = tid + k * NT;
+        if (u >= RV) continue;
+        const int c16 = u >> 5, l = u & 31;
+        const uint32_t kx[4] = {rk[k].x, rk[k].y, rk[k].z, rk[k].w};
+        const uint32_t vx[4] = {rv[k].x, rv[k].y, rv[k].z, rv[k].w};
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          // K block: word r holds channels cc, cc+1 of token t
+          const int t = 8 * (r & 1) + (l >> 2), cc = 8 * (r >> 1) + 2 * (l & 3);
+          const int c = 16 * c16 + cc;
+          Kt[buf][t][kpos<BITS>(c)] = __ushort_as_half(static_cast<unsigned short>(kx[r] & 0xffffu));
+          Kt[buf][t][kpos<BITS>(c + 1)] = __ushort_as_half(static_cast<unsigned short>(kx[r] >> 16));
+          // V block: word r holds tokens tv, tv+1 of channel 16c16 + cv; tokens
+          // past the end (stale ring slots) become 0
+          const int tv = 8 * (r >> 1) + 2 * (l & 3), cv = 8 * (r & 1) + (l >> 2);
+          const uint32_t msk = (t0 + tv < L ? 0x0000ffffu : 0u) | (t0 + tv + 1 < L ? 0xffff0000u : 0u);
+          *reinterpret_cast<uint32_t*>(&Vt[buf][16 * c16 + cv][tv]) = vx[r] & msk;
+        }
+      }
+    }
+  };
+
+  RowState<D> st;
   st.m[0] = st.m[1] = -INFINITY;
   st.l[0] = st.l[1] = 0.f;
 #pragma unroll
   for (int nt = 0; nt < D / 8; ++nt) st.o[nt][0] = st.o[nt][1] = st.o[nt][2] = st.o[nt][3] = 0.f;
+  const float alpha = a.alpha;
+  const int mi = lane >> 3, mr = lane & 7;
 
-  const uint8_t* pool_h = a.pool + (int64_t)h * F::PB;
-  const int64_t page_stride = (int64_t)a.n_kv_heads * F::PB;
-
-  // =================== quantised pages ===================
-  if (n_pages > 0) {
-    // A operand: q rows g, g+8 as exact f16, channels in the thread's key-code order
-    uint32_t aq[NKB][4];
+  load_tile(0);
+  store_tile(0, 0);
+  __syncthreads();
+  for (int j = 0; j < n_tiles; ++j) {
+    const int buf = j & 1;
+    if (j + 1 < n_tiles) load_tile(j + 1);  // in flight during this tile's MMAs
+    // ---- S = Q K^T over the tile's 16 tokens ----
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-    for (int kb = 0; kb < NKB; ++kb)
-#pragma unroll
-      for (int hi = 0; hi < 2; ++hi) {
-        const int c0 = tig * F::CH + kchan<BITS>(kb, hi, 0);
-        const int c1 = tig * F::CH + kchan<BITS>(kb, hi, 1);
-        aq[kb][2 * hi + 0] = pack_h2(va ? load_qv(a, qa + c0) : 0.f, va ? load_qv(a, qa + c1) : 0.f);
-        aq[kb][2 * hi + 1] = pack_h2(vb ? load_qv(a, qb + c0) : 0.f, vb ? load_qv(a, qb + c1) : 0.f);
-      }
-    // key-group meta: META bytes from the group's PPG pages, one 16-byte
-    // vector per lane (lanes beyond META / 16 idle), a group ahead
-    constexpr int MV = F::META / 16;
-    static_assert(MV <= 32, "key meta of a group fits one vector per lane");
-    auto load_meta = [&](int grp) {
-      uint4 x = make_uint4(0, 0, 0, 0);
-      if (lane < MV) {
-        const int slice = lane * 16 / F::KMS, off = lane * 16 % F::KMS;
-        const int ph = bt[grp * F::PPG + slice];
-        x = __ldg(reinterpret_cast<const uint4*>(pool_h + ph * page_stride + F::BODY + off));
-      }
-      return x;
-    };
-    const int ngroups = n_pages / F::PPG + (n_pages % F::PPG ? 1 : 0);
-    uint4 mnext = load_meta(0);
-    PageWords<D, BITS, NVG> cur, nxt;
-    load_page<D, BITS, G>(cur, pool_h + bt[0] * page_stride, lane);
-    int pgi = 0;
-    for (int grp = 0; grp < ngroups; ++grp) {
-      __syncwarp();
-      if (lane < MV) reinterpret_cast<uint4*>(meta)[lane] = mnext;
-      __syncwarp();
-      if (grp + 1 < ngroups) mnext = load_meta(grp + 1);
-      uint32_t ks[NKB][2], kz[NKB][2];
-      const uint32_t* mwords = reinterpret_cast<const uint32_t*>(meta);
-#pragma unroll
-      for (int kb = 0; kb < NKB; ++kb)
-#pragma unroll
-        for (int hi = 0; hi < 2; ++hi) {
-          const uint32_t m0 = mwords[tig * F::CH + kchan<BITS>(kb, hi, 0)];
-          const uint32_t m1 = mwords[tig * F::CH + kchan<BITS>(kb, hi, 1)];
-          ks[kb][hi] = __byte_perm(m0, m1, 0x5410);
-          kz[kb][hi] = __byte_perm(m0, m1, 0x7632);
-        }
-      const int pend = min(n_pages, (grp + 1) * F::PPG);
-      for (; pgi < pend; ++pgi) {
-        if (pgi + 1 < n_pages) load_page<D, BITS, G>(nxt, pool_h + bt[pgi + 1] * page_stride, lane);
-        // ---- S = Q K^T over the page's 16 tokens (two 8-token n-tiles) ----
-        float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-        for (int kb = 0; kb < NKB; ++kb) {
-          uint32_t r[4];
-          switch (kb) {
-#define TKV_KF(K)                                                                            \
-  case K:                                                                                    \
-    key_frag<BITS, (K < NKB ? K : 0)>(cur.wg, cur.wh, ks[K < NKB ? K : 0], kz[K < NKB ? K : 0], \
-                                      r);                                                    \
-    break;
-            TKV_KF(0) TKV_KF(1) TKV_KF(2) TKV_KF(3) TKV_KF(4) TKV_KF(5) TKV_KF(6) TKV_KF(7)
-#undef TKV_KF
-          }
-          mma16816(s[0], aq[kb][0], aq[kb][1], aq[kb][2], aq[kb][3], r[0], r[2]);
-          mma16816(s[1], aq[kb][0], aq[kb][1], aq[kb][2], aq[kb][3], r[1], r[3]);
-        }
-        const int t0 = pgi * kPage;
-        if (t0 + kPage - 1 > min(pa, pb)) causal_mask(s, t0, tig, pa, pb);
-        row_softmax<D, NVG>(st, s, alpha);
-        // ---- O += P V with V = fp16(code * step + zero), the reference
-        //      decompress value, per token (step, zero) ----
-        const uint32_t a0 = pack_h2(s[0][0], s[0][1]);  // row g,   tokens 2tig, 2tig+1
-        const uint32_t a1 = pack_h2(s[0][2], s[0][3]);  // row g+8
-        const uint32_t a2 = pack_h2(s[1][0], s[1][1]);  // row g,   tokens 2tig+8, 2tig+9
-        const uint32_t a3 = pack_h2(s[1][2], s[1][3]);  // row g+8
-#pragma unroll
-        for (int vg = 0; vg < NVG; ++vg) {
-          const uint32_t s01 = __byte_perm(cur.vm[0][vg], cur.vm[1][vg], 0x5410);
-          const uint32_t z01 = __byte_perm(cur.vm[0][vg], cur.vm[1][vg], 0x7632);
-          const uint32_t s89 = __byte_perm(cur.vm[2][vg], cur.vm[3][vg], 0x5410);
-          const uint32_t z89 = __byte_perm(cur.vm[2][vg], cur.vm[3][vg], 0x7632);
-#pragma unroll
-          for (int k = 0; k < F::MB_PER_VG; ++k) {
-            const int mb = vg * F::MB_PER_VG + k;
-            uint32_t r[4];
-            switch (mb) {
-#define TKV_VF(M)                                      \
-  case M:                                              \
-    value_frag<BITS, (M < D / 16 ? M : 0)>(cur.vw, r); \
-    break;
-              TKV_VF(0) TKV_VF(1) TKV_VF(2) TKV_VF(3) TKV_VF(4) TKV_VF(5) TKV_VF(6) TKV_VF(7)
-#undef TKV_VF
-            }
-            // registers 0, 1 hold tokens 2tig, 2tig+1; registers 2, 3 tokens 2tig+8, 2tig+9
-            const uint32_t v0 = hfma2(hfma2(r[0], VCode<BITS>::kMul, VCode<BITS>::kAddLo), s01, z01);
-            const uint32_t v1 = hfma2(hfma2(r[1], VCode<BITS>::kMul, VCode<BITS>::kAddLo), s01, z01);
-            const uint32_t v2 = hfma2(hfma2(r[2], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
-            const uint32_t v3 = hfma2(hfma2(r[3], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
-            mma16816(st.o[2 * mb], a0, a1, a2, a3, v0, v2);      // channels 16mb .. 16mb+7
-            mma16816(st.o[2 * mb + 1], a0, a1, a2, a3, v1, v3);  // channels 16mb+8 .. 16mb+15
-          }
-        }
-        cur = nxt;
-      }
+    for (int kb = 0; kb < NKB; ++kb) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(&Kt[buf][(mi >> 1) * 8 + mr][16 * kb + (mi & 1) * 8], b0, b1, b2, b3);
+      mma16816(s[0], aq[kb][0], aq[kb][1], aq[kb][2], aq[kb][3], b0, b1);
+      mma16816(s[1], aq[kb][0], aq[kb][1], aq[kb][2], aq[kb][3], b2, b3);
     }
+    const int t0 = j < n_pages ? j * kPage : nq + (j - n_pages) * kPage;
+    if (t0 + kPage - 1 > min(pa, pb)) causal_mask(s, t0, tig, pa, pb);
+    row_softmax<D>(st, s, alpha);
+    // ---- O += P V ----
+    const uint32_t a0 = pack_h2(s[0][0], s[0][1]);
+    const uint32_t a1 = pack_h2(s[0][2], s[0][3]);
+    const uint32_t a2 = pack_h2(s[1][0], s[1][1]);
+    const uint32_t a3 = pack_h2(s[1][2], s[1][3]);
+#pragma unroll
+    for (int mb = 0; mb < D / 16; ++mb) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(&Vt[buf][16 * mb + (mi >> 1) * 8 + mr][(mi & 1) * 8], b0, b1, b2, b3);
+      mma16816(st.o[2 * mb], a0, a1, a2, a3, b0, b1);
+      mma16816(st.o[2 * mb + 1], a0, a1, a2, a3, b2, b3);
+    }
+    if (j + 1 < n_tiles) store_tile(j + 1, buf ^ 1);
+    __syncthreads();
   }
 
-  // =================== fp16 ring: tokens [nq, kv_end) ===================
-  if (kv_end > nq) {
-    constexpr int CHUNK = 2 * F::RBLK;
-    const int64_t chunks_per_row = a.ring_cap / kPage;
-    const uint8_t* ring_base = reinterpret_cast<const uint8_t*>(a.ring) +
-                               (((int64_t)row * a.n_kv_heads + h) * chunks_per_row) * CHUNK;
-    // A operand in natural channel order (the ring's fragment layout)
-    uint32_t aq[NKB][4];
-#pragma unroll
-    for (int kb = 0; kb < NKB; ++kb)
-#pragma unroll
-      for (int hi = 0; hi < 2; ++hi) {
-        const int c = 16 * kb + 2 * tig + 8 * hi;
-        aq[kb][2 * hi + 0] = pack_h2(va ? load_qv(a, qa + c) : 0.f, va ? load_qv(a, qa + c + 1) : 0.f);
-        aq[kb][2 * hi + 1] = pack_h2(vb ? load_qv(a, qb + c) : 0.f, vb ? load_qv(a, qb + c + 1) : 0.f);
-      }
-    const int n_chunks = (kv_end - nq + kPage - 1) / kPage;
-    for (int ci = 0; ci < n_chunks; ++ci) {
-      const int t0 = nq + ci * kPage;
-      const uint8_t* ck =
-          ring_base + (int64_t)((t0 % a.ring_cap) / kPage) * CHUNK;
-      const uint8_t* cv = ck + F::RBLK;
-      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-      for (int kb = 0; kb < NKB; ++kb) {
-        const uint4 x = __ldg(reinterpret_cast<const uint4*>(ck + (kb * 32 + lane) * 16));
-        mma16816(s[0], aq[kb][0], aq[kb][1], aq[kb][2], aq[kb][3], x.x, x.z);
-        mma16816(s[1], aq[kb][0], aq[kb][1], aq[kb][2], aq[kb][3], x.y, x.w);
-      }
-      causal_mask(s, t0, tig, pa, pb);  // also covers stale slots: tokens >= L > p
-      row_softmax<D, NVG>(st, s, alpha);
-      const uint32_t a0 = pack_h2(s[0][0], s[0][1]);
-      const uint32_t a1 = pack_h2(s[0][2], s[0][3]);
-      const uint32_t a2 = pack_h2(s[1][0], s[1][1]);
-      const uint32_t a3 = pack_h2(s[1][2], s[1][3]);
-      // zero the values of tokens past the end (stale ring slots)
-      const int tt = t0 + 2 * tig;
-      const uint32_t m01 = (tt < L ? 0x0000ffffu : 0u) | (tt + 1 < L ? 0xffff0000u : 0u);
-      const uint32_t m23 = (tt + 8 < L ? 0x0000ffffu : 0u) | (tt + 9 < L ? 0xffff0000u : 0u);
-#pragma unroll
-      for (int mb = 0; mb < D / 16; ++mb) {
-        const uint4 x = __ldg(reinterpret_cast<const uint4*>(cv + (mb * 32 + lane) * 16));
-        mma16816(st.o[2 * mb], a0, a1, a2, a3, x.x & m01, x.z & m23);
-        mma16816(st.o[2 * mb + 1], a0, a1, a2, a3, x.y & m01, x.w & m23);
-      }
-    }
-  }
-
-  // =================== normalise and write ===================
+  // ---- normalise and write this warp's rows ----
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     st.l[r] += __shfl_xor_sync(0xffffffffu, st.l[r], 1);
@@ -414,33 +429,38 @@ __global__ void __launch_bounds__(32, TKV_PREFILL_MIN_BLOCKS) prefill_kernel(Pre
   }
 }
 
+constexpr int kPrefillWarps = 4;  // 16 query rows each: 64 rows per CTA
+
 template <int D, int BITS, int G>
-static int launch_prefill_t(const PrefillArgs& a, int64_t blocks, cudaStream_t stream) {
-  prefill_kernel<D, BITS, G><<<(unsigned)blocks, 32, 0, stream>>>(a);
+static int launch_prefill_t(PrefillArgs a, cudaStream_t stream) {
+  constexpr int NW = kPrefillWarps;
+  const int64_t tiles = ((int64_t)a.max_q * a.grp + 16 * NW - 1) / (16 * NW);
+  const int64_t blocks = (int64_t)a.num_seqs * a.n_kv_heads * tiles;
+  if (blocks <= 0) return TKV_OK;
+  if (blocks > 0x7fffffffLL) return TKV_INVALID_ARGUMENT;
+  a.n_rt = (int)tiles;
+  prefill_cta_kernel<D, BITS, G, NW><<<(unsigned)blocks, 32 * NW, 0, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
 }
 
 template <int D, int BITS>
-static int launch_prefill_g(const PrefillArgs& a, int G, int64_t blocks, cudaStream_t stream) {
+static int launch_prefill_g(const PrefillArgs& a, int G, cudaStream_t stream) {
   switch (G) {
-    case 16: return launch_prefill_t<D, BITS, 16>(a, blocks, stream);
-    case 32: return launch_prefill_t<D, BITS, 32>(a, blocks, stream);
-    case 64: return launch_prefill_t<D, BITS, 64>(a, blocks, stream);
-    case 128: return launch_prefill_t<D, BITS, 128>(a, blocks, stream);
+    case 16: return launch_prefill_t<D, BITS, 16>(a, stream);
+    case 32: return launch_prefill_t<D, BITS, 32>(a, stream);
+    case 64: return launch_prefill_t<D, BITS, 64>(a, stream);
+    case 128: return launch_prefill_t<D, BITS, 128>(a, stream);
     default: return TKV_NOT_IMPLEMENTED;
   }
 }
 
 int launch_prefill(const PrefillArgs& a, int head_dim, int bits, int group, cudaStream_t stream) {
-  const int64_t blocks = (int64_t)a.num_seqs * a.n_kv_heads * a.n_rt;
-  if (blocks <= 0) return TKV_OK;
-  if (blocks > 0x7fffffffLL) return TKV_INVALID_ARGUMENT;
   if (head_dim == 128)
-    return bits == 4 ? launch_prefill_g<128, 4>(a, group, blocks, stream)
-                     : launch_prefill_g<128, 2>(a, group, blocks, stream);
+    return bits == 4 ? launch_prefill_g<128, 4>(a, group, stream)
+                     : launch_prefill_g<128, 2>(a, group, stream);
   if (head_dim == 64)
-    return bits == 4 ? launch_prefill_g<64, 4>(a, group, blocks, stream)
-                     : launch_prefill_g<64, 2>(a, group, blocks, stream);
+    return bits == 4 ? launch_prefill_g<64, 4>(a, group, stream)
+                     : launch_prefill_g<64, 2>(a, group, stream);
   return TKV_NOT_IMPLEMENTED;
 }
 

@@ -208,6 +208,48 @@ def append_algorithmic_bytes(w: AppendWorkload) -> int:
     return w.B * H * per_head
 
 
+@dataclass
+class PrefillWorkload:
+    """Chunked prefill: each sequence has `hist` cached tokens and appends a
+    `chunk`-token prompt chunk whose query rows then attend causally to the
+    whole cache (one attention layer)."""
+    name: str
+    B: int
+    hist: int
+    chunk: int
+    Hq: int
+    Hkv: int
+    D: int
+    group: int
+    residual: int
+    bits: int
+    block_tables: np.ndarray  # [B, ceil((hist + chunk) / 16)] int32
+    num_pages: int
+    outlier_channels: np.ndarray
+    outlier_scale: float
+    seed: int
+
+
+def prefill(seed: int = 6, B: int = 8, hist: int = 4096, chunk: int = 512) -> PrefillWorkload:
+    """Llama-3-8B heads (Hq=32, Hkv=8, D=128), KIVI INT4 G=R=128: B sequences
+    of `hist` cached tokens plus a `chunk`-token chunk; pages from a shared
+    pool (+10% slack) in random order, 3 key outlier channels x8."""
+    rng = np.random.default_rng(seed)
+    lengths = np.full(B, hist + chunk, np.int32)
+    num_pages = int(B * (-(-(hist + chunk) // PAGE)) * 1.1) + 1
+    bt = random_block_tables(lengths, num_pages, rng)
+    outl = np.sort(rng.choice(128, size=3, replace=False))
+    return PrefillWorkload("prefill", B, hist, chunk, 32, 8, 128, 128, 128, 4, bt, num_pages,
+                           outl, 8.0, seed)
+
+
+def prefill_flops(w: PrefillWorkload) -> float:
+    """QK^T and PV multiply-adds of the causal chunk: 4 * D * Hq per (query
+    row, attended token), summed over the chunk's positions."""
+    ctx = sum(w.hist + i + 1 for i in range(w.chunk))
+    return 4.0 * w.D * w.Hq * w.B * ctx
+
+
 def decode_algorithmic_bytes(w: DecodeWorkload) -> int:
     """HBM bytes one decode step must move (per-unit figures in DESIGN.md):
     per quantised token-head  2*D*b/8 codes + 4*ceil(D/G) value meta + 4*D/G key
