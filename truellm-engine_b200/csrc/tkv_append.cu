@@ -184,13 +184,15 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
     __syncthreads();
   }
 
-  // clamp(rint(y), 0, QMAX) of the reference: the unsigned round-to-nearest
-  // conversion saturates negatives (and NaN) to 0, the min caps the top
   // clamp(rint((x - gmin) * scale), 0, QMAX) of the reference with
-  // p = (-gmin, scale): x - gmin as x + (-gmin); the unsigned round-to-nearest
-  // conversion saturates negatives (and NaN) to 0, the min caps the top
+  // p = (-gmin, scale), x - gmin as x + (-gmin).  The unsigned round-to-nearest
+  // conversion saturates negatives and NaN to 0.  The top clamp never binds:
+  // for finite values in [gmin, gmax], fl(x - gmin) <= fl(gmax - gmin) = range
+  // (rounding is monotonic) and scale = fl(QMAX / range), so the product is at
+  // most QMAX * (1 + 2^-24)^2 and rounds to QMAX; with an infinite extreme the
+  // range is infinite, scale is 0 and every product is 0 or NaN.
   auto code = [&](float x, float2 p) {
-    return min(__float2uint_rn(__fmul_rn(__fadd_rn(x, p.x), p.y)), static_cast<uint32_t>(QMAX));
+    return __float2uint_rn(__fmul_rn(__fadd_rn(x, p.x), p.y));
   };
   auto page_base = [&](int pi) -> uint8_t* {
     const int ph = S.phys[pi];
