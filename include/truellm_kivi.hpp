@@ -158,6 +158,18 @@ class PagedKiviCache {
     return tkv_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, max_context_len);
   }
 
+  // Chunked prefill (the reference's token-by-token prefill, cuda_engine.cpp:842-860):
+  // each sequence's last cu_q[s+1]-cu_q[s] tokens attend causally to the cache.
+  void prefill(const void* q, int q_dtype, void* out, int out_dtype, const int32_t* cu_q,
+               const int32_t* block_tables, int max_blocks_per_seq, const int32_t* seq_lens,
+               const int32_t* seq_slots, int num_seqs, int num_q_heads, int total_q_tokens,
+               int max_q_tokens, float scale, int* err_flag, cudaStream_t stream) const {
+    throw_on(tkv_paged_prefill(&c_, q, q_dtype, out, out_dtype, cu_q, block_tables,
+                               max_blocks_per_seq, seq_lens, seq_slots, num_seqs, num_q_heads,
+                               total_q_tokens, max_q_tokens, scale, err_flag, stream),
+             "PagedKiviCache::prefill");
+  }
+
   // The paged_attention_v1/v2 slot (cuda_engine.cpp:1137-1159).
   void decode(const void* q, int q_dtype, void* out, int out_dtype, const int32_t* block_tables,
               int max_blocks_per_seq, const int32_t* seq_lens, const int32_t* seq_slots,

@@ -71,6 +71,14 @@ int main() {
   }
   CHECK(threw);
   threw = false;
+  try {  // prefill with a null pool: rejected before any launch
+    cache.prefill(nullptr, TKV_BF16, nullptr, TKV_BF16, nullptr, nullptr, 1, nullptr, nullptr, 1,
+                  32, 4, 4, 0.1f, nullptr, nullptr);
+  } catch (const std::invalid_argument&) {
+    threw = true;
+  }
+  CHECK(threw);
+  threw = false;
   try {
     kb::PagedKiviCache::format(96, 128, 128, 4, 8);
   } catch (const std::exception&) {

@@ -7,7 +7,8 @@
 * A serving loop on KiviCacheAllocator (2 layers): prefill, one-token decode
   steps, a fork (copy_sequence) whose two sequences then diverge, an
   eviction to pinned host and a reload onto other pages, a free whose pages
-  are reused by a new sequence.  At checkpoints every live sequence's pages
+  are reused by a new sequence; each new sequence's prefill attention is
+  checked against the oracle.  At checkpoints every live sequence's pages
   equal, byte for byte, the oracle's pages for the same token history
   appended in one call, and decode attention through the allocator's tables
   and ring rows matches the oracle within 2e-3.
@@ -141,9 +142,36 @@ class Loop:
         return self.wl.to_bits(k, "bf16"), self.wl.to_bits(v, "bf16")
 
     def add(self, sid, n):
+        """A new sequence: its prompt appended, then its prefill attention
+        (every prompt row over the cache) checked against the oracle."""
         assert self.alloc.allocate_sequence(sid, 0)
         self.hist[sid] = [([], []) for _ in range(self.layers)]
         self.append({sid: n})
+        self.check_prefill(sid, n)
+
+    def check_prefill(self, sid, n):
+        f = self.fmt
+        bt_h, lens, rows = self.alloc.pages.block_tables([sid])
+        bt, lens_d, rows_d = self.alloc.get_device_block_tables([sid])
+        scale = 1 / math.sqrt(f.head_dim)
+        cu_q = torch.tensor([0, n], dtype=torch.int32, device=self.cuda)
+        for layer in range(self.layers):
+            q = torch.from_numpy(self.wl.f32_to_bf16_bits(
+                self.rng.standard_normal((n, self.Hq, f.head_dim))).view(np.int16)).view(
+                torch.bfloat16).to(self.cuda)
+            out = self.ops.paged_prefill(self.alloc.caches[layer], q, cu_q, bt, lens_d,
+                                         max_q_tokens=n, scale=scale, seq_slots=rows_d,
+                                         out_dtype=torch.float32, err=self.err)
+            kb = np.concatenate(self.hist[sid][layer][0])
+            vb = np.concatenate(self.hist[sid][layer][1])
+            npg = (len(kb) + 15) // 16 + 1
+            st = self.O.PagedState(f.head_dim, f.group_size, f.residual, f.bits, f.n_kv_heads,
+                                   npg, 1)
+            tbl = np.arange(npg, dtype=np.int32)[None, :]
+            st.append(kb, vb, True, np.array([0, len(kb)], np.int32), np.zeros(1, np.int32), tbl)
+            ref = st.prefill(q.float().cpu().numpy(), np.array([0, n], np.int32), tbl,
+                             np.array([len(kb)], np.int32), scale)
+            check_close(out.cpu().numpy(), ref)
 
     def append(self, counts):
         ids = sorted(counts)
