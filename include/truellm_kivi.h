@@ -289,8 +289,8 @@ TKV_API int tkv_paged_decode_range(const tkv_cache_t* cache, const void* q, int 
  * attends causally to tokens [0, p] with the decode's math and kv-head
  * mapping.  q: [total_q_tokens, num_q_heads, D] fp16 or bf16; out: same
  * shape, fp16, bf16 or f32, 16-byte aligned.  max_q_tokens bounds n_s (it
- * sizes the grid).  Sequences with n_s > seq_lens[s] are skipped and flagged
- * TKV_ERR_BAD_LENGTH.  One launch, no workspace. */
+ * sizes the grid).  Sequences with n_s > seq_lens[s] or n_s > max_q_tokens
+ * are skipped and flagged TKV_ERR_BAD_LENGTH.  One launch, no workspace. */
 TKV_API int tkv_paged_prefill(const tkv_cache_t* cache, const void* q, int q_dtype, void* out,
                               int out_dtype, const int32_t* cu_q, const int32_t* block_tables,
                               int max_blocks_per_seq, const int32_t* seq_lens,

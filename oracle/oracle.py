@@ -21,12 +21,13 @@ REF_LIB = HERE / "_ref" / "libkivi_ref.so"
 _o = None
 
 
-def build(ref: bool = False) -> None:
-    """Compile the oracle (and the reference TU when ref=True and the reference
-    tree is present)."""
+def build(ref_root: str | None = None) -> None:
+    """Compile the oracle and, when ref_root names the truellm-engine source
+    tree, the reference's own kivi_cache.cu into _ref/ (the checker)."""
     subprocess.run(["make", "-s", "-C", os.fspath(HERE), "liboracle.so"], check=True)
-    if ref:
-        subprocess.run(["make", "-s", "-C", os.fspath(HERE), "ref"], check=True)
+    if ref_root:
+        subprocess.run(["make", "-s", "-C", os.fspath(HERE), "ref", f"REF_ROOT={ref_root}"],
+                       check=True)
 
 
 class Fmt(C.Structure):

@@ -109,3 +109,21 @@ def test_prefill_rejects_chunks_longer_than_the_sequence(ops, wl, cuda):
     torch.cuda.synchronize()
     assert int(err.item()) & 0x4
     assert torch.all(out[4:] == 7.0)     # the bad sequence's rows are untouched
+
+
+def test_prefill_flags_chunks_longer_than_max_q_tokens(ops, wl, cuda):
+    """max_q_tokens sizes the grid: a chunk longer than it is flagged and its
+    rows left untouched instead of being partly computed."""
+    fmt = ops.KiviFormat(128, 128, 128, 4, 2)
+    cache = ops.KiviPagedCache(fmt, 16, 2, cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    q = torch.zeros((12, 8, 128), dtype=torch.bfloat16, device=cuda)
+    bt = torch.zeros((2, 8), dtype=torch.int32, device=cuda)
+    out = torch.full((12, 8, 128), 7.0, dtype=torch.float32, device=cuda)
+    ops.paged_prefill(cache, q, torch.tensor([0, 3, 12], dtype=torch.int32, device=cuda), bt,
+                      torch.tensor([3, 40], dtype=torch.int32, device=cuda), max_q_tokens=4,
+                      out=out, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & 0x4
+    assert torch.all(out[3:] == 7.0)     # the 9-token chunk's rows are untouched
+    assert torch.all(out[:3] != 7.0)     # the 3-token chunk was computed

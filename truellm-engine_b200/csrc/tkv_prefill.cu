@@ -163,7 +163,10 @@ __global__ void __launch_bounds__(32 * NW, 2) prefill_cta_kernel(PrefillArgs a) 
   const int b = bh / a.n_kv_heads, h = bh - b * a.n_kv_heads;
   const int L = a.seq_lens[b];
   const int q0 = a.cu_q[b], n = a.cu_q[b + 1] - q0;
-  if (L < 0 || L > a.max_blocks * kPage || n < 0 || n > L || q0 < 0 || q0 + n > a.total_q) {
+  // n > max_q: the grid has row tiles for max_q tokens only, so the chunk's
+  // later rows would stay unwritten; flag the sequence instead
+  if (L < 0 || L > a.max_blocks * kPage || n < 0 || n > L || n > a.max_q || q0 < 0 ||
+      q0 + n > a.total_q) {
     if (rt == 0 && h == 0 && tid == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
     return;
   }

@@ -251,9 +251,10 @@ def prefill_flops(w: PrefillWorkload) -> float:
 
 
 def decode_algorithmic_bytes(w: DecodeWorkload) -> int:
-    """HBM bytes one decode step must move (per-unit figures in DESIGN.md):
-    per quantised token-head  2*D*b/8 codes + 4*ceil(D/G) value meta + 4*D/G key
-    meta, per residual token-head 4*D, plus q, out (2 B each) and block tables."""
+    """HBM bytes one decode step must move: per quantised token-head
+    2*D*b/8 codes + 4*ceil(D/G) value meta + 4*D/G key meta (136 B at D=128,
+    G=128, INT4), per residual token-head 4*D (fp16 K and V), plus q, out
+    (2 B each) and the block tables (4 B per 16-token page)."""
     D, G, R, b, H = w.D, w.group, w.residual, w.bits, w.Hkv
     nvg = -(-D // G)
     total = 0
