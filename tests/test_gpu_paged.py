@@ -285,3 +285,22 @@ def test_seq_slots_indirection(ops, O, wl, cuda):
                                seq_slots=i32([1, 0], cuda))
     torch.cuda.synchronize()
     assert torch.equal(base, swapped)
+
+
+def test_sequence_longer_than_max_context_len_is_flagged(ops, O, wl, cuda):
+    """max_context_len bounds seq_lens: a longer sequence is reported with
+    TKV_ERR_BAD_LENGTH and gets a zero output instead of a silently truncated
+    one; the other sequences of the call are unaffected."""
+    lengths = [900, 300, 2000]
+    tw, bt, lengths, rng = _build(ops, O, wl, cuda, 128, 128, 128, 4, 8, lengths, "bf16",
+                                  seed=12)
+    q = bits_to_torch(wl.f32_to_bf16_bits(rng.standard_normal((3, 32, 128))), "bf16", cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    scale = 1 / math.sqrt(128)
+    out = ops.paged_decode(tw.gpu, q, i32(bt, cuda), i32(lengths, cuda), 1000, scale=scale,
+                           out_dtype=torch.float32, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & 0x4
+    assert torch.all(out[2] == 0)
+    ref = tw.cpu.decode(q.float().cpu().numpy()[:2], bt[:2], lengths[:2], scale, n_threads=8)
+    check_close(out[:2].cpu().numpy(), ref)

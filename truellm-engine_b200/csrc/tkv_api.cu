@@ -1,6 +1,7 @@
 // tkv_api.cu -- the extern "C" boundary declared in include/truellm_kivi.h:
 // argument validation, format math, kernel launches and kernel manifests.
 // Nothing here allocates device memory or synchronises the host.
+#include <limits.h>
 #include <math.h>
 #include <string.h>
 
@@ -222,49 +223,15 @@ int tkv_decode_num_splits(int max_context_len) {
   return (max_context_len + TKV_SPLIT_TOKENS - 1) / TKV_SPLIT_TOKENS + 1;
 }
 
-// Workspace layout: [work counters, 256 B][per-(sequence, kv head) counters,
-// num_seqs * num_q_heads * 4 B rounded up to 256 (num_q_heads bounds the kv
-// heads)][part_ml][part_o].  Counters must be zero before the first call and
-// every call leaves them zero.
-static constexpr size_t kWorkBytes = 256;
-
-static size_t pair_counter_bytes(int num_seqs, int num_q_heads) {
-  return ((size_t)num_seqs * (size_t)num_q_heads * 4 + 255) / 256 * 256;
-}
-
-// Split granularity of a decode launch over n_coarse 512-token splits: 128-token
-// splits when even num_seqs * num_q_heads * n_coarse (an upper bound of the
-// 512-token work items, reached at one q head per kv head) is below 8 items
-// per resident warp, i.e. when the 512-token items certainly leave resident
-// warps idle; decided from the call's sizes alone (the same rule in the
-// workspace queries and the launches), with the B200 count of 148 SMs x 12
-// resident warps.
-static int split_pages_for(int num_seqs, int num_q_heads, int n_coarse) {
-  constexpr long long kResidentWarps = 148LL * 12;
-  const long long units = (long long)num_seqs * num_q_heads * n_coarse;
-  return units < 8 * kResidentWarps ? kFineSplitPages : kSplitPages;
-}
-
-static size_t workspace_bytes_for(int num_seqs, int num_q_heads, int head_dim, size_t slots) {
-  const size_t n = slots * (size_t)num_seqs * (size_t)num_q_heads;
-  return kWorkBytes + pair_counter_bytes(num_seqs, num_q_heads) + n * 2 * sizeof(float) +
-         n * (size_t)head_dim * sizeof(float);
-}
-
 size_t tkv_decode_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
                                   int max_context_len) {
   if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || max_context_len < 0) return 0;
-  const int n_coarse = tkv_decode_num_splits(max_context_len) - 1;
-  const int sp = split_pages_for(num_seqs, num_q_heads, n_coarse);
-  return workspace_bytes_for(num_seqs, num_q_heads, head_dim,
-                             (size_t)n_coarse * (kSplitPages / sp) + 1);
+  return stream_workspace_bytes(num_seqs, num_q_heads, head_dim);
 }
 
 int tkv_decode_launches(int num_seqs, int num_q_heads, int max_context_len) {
   if (num_seqs <= 0 || num_q_heads <= 0 || max_context_len < 0) return 0;
-  const int n_coarse = tkv_decode_num_splits(max_context_len) - 1;
-  const int sp = split_pages_for(num_seqs, num_q_heads, n_coarse);
-  return n_coarse * (kSplitPages / sp) + 1 > kWideMergeSlots ? 2 : 1;
+  return stream_decode_launches(num_seqs, num_q_heads);
 }
 
 size_t tkv_decode_range_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
@@ -272,9 +239,51 @@ size_t tkv_decode_range_workspace_bytes(int num_seqs, int num_q_heads, int head_
   if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || split_lo < 0 ||
       split_hi < split_lo)
     return 0;
-  const int sp = split_pages_for(num_seqs, num_q_heads, split_hi - split_lo);
-  return workspace_bytes_for(num_seqs, num_q_heads, head_dim,
-                             (size_t)(split_hi - split_lo) * (kSplitPages / sp) + 1);
+  return stream_workspace_bytes(num_seqs, num_q_heads, head_dim);
+}
+
+// Arguments of the stream decode shared by tkv_paged_decode and
+// tkv_paged_decode_range; TKV_OK when they are valid.
+static int stream_args(StreamArgs& a, const tkv_cache_t* cache, const void* q, int q_dtype,
+                       const int32_t* block_tables, int max_blocks_per_seq,
+                       const int32_t* seq_lens, const int32_t* seq_slots, int num_seqs,
+                       int num_q_heads, float scale, int* err_flag) {
+  if (!cache_ok(cache)) return TKV_INVALID_ARGUMENT;
+  const tkv_format_t& f = cache->fmt;
+  if (q_dtype != TKV_F16 && q_dtype != TKV_BF16) return TKV_NOT_IMPLEMENTED;
+  if (num_seqs <= 0 || num_seqs > 65535 || num_q_heads <= 0) return TKV_INVALID_ARGUMENT;
+  if (num_q_heads % f.n_kv_heads != 0) return TKV_INVALID_ARGUMENT;
+  const int grp = num_q_heads / f.n_kv_heads;
+  if (grp > 8) return TKV_NOT_IMPLEMENTED;  // one mma n-tile of 8 q heads per kv head
+  if (!q || !block_tables || !seq_lens || max_blocks_per_seq <= 0) return TKV_INVALID_ARGUMENT;
+  if (!(scale > 0.f) || !isfinite(scale)) return TKV_INVALID_ARGUMENT;
+  // q rows, pool pages and ring chunks are moved by 16-byte bulk copies
+  if (!aligned16(q) || !aligned16(cache->pool) || !aligned16(cache->ring))
+    return TKV_INVALID_ARGUMENT;
+  memset(&a, 0, sizeof(a));
+  a.pool = static_cast<const uint8_t*>(cache->pool);
+  a.ring = static_cast<const uint16_t*>(cache->ring);
+  a.num_pages = cache->num_pages;
+  a.max_seqs = cache->max_seqs;
+  a.n_kv_heads = f.n_kv_heads;
+  a.residual = f.residual;
+  a.ring_cap = f.ring_cap;
+  a.q = q;
+  a.q_bf16 = q_dtype == TKV_BF16;
+  a.block_tables = block_tables;
+  a.max_blocks = max_blocks_per_seq;
+  a.seq_lens = seq_lens;
+  a.seq_slots = seq_slots;
+  a.num_seqs = num_seqs;
+  a.num_q_heads = num_q_heads;
+  a.grp = grp;
+  a.max_len = INT_MAX;
+  a.alpha = scale * 1.4426950408889634f;
+  a.pg_lo = 0;
+  a.pg_hi = INT_MAX;
+  a.include_residual = 1;
+  a.err = err_flag;
+  return TKV_OK;
 }
 
 static int decode_partials_impl(const tkv_cache_t* cache, const void* q, int q_dtype,
@@ -363,32 +372,23 @@ int tkv_paged_decode_range(const tkv_cache_t* cache, const void* q, int q_dtype,
     return TKV_INVALID_ARGUMENT;
   if (num_seqs <= 0 || num_q_heads <= 0 || split_lo < 0 || split_hi < split_lo)
     return TKV_INVALID_ARGUMENT;
+  if (split_hi == split_lo && !include_residual) return TKV_INVALID_ARGUMENT;  // nothing to do
   const int D = cache->fmt.head_dim;
-  // finer splits when the range has few items and the workspace holds them
-  int sp = split_pages_for(num_seqs, num_q_heads, split_hi - split_lo);
-  auto need_for = [&](int pages) {
-    const size_t sl = (size_t)(split_hi - split_lo) * (kSplitPages / pages) + 1;
-    return workspace_bytes_for(num_seqs, num_q_heads, D, sl);
-  };
-  if (workspace_bytes < need_for(sp)) sp = kSplitPages;
-  if (workspace_bytes < need_for(sp)) return TKV_INVALID_ARGUMENT;
-  const int mult = kSplitPages / sp;
-  split_lo *= mult;
-  split_hi *= mult;
-  const int slots = (split_hi - split_lo) + (include_residual ? 1 : 0);
-  const size_t n = (size_t)slots * num_seqs * num_q_heads;
-  if (slots == 0) return TKV_INVALID_ARGUMENT;  // nothing would write out_ml / out_o
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  float* part_ml =
-      reinterpret_cast<float*>(ws + kWorkBytes + pair_counter_bytes(num_seqs, num_q_heads));
-  float* part_o = part_ml + 2 * n;
-  const cudaStream_t s = as_stream(stream);
-  const int st = decode_partials_impl(cache, q, q_dtype, block_tables, max_blocks_per_seq,
-                                      seq_lens, seq_slots, num_seqs, num_q_heads, scale, split_lo,
-                                      split_hi, include_residual, part_ml, part_o, ws, nullptr,
-                                      nullptr, 0, err_flag, s, sp);
+  if (workspace_bytes < stream_workspace_bytes(num_seqs, num_q_heads, D))
+    return TKV_INVALID_ARGUMENT;
+  StreamArgs a;
+  const int st = stream_args(a, cache, q, q_dtype, block_tables, max_blocks_per_seq, seq_lens,
+                             seq_slots, num_seqs, num_q_heads, scale, err_flag);
   if (st != TKV_OK) return st;
-  return launch_reduce(part_ml, part_o, slots, num_seqs, num_q_heads, D, out_ml, out_o, s);
+  constexpr int kMaxSplit = INT_MAX / kSplitPages;
+  a.pg_lo = split_lo < kMaxSplit ? split_lo * kSplitPages : INT_MAX;
+  a.pg_hi = split_hi < kMaxSplit ? split_hi * kSplitPages : INT_MAX;
+  a.include_residual = include_residual ? 1 : 0;
+  a.mode = kStreamPartials;
+  a.out = out_o;
+  a.out_dtype = TKV_F32;
+  return launch_stream_decode(a, D, cache->fmt.bits, cache->fmt.group_size, workspace,
+                              workspace_bytes, out_ml, as_stream(stream));
 }
 
 int tkv_paged_prefill(const tkv_cache_t* cache, const void* q, int q_dtype, void* out,
@@ -458,32 +458,16 @@ int tkv_paged_decode(const tkv_cache_t* cache, const void* q, int q_dtype, void*
   if (workspace_bytes < need || !aligned16(workspace)) return TKV_INVALID_ARGUMENT;
   if (out_dtype != TKV_F32 && out_dtype != TKV_F16 && out_dtype != TKV_BF16)
     return TKV_NOT_IMPLEMENTED;
-  const int n_coarse = tkv_decode_num_splits(max_context_len) - 1;
-  const int sp = split_pages_for(num_seqs, num_q_heads, n_coarse);
-  const int slots = n_coarse * (kSplitPages / sp) + 1;
-  const size_t n = (size_t)slots * num_seqs * num_q_heads;
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  void* work = ws;
-  unsigned int* bh_count = reinterpret_cast<unsigned int*>(ws + kWorkBytes);
-  float* part_ml =
-      reinterpret_cast<float*>(ws + kWorkBytes + pair_counter_bytes(num_seqs, num_q_heads));
-  float* part_o = part_ml + 2 * n;
-  const cudaStream_t st = as_stream(stream);
-  if (slots > kWideMergeSlots) {
-    // long contexts: the split kernel, then a slot-parallel merge (a single
-    // warp merging hundreds of slots would be the launch's tail)
-    const int r = decode_partials_impl(cache, q, q_dtype, block_tables, max_blocks_per_seq,
-                                       seq_lens, seq_slots, num_seqs, num_q_heads, scale, 0,
-                                       slots - 1, 1, part_ml, part_o, work, nullptr, nullptr, 0,
-                                       err_flag, st, sp);
-    if (r != TKV_OK) return r;
-    return launch_merge(part_ml, part_o, slots, num_seqs, num_q_heads, D, out, out_dtype, st);
-  }
-  // one launch: the split kernel merges each (sequence, kv head) when its last
-  // split finishes
-  return decode_partials_impl(cache, q, q_dtype, block_tables, max_blocks_per_seq, seq_lens,
-                              seq_slots, num_seqs, num_q_heads, scale, 0, slots - 1, 1, part_ml,
-                              part_o, work, bh_count, out, out_dtype, err_flag, st, sp);
+  StreamArgs a;
+  const int st = stream_args(a, cache, q, q_dtype, block_tables, max_blocks_per_seq, seq_lens,
+                             seq_slots, num_seqs, num_q_heads, scale, err_flag);
+  if (st != TKV_OK) return st;
+  a.max_len = max_context_len;  // longer sequences: TKV_ERR_BAD_LENGTH, zero output
+  a.mode = stream_decode_launches(num_seqs, num_q_heads) == 2 ? kStreamPartials : kStreamFused;
+  a.out = out;
+  a.out_dtype = out_dtype;
+  return launch_stream_decode(a, D, cache->fmt.bits, cache->fmt.group_size, workspace,
+                              workspace_bytes, nullptr, as_stream(stream));
 }
 
 // ---------------------------------------------------------------------------

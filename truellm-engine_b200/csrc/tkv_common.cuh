@@ -86,6 +86,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return false;
 }
 
+// Non-blocking check of the phase with the given parity.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// mbar_wait with a non-blocking first check: a phase that has already
+// completed (the common case in a deep enough ring) costs no suspend.
+__device__ __forceinline__ bool mbar_wait_fast(uint64_t* bar, uint32_t parity, int* err) {
+  return mbar_test(bar, parity) || mbar_wait(bar, parity, err);
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes % 16 == 0,
 // both addresses 16-byte aligned).
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes,
@@ -111,6 +132,20 @@ __device__ __forceinline__ void cp_async4(void* dst_smem, const void* src_gmem) 
 }
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;\n" ::: "memory");
+}
+// 16-byte cp.async with an L2 cache policy
+__device__ __forceinline__ void cp_async16_hint(void* dst_smem, const void* src_gmem,
+                                                uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;\n" ::"r"(
+                   smem_u32(dst_smem)),
+               "l"(src_gmem), "l"(policy)
+               : "memory");
+}
+// Arrives on `bar` once every cp.async this thread issued before has landed;
+// the arrival is one of the barrier's expected count (.noinc).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(smem_u32(bar))
+               : "memory");
 }
 
 // L2 policy for data read once per launch (cache pages): evict it first, so
@@ -304,6 +339,46 @@ struct PrefillArgs {
   float alpha;  // scale * log2(e)
   int* err;
 };
+
+// Balanced ("stream") decode: see tkv_stream.cu.
+constexpr int kStreamFused = 0;     // the last warp of each pair merges into out
+constexpr int kStreamPartials = 1;  // partials + pair_info; stream_merge_kernel merges
+
+struct StreamArgs {
+  const uint8_t* pool;
+  const uint16_t* ring;
+  int num_pages, max_seqs, n_kv_heads, residual, ring_cap;
+  const void* q;
+  int q_bf16;
+  const int32_t* block_tables;
+  int max_blocks;
+  const int32_t* seq_lens;
+  const int32_t* seq_slots;
+  int num_seqs, num_q_heads, grp;
+  int max_len;           // longer sequences are flagged TKV_ERR_BAD_LENGTH
+  float alpha;           // scale * log2(e)
+  int pg_lo, pg_hi;      // quantised pages [pg_lo, pg_hi) of every sequence
+  int include_residual;  // 1: the fp16 residual tokens too
+  int n_warps;           // warps launched (bounded by the workspace's partial slots)
+  int warp_smem;         // shared memory bytes of one warp
+  int mode;              // kStreamFused or kStreamPartials
+  unsigned int* pair_count;  // [num_seqs * n_kv_heads], zero between launches (fused)
+  int2* pair_info;           // [num_seqs * n_kv_heads] (first slot, slots) (partials)
+  float* part_ml;            // [slots][grp][2]  (m in log2 units, l)
+  float* part_o;             // [slots][grp][D]
+  void* out;                 // fused: [num_seqs, num_q_heads, D] in out_dtype
+  int out_dtype;
+  int* err;
+};
+
+// Workspace of the stream decode for these sizes (the query functions' value).
+size_t stream_workspace_bytes(int num_seqs, int num_q_heads, int head_dim);
+// Launches the stream decode: fused (one launch) or partials + merge (two
+// launches; out_ml != nullptr: the merge writes unnormalised (M, L) and O).
+int launch_stream_decode(StreamArgs a, int head_dim, int bits, int group, void* workspace,
+                         size_t workspace_bytes, float* out_ml, cudaStream_t stream);
+// 1 or 2: the launches tkv_paged_decode makes for these sizes.
+int stream_decode_launches(int num_seqs, int num_q_heads);
 
 int launch_ref_kivi(int mode, const void* in, void* out, int n_vecs, int head_dim, int n_outliers,
                     int group_size, cudaStream_t stream);
