@@ -3,12 +3,13 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload config2]
                     [--impl kivi|reference]
 
-Default workload = BASELINE config 2 (Llama-3-8B shape decode): B=64 sequences
-per GPU, Hq=32, Hkv=8, D=128, context U[1024, 8192], 16-token pages scattered
-over a shared pool, KIVI INT4 with G=R=128, bf16 q, synthetic seeded data
-(weak scaling: every rank decodes its own 64 sequences, no collective on the
-data path).  A step = one decode-attention call for all sequences of one
-layer.  metric = sequence-tokens/s (B / step time), whole job.
+Default workload = BASELINE config 2 (Llama-3-8B shape decode): B=64
+sequences, Hq=32, Hkv=8, D=128, context U[1024, 8192], 16-token pages
+scattered over a shared pool, KIVI INT4 with G=R=128, bf16 q, synthetic seeded
+data.  A step = one decode-attention call for all sequences of one layer.
+metric = sequence-tokens/s (B / step time), whole job.  With N GPUs the same
+64 sequences are split over the ranks by token balancing (strong scaling, no
+collective on the data path: every rank decodes whole sequences).
 
 --workload config3 measures the other half of the path, quantize-on-append
 64 sequences x 2048-token bf16 chunk per GPU appended to
@@ -56,7 +57,7 @@ def parse():
     ap.add_argument("--workload", default="config2",
                     choices=["config2", "config3", "config4", "config4b", "config5", "prefill"])
     ap.add_argument("--impl", default="kivi", choices=["kivi", "reference"])
-    ap.add_argument("--cpu-sample", type=int, default=8, help="sequences in the CPU sample")
+    ap.add_argument("--cpu-sample", type=int, default=64, help="sequences in the CPU sample")
     return ap.parse_args()
 
 
@@ -163,20 +164,41 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(sm)}
 
 
-def ncu_traffic(workload: str):
-    """Per-launch DRAM traffic of the decode kernel from the committed ncu
-    summary (profiles/decode_warp_<workload>.json), or None."""
-    p = ROOT / "profiles" / f"decode_warp_{workload}.json"
+CSRC = ROOT / "truellm-engine_b200" / "csrc"
+# the sources each profiled kernel is built from: an ncu figure counts only for
+# the build it was taken from
+KERNEL_SOURCES = {
+    "decode_stream": ["tkv_stream.cu", "tkv_decode_common.cuh", "tkv_frag.cuh", "tkv_common.cuh"],
+    "append": ["tkv_append.cu", "tkv_common.cuh"],
+    "prefill": ["tkv_prefill.cu", "tkv_frag.cuh", "tkv_common.cuh"],
+}
+
+
+def source_sha(kernel: str) -> str:
+    import hashlib
+    h = hashlib.sha256()
+    for name in KERNEL_SOURCES[kernel]:
+        h.update((CSRC / name).read_bytes())
+    return h.hexdigest()
+
+
+def ncu_traffic(profile: str, kernel: str, key: str):
+    """Per-launch DRAM traffic (dram__bytes_read + write) from the committed
+    ncu summary profiles/<profile>.json, or None when there is none or it was
+    taken from other kernel sources than the ones built now."""
+    p = ROOT / "profiles" / f"{profile}.json"
     if not p.exists():
         return None
     d = json.loads(p.read_text())
-    return d.get("dram_bytes_per_launch")
+    if d.get("source_sha256") != source_sha(kernel):
+        return None
+    return d.get(key)
 
 
 # ---------------------------------------------------------------------------
 # CPU timing of the reference algorithm (oracle restatement)
 # ---------------------------------------------------------------------------
-def cpu_sample_size(lengths, cap: int, token_budget: int = 40000) -> int:
+def cpu_sample_size(lengths, cap: int, token_budget: int = 400000) -> int:
     """Leading sequences of the CPU sample: at most `cap`, at most about
     `token_budget` context tokens (long-context workloads), at least one."""
     n, tok = 0, 0
@@ -216,6 +238,15 @@ def host_cache_for_reference(O, wl, w, sample):
     return st
 
 
+def workload_desc(name: str, w) -> str:
+    """The workload string of the JSON line's config (the same in both arms)."""
+    return {"config2": f"config2: B={w.B} Hq={w.Hq} Hkv={w.Hkv} D={w.D} L~U[1024,8192]",
+            "config4": f"config4 run A: B={w.B} Hq={w.Hq} Hkv={w.Hkv} D={w.D} L=131072",
+            "config4b": f"config4 run B: B=1 Hq={w.Hq} Hkv={w.Hkv} D={w.D} L=131072",
+            "config5": f"config5: B={w.B} Hq={w.Hq} Hkv={w.Hkv} D={w.D} L~logU[128,32768] "
+                       "INT4 x128 + INT2 x128"}[name] + f" G={w.group} R={w.residual}"
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -223,7 +254,8 @@ def run_reference(args):
     from oracle import oracle as O
     O.build()
     wl = importlib.import_module("truellm-engine_b200.workloads")
-    w = make_workload(wl, args.workload, 0)
+    w = (wl.config4(seed=4000, B=1) if args.workload == "config4b"
+         else make_workload(wl, args.workload, 0))
     sample = cpu_sample_size(w.lengths, args.cpu_sample)
     st = host_cache_for_reference(O, wl, w, sample)
     rng = np.random.default_rng(w.seed + 1)
@@ -231,26 +263,32 @@ def run_reference(args):
     threads = os.cpu_count() or 1
     bt = np.ascontiguousarray(w.block_tables[:sample])
     lens = np.ascontiguousarray(w.lengths[:sample])
-    for _ in range(max(1, min(args.warmup, 2))):
+    # each step decodes the whole sample (all 64 sequences at config 2, about
+    # a second on 16 threads): at most 10 timed steps keep the arm to minutes
+    steps, warmup = max(1, min(args.steps, 10)), max(1, min(args.warmup, 2))
+    for _ in range(warmup):
         st.decode(q[:sample], bt, lens, 1 / math.sqrt(w.D), n_threads=threads)
     times = []
-    for _ in range(args.steps):
+    for _ in range(steps):
         t0 = time.perf_counter()
         st.decode(q[:sample], bt, lens, 1 / math.sqrt(w.D), n_threads=threads)
         times.append(time.perf_counter() - t0)
     t = float(np.mean(times))
     value = sample / t
+    whole = sample == w.B
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
+        "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
+        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: sample of {sample} sequences",
-                   "mean_context": float(lens.mean())},
+        "config": {"workload": workload_desc(args.workload, w) if whole else
+                   f"{workload_desc(args.workload, w)}: sample of {sample} sequences",
+                   "global_batch": sample, "mean_context": float(lens.mean())},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{sample} sequences of {args.workload} (mean context "
-                                   f"{lens.mean():.0f}), fp64 attention over the "
-                                   "dequantised pages, all host threads"},
+                         "sample": f"{sample} of the {w.B} sequences of {args.workload} (mean "
+                                   f"context {lens.mean():.0f}), CPU restatement of the "
+                                   "reference algorithm: fp64 attention over the dequantised "
+                                   "pages, all host threads"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -281,6 +319,11 @@ class DecodePart:
         self.out_host = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
         self.q_dev = torch.empty_like(self.q)
         self.lens_dev = torch.empty_like(self.lens)
+        self.calls = {}  # prepared decode calls per (q, lens, stream)
+
+
+def _stream_id(st) -> int:
+    return st.cuda_stream if hasattr(st, "cuda_stream") else int(st)
 
 
 def decode_plan(args, wl, ops, torch, dev, rank, world):
@@ -288,10 +331,15 @@ def decode_plan(args, wl, ops, torch, dev, rank, world):
     layout, algorithmic bytes per step on this rank, token-split decoder)."""
     SH = importlib.import_module("truellm-engine_b200.sharding")
     name = args.workload
-    if name == "config2":  # every rank decodes its own 64 sequences
-        w = make_workload(wl, name, rank)
-        return ([DecodePart(ops, wl, torch, w, dev, "all")], world * w.B, "weak",
-                f"sequence-sharded x{world}", wl.decode_algorithmic_bytes(w), None, w)
+    if name == "config2":  # the 64 sequences, split over the ranks by token balancing
+        w = make_workload(wl, name, 0)
+        if world == 1:
+            return ([DecodePart(ops, wl, torch, w, dev, "all")], w.B, "strong",
+                    "one GPU", wl.decode_algorithmic_bytes(w), None, w)
+        mine = SH.balance_sequences(w.lengths, world)[rank]
+        sub = wl.subset(w, mine)
+        return ([DecodePart(ops, wl, torch, sub, dev, f"{len(mine)} sequences")], w.B, "strong",
+                f"token-balanced sequences x{world}", wl.decode_algorithmic_bytes(sub), None, w)
     if name == "config4":  # run A: kv heads split over the ranks, same 8 sequences
         w = make_workload(wl, name, 0)
         kvh, qh = SH.head_shard(w.Hkv, w.Hq, world, rank)
@@ -360,9 +408,14 @@ def run_kivi(args):
             graph.replay()
         elif dec is not None:
             dec(p.cache, q, p.bt, lens, p.out, scale=p.scale, err=err, stream=st)
-        else:
-            ops.paged_decode(p.cache, q, p.bt, lens, p.max_ctx, scale=p.scale, out=p.out,
-                             workspace=p.ws, err=err, stream=st)
+        else:  # the C entry point with its arguments bound once per (buffers, stream)
+            key = (q.data_ptr(), lens.data_ptr(), _stream_id(st))
+            call = p.calls.get(key)
+            if call is None:
+                call = p.calls[key] = ops.PreparedDecode(
+                    p.cache, q, p.bt, lens, p.max_ctx, p.out, p.ws, scale=p.scale, err=err,
+                    stream=st)
+            call()
 
     # parts of one step (config 5: the INT4 and the INT2 sequences) run on
     # their own streams so one launch's tail overlaps the other's work
@@ -447,7 +500,8 @@ def run_kivi(args):
 
     peak, peak_kind = peaks()
     achieved = alg_bytes / t_split / 1e9
-    traffic = ncu_traffic(args.workload) if world == 1 else None
+    traffic = (ncu_traffic(f"decode_stream_{args.workload}", "decode_stream",
+                           "dram_bytes_per_launch") if world == 1 else None)
     # our kernel launches per step: the token split runs three (split kernel
     # and reduce of the range, merge) besides NCCL's all-gathers; otherwise one
     # or two per decode call (ops.decode_launches)
@@ -475,18 +529,13 @@ def run_kivi(args):
             except Exception as e:  # the baseline is reported, never required
                 cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                        "sample": f"failed: {e!r}"[:200]}
-        desc = {"config2": f"config2: B={w.B}/GPU Hq={w.Hq} Hkv={w.Hkv} D={w.D} L~U[1024,8192]",
-                "config4": f"config4 run A: B={w.B} Hq={w.Hq} Hkv={w.Hkv} D={w.D} L=131072",
-                "config4b": f"config4 run B: B=1 Hq={w.Hq} Hkv={w.Hkv} D={w.D} L=131072",
-                "config5": f"config5: B={w.B} Hq={w.Hq} Hkv={w.Hkv} D={w.D} L~logU[128,32768] "
-                           "INT4 x128 + INT2 x128"}[args.workload]
         line = {
             "metric": METRIC, "value": total_seqs / t_step, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step * 1e3,
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
             "dtype": "int4/bf16" if args.workload != "config5" else "int4+int2/bf16",
             "data": "synthetic (seeded N(0,1) K/V, key outlier channels x8)",
-            "config": {"workload": f"{desc} G={w.group} R={w.residual}",
+            "config": {"workload": workload_desc(args.workload, w),
                        "global_batch": total_seqs, "mean_context": float(w.lengths.mean()),
                        "parallelism": layout, "rank0_parts": [p.label for p in parts],
                        "l2": "inputs larger than L2 (cache %.0f MB per rank)" % (alg_bytes / 1e6)},
@@ -496,8 +545,11 @@ def run_kivi(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": traffic,
-                         "kernel": "decode_warp_kernel<128,%d,128> (split + fused merge)%s" % (
-                             w.bits, " + all-gather + merge_kernel" if dec is not None else ""),
+                         "kernel": "decode_stream_kernel<128,%d,128>%s" % (
+                             w.bits, " (range) + stream_merge_kernel + all-gather + merge_kernel"
+                             if dec is not None else
+                             " + stream_merge_kernel" if n_launch > len(parts) else
+                             " (merge fused)"),
                          "alg_bytes_per_launch": alg_bytes,
                          "kernel_ms": t_split * 1e3},
             "cpu_baseline": cpu,

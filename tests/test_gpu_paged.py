@@ -304,3 +304,22 @@ def test_sequence_longer_than_max_context_len_is_flagged(ops, O, wl, cuda):
     assert torch.all(out[2] == 0)
     ref = tw.cpu.decode(q.float().cpu().numpy()[:2], bt[:2], lengths[:2], scale, n_threads=8)
     check_close(out[:2].cpu().numpy(), ref)
+
+
+def test_prepared_decode_equals_paged_decode(ops, O, wl, cuda):
+    """PreparedDecode (arguments bound once) launches the same decode."""
+    lengths = [700, 1300, 90]
+    tw, bt, lengths, rng = _build(ops, O, wl, cuda, 128, 128, 128, 4, 8, lengths, "bf16",
+                                  seed=13)
+    q = bits_to_torch(wl.f32_to_bf16_bits(rng.standard_normal((3, 32, 128))), "bf16", cuda)
+    bt_d, lens_d = i32(bt, cuda), i32(lengths, cuda)
+    want = ops.paged_decode(tw.gpu, q, bt_d, lens_d, 1300, out_dtype=torch.float32)
+    out = torch.empty_like(want)
+    ws = torch.zeros(ops.decode_workspace_bytes(3, 32, 128, 1300), dtype=torch.uint8,
+                     device=cuda)
+    call = ops.PreparedDecode(tw.gpu, q, bt_d, lens_d, 1300, out, ws, err=tw.err)
+    for _ in range(2):
+        call()
+        torch.cuda.synchronize()
+        assert int(tw.err.item()) == 0
+        assert torch.equal(out, want)

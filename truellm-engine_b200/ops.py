@@ -222,6 +222,38 @@ def paged_decode(cache: KiviPagedCache, q: torch.Tensor, block_tables: torch.Ten
     return out
 
 
+class PreparedDecode:
+    """tkv_paged_decode with its arguments bound once to fixed buffers: each
+    call is one ctypes call, for decode loops where the wrapper's per-call
+    work (argument conversion, the format struct) would show beside a
+    ~0.1 ms kernel.  The buffers must stay alive and keep their addresses."""
+
+    def __init__(self, cache: KiviPagedCache, q: torch.Tensor, block_tables: torch.Tensor,
+                 seq_lens: torch.Tensor, max_context_len: int, out: torch.Tensor,
+                 workspace: torch.Tensor, scale: Optional[float] = None,
+                 seq_slots: Optional[torch.Tensor] = None, err: Optional[torch.Tensor] = None,
+                 stream=None):
+        _need_cuda(q, block_tables, seq_lens, out, workspace)
+        if not q.is_contiguous():
+            raise ValueError("q must be contiguous")
+        B, Hq, D = q.shape
+        if scale is None:
+            scale = 1.0 / math.sqrt(D)
+        self._keep = (q, block_tables, seq_lens, out, workspace, seq_slots, err)
+        self._c = cache.c_struct()
+        self._fn = L.lib().tkv_paged_decode
+        self._args = (C.byref(self._c), _ptr(q), _DT[q.dtype], _ptr(out), _DT[out.dtype],
+                      _ptr(block_tables), int(block_tables.shape[1]), _ptr(seq_lens),
+                      _ptr(seq_slots), B, Hq, float(scale), int(max_context_len),
+                      _ptr(workspace), int(workspace.numel() * workspace.element_size()),
+                      _ptr(err), C.c_void_p(_stream(stream)))
+
+    def __call__(self) -> None:
+        st = self._fn(*self._args)
+        if st != L.TKV_OK:
+            raise L.TkvError("tkv_paged_decode", st)
+
+
 def paged_decode_partials(cache: KiviPagedCache, q: torch.Tensor, block_tables: torch.Tensor,
                           seq_lens: torch.Tensor, split_lo: int, split_hi: int,
                           include_residual: bool, part_ml: torch.Tensor, part_o: torch.Tensor,
