@@ -228,12 +228,13 @@ TKV_API int tkv_paged_decode(const tkv_cache_t* cache, const void* q, int q_dtyp
  * all device memory, or a decode loop that must not call cudaMalloc -- the
  * split-KV partials and work counters live in a static device array of
  * TKV_NOALLOC_SCRATCH_BYTES that every GPU loading this library keeps until
- * the process exits.  Nothing is allocated.  The first call on a device looks
- * up the array's device address and zeroes the array (stream-ordered on
- * `stream`); make that first call before any stream capture.  Calls whose
- * tkv_decode_workspace_bytes() exceeds the scratch return TKV_OUT_OF_MEMORY
- * without launching.  All calls on a device share the array, so calls that
- * overlap on the GPU race; it keeps the last call's partials. */
+ * the process exits.  Nothing is allocated.  Every call looks up the array's
+ * device address on the current device and clears its completion counters
+ * with a stream-ordered memset on `stream` before the decode launch.  Calls
+ * whose tkv_decode_workspace_bytes() exceeds the scratch return
+ * TKV_OUT_OF_MEMORY without launching.  All calls on a device share the
+ * array, so calls that overlap on the GPU race; it keeps the last call's
+ * partials. */
 TKV_API int tkv_paged_decode_noalloc(const tkv_cache_t* cache, const void* q, int q_dtype,
                                      void* out, int out_dtype, const int32_t* block_tables,
                                      int max_blocks_per_seq, const int32_t* seq_lens,

@@ -118,18 +118,25 @@ int tkv_allocator_add_sequence(tkv_allocator_t* a, uint64_t seq_id, int num_toke
   if (a->seqs.count(seq_id)) return TKV_INVALID_ARGUMENT;
   const int need = a->pages_for(num_tokens);
   if ((int)a->free_pages.size() < need || a->free_rows.empty()) return TKV_OUT_OF_MEMORY;
+  // Every step that can throw comes before pages or a row are taken: the
+  // entry is created, then its page list reserved (erased again on failure),
+  // so an allocation failure leaves the allocator as it was.
+  decltype(a->seqs.begin()) it;
   try {
-    tkv_allocator::Seq s;
-    s.pages.reserve(need);
-    auto& slot = a->seqs[seq_id];
-    for (int i = 0; i < need; ++i) s.pages.push_back(a->take_page());
-    s.len = num_tokens;
-    s.row = a->take_row();
-    slot = std::move(s);
-    if (ring_row) *ring_row = slot.row;
+    it = a->seqs.emplace(seq_id, tkv_allocator::Seq{}).first;
   } catch (const std::bad_alloc&) {
     return TKV_OUT_OF_MEMORY;
   }
+  try {
+    it->second.pages.reserve(need);
+  } catch (const std::bad_alloc&) {
+    a->seqs.erase(it);
+    return TKV_OUT_OF_MEMORY;
+  }
+  for (int i = 0; i < need; ++i) it->second.pages.push_back(a->take_page());
+  it->second.len = num_tokens;
+  it->second.row = a->take_row();
+  if (ring_row) *ring_row = it->second.row;
   return TKV_OK;
 }
 

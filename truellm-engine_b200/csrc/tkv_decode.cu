@@ -34,6 +34,8 @@
 //     layout into the B-operand layout with 4 shuffles + 2 PRMT.
 // Tensor cores are used because at GQA 4 the INT4 cache carries ~7.5 MAC per
 // HBM byte, above what the FP32 pipes can issue at HBM speed.
+#include <atomic>
+
 #include "tkv_decode_common.cuh"
 
 namespace tkv {
@@ -116,6 +118,10 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
   int stage = 0;
   uint32_t phase = 0;
   int gcount = 0;  // key groups consumed so far (meta buffer = gcount & 1)
+  // After a bounded wait gives up (TKV_ERR_TIMEOUT set) the warp waits no
+  // more, finishes its current item without waiting and takes no new one, so
+  // a stuck copy costs one timeout per warp, not one per stage.
+  bool dead = false;
 
   // After an item's partial is written: with fuse_merge, the warp that
   // finishes the last of the nv + 1 written items of (sequence b, kv head h)
@@ -138,6 +144,7 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
   };
 
   for (;;) {
+    if (dead) break;
     int item = 0;
     if (lane == 0) item = static_cast<int>(atomicAdd(&a.work[0], 1u));
     item = __shfl_sync(0xffffffffu, item, 0);
@@ -241,7 +248,7 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
       for (int grp = 0; grp < ngroups; ++grp, ++gcount) {
         const int buf = gcount & 1;
         if (grp + 1 < ngroups) issue_meta(grp + 1, buf ^ 1);
-        mbar_wait(&bars[ST + buf], (gcount >> 1) & 1, a.err);
+        if (!dead && !mbar_wait(&bars[ST + buf], (gcount >> 1) & 1, a.err)) dead = true;
         // per-channel (step, zero) pairs of this key group as f16x2
         uint32_t ks[F::NKB][2], kz[F::NKB][2];
         const uint32_t* mwords = reinterpret_cast<const uint32_t*>(meta + buf * F::META);
@@ -255,7 +262,7 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
             kz[kb][hi] = __byte_perm(m0, m1, 0x7632);
           }
         for (int pi = 0; pi < F::PPG; pi += NP, ++j) {
-          mbar_wait(&bars[stage], phase, a.err);
+          if (!dead && !mbar_wait(&bars[stage], phase, a.err)) dead = true;
           const uint8_t* sbase = ring + stage * SB;
           // ---- S^T = K Q^T for NP pages (independent MMA chains).  Columns of
           //      padded heads (>= grp) see q = 0: their weights are computed and
@@ -374,13 +381,13 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
     const int n_chunks = n >> 1;
     for (int ci = 0; ci < n_chunks; ++ci) {
       const int sk = stage;
-      mbar_wait(&bars[stage], phase, a.err);
+      if (!dead && !mbar_wait(&bars[stage], phase, a.err)) dead = true;
       if (++stage == ST) {
         stage = 0;
         phase ^= 1u;
       }
       const int sv = stage;
-      mbar_wait(&bars[stage], phase, a.err);
+      if (!dead && !mbar_wait(&bars[stage], phase, a.err)) dead = true;
       if (++stage == ST) {
         stage = 0;
         phase ^= 1u;
@@ -419,6 +426,15 @@ __global__ void __launch_bounds__(32, TKV_DECODE_MIN_BLOCKS) decode_warp_kernel(
     item_done(b, h, nv);
   }
 
+  if (dead) {
+    // let the copies still in flight into this warp's ring and meta buffers
+    // land before the warp exits (each wait bounded again)
+    for (int i = 0; i < ST; ++i) {
+      const int s2 = (stage + i) % ST;
+      mbar_wait(&bars[s2], s2 >= stage ? phase : phase ^ 1u, nullptr);
+    }
+    for (int i = 0; i < 2; ++i) mbar_wait(&bars[ST + ((gcount + i) & 1)], ((gcount + i) >> 1) & 1, nullptr);
+  }
   // the last warp to finish resets the work counters for the next launch
   if (lane == 0) {
     __threadfence();
@@ -508,11 +524,14 @@ __global__ void __launch_bounds__(32 * kReduceWarps) wide_merge_kernel(
 template <int D, int BITS, int G>
 static int launch_warp_t(const DecodeArgs& a, cudaStream_t stream) {
   constexpr int smem = decode_smem_bytes<D, BITS, G>();
-  static int resident = 0;  // CTAs that fit on the device at once
-  if (resident == 0) {
-    int dev = 0, sms = 0, per_sm = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+  // CTAs that fit on each device at once (computed per device, thread-safe)
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return TKV_BACKEND_ERROR;
+  int resident = dev >= 0 && dev < 64 ? cache[dev].load(std::memory_order_relaxed) : 0;
+  if (resident <= 0) {
+    int sms = 0, per_sm = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
         cudaFuncSetAttribute(decode_warp_kernel<D, BITS, G>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_warp_kernel<D, BITS, G>, 32,
@@ -520,6 +539,7 @@ static int launch_warp_t(const DecodeArgs& a, cudaStream_t stream) {
         per_sm <= 0)
       return TKV_BACKEND_ERROR;
     resident = sms * per_sm;
+    if (dev >= 0 && dev < 64) cache[dev].store(resident, std::memory_order_relaxed);
   }
   const int grid = a.n_items < resident ? a.n_items : resident;
   decode_warp_kernel<D, BITS, G><<<grid, 32, smem, stream>>>(a);

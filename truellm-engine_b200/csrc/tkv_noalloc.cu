@@ -2,7 +2,7 @@
 // memory.
 //
 // tkv_paged_decode needs a caller-provided workspace (the split-KV partials
-// and the persistent kernel's work counters).  Some callers have no way to
+// and their completion counters).  Some callers have no way to
 // provide one: a kernel plugin handed only the engine's tensors, a host whose
 // allocator owns all device memory and forbids side allocations, or a decode
 // loop that must not call cudaMalloc (it can synchronise the device) in the
@@ -11,40 +11,22 @@
 //
 // The array below lives in every GPU that loads this library, for the life of
 // the process.  Host code never dereferences its name: on the host the symbol
-// is only a stand-in, so its device address is fetched with
-// cudaGetSymbolAddress once per device, with that device current, on the
-// first call made on it.
-#include <mutex>
-
+// is only a stand-in, so every call looks up its device address with
+// cudaGetSymbolAddress, for the device that is current (a cheap host-side
+// lookup, correct also after cudaDeviceReset gives the device a new context).
 #include "tkv_common.cuh"
 
 namespace {
 
 constexpr size_t kScratchBytes = TKV_NOALLOC_SCRATCH_BYTES;
-constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_decode_scratch[kScratchBytes];
 
-std::mutex g_setup_mu;
-void* g_scratch_ptr[kMaxDevices] = {};
-
-// Per-device set-up: device address of the scratch array, zeroed once (its
-// work and completion counters must start at zero; the decode kernel leaves
-// them zero after every call).
-int scratch_for_current_device(void** ptr, cudaStream_t stream) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-    return TKV_BACKEND_ERROR;
-  std::lock_guard<std::mutex> lock(g_setup_mu);
-  if (g_scratch_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || p == nullptr)
-      return TKV_BACKEND_ERROR;
-    if (cudaMemsetAsync(p, 0, kScratchBytes, stream) != cudaSuccess) return TKV_BACKEND_ERROR;
-    g_scratch_ptr[dev] = p;
-  }
-  *ptr = g_scratch_ptr[dev];
-  return TKV_OK;
+// Bytes at the start of the decode workspace that must be zero when a call
+// begins: the per-(sequence, kv head) completion counters (256 bytes of
+// reserved space, then num_seqs * num_q_heads counters rounded up to 256).
+size_t counter_bytes(int num_seqs, int num_q_heads) {
+  return 256 + ((size_t)num_seqs * (size_t)num_q_heads * 4 + 255) / 256 * 256;
 }
 
 }  // namespace
@@ -63,8 +45,13 @@ int tkv_paged_decode_noalloc(const tkv_cache_t* cache, const void* q, int q_dtyp
   if (need == 0) return TKV_INVALID_ARGUMENT;
   if (need > kScratchBytes) return TKV_OUT_OF_MEMORY;  // larger than the static scratch
   void* scratch = nullptr;
-  const int st = scratch_for_current_device(&scratch, static_cast<cudaStream_t>(stream));
-  if (st != TKV_OK) return st;
+  if (cudaGetSymbolAddress(&scratch, g_decode_scratch) != cudaSuccess || scratch == nullptr)
+    return TKV_BACKEND_ERROR;
+  // Every call shares the array: clear its counters (stream-ordered) so the
+  // call does not depend on what an earlier call left there.
+  if (cudaMemsetAsync(scratch, 0, counter_bytes(num_seqs, num_q_heads),
+                      static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return TKV_BACKEND_ERROR;
   return tkv_paged_decode(cache, q, q_dtype, out, out_dtype, block_tables, max_blocks_per_seq,
                           seq_lens, seq_slots, num_seqs, num_q_heads, scale, max_context_len,
                           scratch, kScratchBytes, err_flag, stream);
