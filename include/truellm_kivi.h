@@ -186,17 +186,17 @@ TKV_API int tkv_paged_append(const tkv_cache_t* cache, const void* k_new, const 
 /* Number of split slots per sequence: ceil(max_context_len / TKV_SPLIT_TOKENS) + 1
  * (the last one holds the fp16 residual). */
 TKV_API int tkv_decode_num_splits(int max_context_len);
-/* Workspace bytes for tkv_paged_decode: work counters, per-(sequence, kv head)
- * completion counters and the split partials.  Zero the whole workspace once
- * when it is allocated; every call leaves the counters zero again.  Calls that
- * share a workspace must not overlap on the GPU.  Launches with few work items
- * (num_seqs * num_q_heads * splits small: long single sequences, few kv heads)
- * use 128-token splits internally; the size accounts for that. */
+/* Workspace bytes for tkv_paged_decode: per-(sequence, kv head) completion
+ * counters and the partials of pairs whose pages are spread over several
+ * warps (one slot per pair plus one per resident warp of the GPU).  Zero the
+ * whole workspace once when it is allocated; every call leaves the counters
+ * zero again.  Calls that share a workspace must not overlap on the GPU.  The
+ * size does not depend on max_context_len. */
 TKV_API size_t tkv_decode_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
                                   int max_context_len);
 /* Kernel launches tkv_paged_decode makes for these sizes: 1 (merge fused into
- * the decode launch) or 2 (contexts beyond 64K tokens: a separate
- * slot-parallel merge). */
+ * the decode launch) or 2 (num_seqs * num_q_heads < 1024: few, long pairs
+ * whose merge runs in a separate slot-parallel launch). */
 TKV_API int tkv_decode_launches(int num_seqs, int num_q_heads, int max_context_len);
 /* Workspace bytes for tkv_paged_decode_range over splits [split_lo, split_hi)
  * (with the finer internal splits the range may use). */
@@ -208,11 +208,14 @@ TKV_API size_t tkv_decode_range_workspace_bytes(int num_seqs, int num_q_heads, i
  * cache: out[s, h, :] = softmax(scale * q[s,h,:] . K^T) V over the
  * seq_lens[s] tokens of sequence s, kv head = h / (num_q_heads / n_kv_heads)
  * (megakernel.cu:270-277).  q, out: [num_seqs, num_q_heads, D]; q is fp16 or
- * bf16, out is fp16, bf16 or f32.  Split-KV over TKV_SPLIT_TOKENS-token splits
- * plus a log-sum-exp merge (paged_attention_v2.cu:132-170), done by the warp
- * that finishes the last split of each (sequence, kv head): one launch.
- * Contexts beyond 64K tokens merge in a second, slot-parallel launch
- * (tkv_decode_launches). */
+ * bf16, out is fp16, bf16 or f32.  Every resident warp of the GPU takes an
+ * equal-cost range of the call's (sequence, kv head) pages and residual
+ * chunks; a pair spread over several warps is merged by log-sum-exp
+ * (paged_attention_v2.cu:132-170) in the warp that finishes its last part
+ * (one launch) or, when num_seqs * num_q_heads < 1024, in a second
+ * slot-parallel launch (tkv_decode_launches).  Sequences longer than
+ * max_context_len (or than max_blocks_per_seq pages) set TKV_ERR_BAD_LENGTH
+ * in *err_flag and get a zero output row. */
 TKV_API int tkv_paged_decode(const tkv_cache_t* cache, const void* q, int q_dtype, void* out,
                      int out_dtype, const int32_t* block_tables, int max_blocks_per_seq,
                      const int32_t* seq_lens, const int32_t* seq_slots, int num_seqs,

@@ -1,4 +1,4 @@
-"""Parity at BASELINE's full sizes (configs 2 and 3), where the CPU oracle
+"""Parity at BASELINE's full sizes (configs 2-5), where the CPU oracle
 cannot redo everything: sampled sequences against the oracle, plus properties
 that hold at any size.
 
@@ -9,6 +9,10 @@ that hold at any size.
 * config 3 append (64 x 2048 bf16 tokens): sampled sequences' pages and live
   ring tokens equal the oracle's bytes; appending the chunk in two halves
   gives the same pool and ring bytes as one call (chunking invariance).
+* config 4 decode (B=8, 131072 tokens, Hq=64): two sampled sequences against
+  the oracle; two token ranges merged equal the one-call decode.
+* config 5 decode (B=256 continuous batch, INT4 and INT2 halves): the longest
+  and shortest sequence of each half against the oracle.
 """
 import importlib
 import math
@@ -109,3 +113,93 @@ def test_config3_full_append(ops, O, wl, cuda, bench):
     assert torch.equal(one.pool, two.pool)
     ring2 = two.ring.cpu().numpy().view(np.uint16)
     assert np.array_equal(live_ring_values(ring, st, lengths), live_ring_values(ring2, st, lengths))
+
+
+def _oracle_of(O, cache, w, sample, bits=None):
+    """The oracle state of sampled sequences of a GPU-built cache: their pages
+    gathered into a compact pool (block tables renumbered), their ring rows
+    (ring rows of the GPU cache = batch rows) in sample order."""
+    bits = w.bits if bits is None else bits
+    bt = w.block_tables[sample]
+    used = [bt[i, bt[i] >= 0] for i in range(len(sample))]
+    pages = np.unique(np.concatenate(used))
+    remap = np.full(w.num_pages, -1, np.int32)
+    remap[pages] = np.arange(len(pages), dtype=np.int32)
+    bt_c = np.where(bt >= 0, remap[np.maximum(bt, 0)], -1).astype(np.int32)
+    st = O.PagedState(w.D, w.group, w.residual, bits, w.Hkv, len(pages), len(sample))
+    idx = torch.from_numpy(pages.astype(np.int64)).to(cache.pool.device)
+    st.pool = np.ascontiguousarray(cache.pool[idx].cpu().numpy())
+    rows = torch.tensor(sample, dtype=torch.long, device=cache.ring.device)
+    st.ring = np.ascontiguousarray(cache.ring[rows].cpu().numpy().view(np.uint16))
+    return st, bt_c
+
+
+def _q(wl, w, cuda, seed_add=1):
+    rng = np.random.default_rng(w.seed + seed_add)
+    return torch.from_numpy(wl.f32_to_bf16_bits(rng.standard_normal((w.B, w.Hq, w.D))).view(
+        np.int16)).view(torch.bfloat16).to(cuda)
+
+
+def test_config4_full_batch(ops, O, wl, cuda, bench):
+    """Config 4 (B=8, 131072-token contexts, Hq=64, Hkv=8): every pair spans
+    hundreds of warps and merges in the slot-parallel merge kernel; two
+    sampled sequences against the oracle, and the token-split layout (two
+    ranges plus the residual, merged) against the one-call decode."""
+    w = wl.config4(seed=4000)
+    cache, bt = bench.build_gpu_cache(ops, w, cuda, torch)
+    lens = torch.from_numpy(w.lengths).to(cuda)
+    q = _q(wl, w, cuda)
+    scale = 1 / math.sqrt(w.D)
+    max_ctx = int(w.lengths.max())
+    assert ops.decode_launches(w.B, w.Hq, max_ctx) == 2
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = ops.paged_decode(cache, q, bt, lens, max_ctx, scale=scale, out_dtype=torch.float32,
+                           err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    sample = [0, 5]
+    st, bt_c = _oracle_of(O, cache, w, sample)
+    ref = st.decode(q.float().cpu().numpy()[sample], bt_c, w.lengths[sample], scale, n_threads=16)
+    check_close(out.cpu().numpy()[sample], ref)
+
+    # token split as the multi-GPU layout runs it: ranges [0, 100), [100, n)
+    # of the 512-token splits, the second with the residual
+    n = (O.PagedState(w.D, w.group, w.residual, w.bits, w.Hkv, 1, 1).nq(max_ctx) + 511) // 512
+    ml = torch.empty((2, w.B, w.Hq, 2), dtype=torch.float32, device=cuda)
+    o = torch.empty((2, w.B, w.Hq, w.D), dtype=torch.float32, device=cuda)
+    for r, (lo, hi) in enumerate(((0, 100), (100, n))):
+        ws = torch.zeros(ops.decode_range_workspace_bytes(w.B, w.Hq, w.D, lo, hi),
+                         dtype=torch.uint8, device=cuda)
+        ops.paged_decode_range(cache, q, bt, lens, lo, hi, r == 1, ml[r], o[r], ws, scale=scale,
+                               err=err)
+    merged = ops.merge_partials(ml, o, torch.empty_like(out))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.allclose(merged, out, atol=2e-3, rtol=2e-3)
+
+
+def test_config5_full_batch(ops, O, wl, cuda, bench):
+    """Config 5 (B=256, log-uniform 128-32768 contexts; sequences 0-127 INT4,
+    128-255 INT2, each half one call with the merge fused): the longest and
+    the shortest sequence of each half against the oracle."""
+    w = wl.config5(seed=5000)
+    scale = 1 / math.sqrt(w.D)
+    for bits, seqs in ((4, np.arange(0, w.B // 2)), (2, np.arange(w.B // 2, w.B))):
+        sub = wl.subset(w, seqs, bits=bits)
+        cache, bt = bench.build_gpu_cache(ops, sub, cuda, torch)
+        lens = torch.from_numpy(sub.lengths).to(cuda)
+        q = _q(wl, sub, cuda)
+        max_ctx = int(sub.lengths.max())
+        assert ops.decode_launches(sub.B, sub.Hq, max_ctx) == 1
+        err = torch.zeros(1, dtype=torch.int32, device=cuda)
+        out = ops.paged_decode(cache, q, bt, lens, max_ctx, scale=scale,
+                               out_dtype=torch.float32, err=err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        sample = [int(np.argmax(sub.lengths)), int(np.argmin(sub.lengths))]
+        st, bt_c = _oracle_of(O, cache, sub, sample, bits)
+        ref = st.decode(q.float().cpu().numpy()[sample], bt_c, sub.lengths[sample], scale,
+                        n_threads=16)
+        check_close(out.cpu().numpy()[sample], ref)
+        del cache
+        torch.cuda.empty_cache()

@@ -185,7 +185,9 @@ def decode_range_workspace_bytes(num_seqs: int, num_q_heads: int, head_dim: int,
 
 
 def decode_launches(num_seqs: int, num_q_heads: int, max_context_len: int) -> int:
-    """Kernel launches one paged_decode call makes (1, or 2 beyond 64K tokens)."""
+    """Kernel launches one paged_decode call makes: 1 (merge fused into the
+    decode kernel), or 2 when num_seqs * num_q_heads < 1024 (a separate merge
+    kernel spreads the merge of few, long pairs over the GPU)."""
     return int(L.lib().tkv_decode_launches(num_seqs, num_q_heads, max_context_len))
 
 
