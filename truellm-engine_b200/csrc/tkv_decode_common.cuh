@@ -23,6 +23,35 @@ struct WarpState {
 #pragma unroll
     for (int i = 0; i < D / 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   }
+  // Adds the value-zero correction into the accumulator (o += w / oscale,
+  // w = 0; the result oscale * o + w is unchanged).  The encoded value codes
+  // carry an offset beta (1024 or 64 for INT4) that the correction removes:
+  // until it is added, o holds beta * sum(p') and rounds at that magnitude,
+  // so a state that runs over thousands of tokens folds it in every few pages.
+  // Each thread's w covers only its token rows (lanes of equal lane & 3 hold
+  // the rest), so it is summed over those lanes first; o covers all tokens.
+  __device__ __forceinline__ void fold(float inv_oscale) {
+    constexpr int MB_PER_VG = (D / 16) / NVG;
+    float c[NVG][2];
+#pragma unroll
+    for (int v = 0; v < NVG; ++v)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        float x = w[v][hh];
+        x += __shfl_xor_sync(0xffffffffu, x, 4);
+        x += __shfl_xor_sync(0xffffffffu, x, 8);
+        x += __shfl_xor_sync(0xffffffffu, x, 16);
+        c[v][hh] = x * inv_oscale;
+        w[v][hh] = 0.f;
+      }
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        o[i][hh] += c[i / MB_PER_VG][hh];
+        o[i][2 + hh] += c[i / MB_PER_VG][hh];
+      }
+  }
 };
 
 // Online-softmax update for NP 16-token tiles.  s[p][4]: raw S^T accumulators

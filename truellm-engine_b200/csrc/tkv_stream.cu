@@ -58,16 +58,23 @@ namespace tkv {
 #ifndef TKV_STREAM_STAGES
 #define TKV_STREAM_STAGES 3
 #endif
+// pages between folds of the value-zero correction into the accumulator
+// (WarpState::fold): bounds the code offset a long run carries in fp32
+#ifndef TKV_STREAM_FOLD_PAGES
+#define TKV_STREAM_FOLD_PAGES 16
+#endif
 
 constexpr int kRcCost = TKV_STREAM_RC_COST;
 constexpr int kMinCost = TKV_STREAM_MIN_COST;
 constexpr int kWPC = TKV_STREAM_WPC;
 constexpr int kWarpsPerSM = TKV_STREAM_WARPS_PER_SM;
+constexpr int kFoldPages = TKV_STREAM_FOLD_PAGES;
 // Bound on the warps of one launch used to size the workspace (148 SMs x 16);
 // a launch uses min(resident warps, what the workspace's slots allow).
 constexpr int kStreamMaxWarps = 148 * 16;
 constexpr int kMaxDevices = 64;
 static_assert(kWarpsPerSM % kWPC == 0, "whole CTAs per SM");
+static_assert(kFoldPages % 2 == 0, "folds fall on step boundaries (1 or 2 pages a step)");
 
 // Stage layout: a quantised step (NP page bodies, then the key-group meta when
 // the step starts a group) or one half (K or V block) of a residual chunk.
@@ -676,6 +683,7 @@ __global__ void __launch_bounds__(32 * kWPC, kWarpsPerSM / kWPC)
             }
           }
         }
+        if (((u + 1) * NP) % kFoldPages == 0) st.fold(1.f / VEnc<BITS>::kScale);
         __syncwarp();
         advance();
       } else {
