@@ -19,6 +19,9 @@ residual_length = 32
 """
 
 PAGED = """
+[inference]
+backend = "cuda"
+
 [inference.kv_cache]
 type_k = "kivi4"
 type_v = "kivi4"
@@ -34,8 +37,9 @@ def test_defaults_match_the_reference_schema():
     cfg = CF.parse("")
     assert (cfg.kv_kivi.enabled, cfg.kv_kivi.bits, cfg.kv_kivi.residual_length) == (False, 8, 128)
     assert (cfg.kv_cache.type_k, cfg.kv_cache.type_v, cfg.kv_cache.size_mb) == ("f16", "f16", 0)
+    assert cfg.backend == "cpu"
     assert CF.validate(cfg) is None
-    assert not cfg.paged_kivi and not cfg.compression_pass
+    assert not cfg.paged_kivi and not cfg.compression_pass and cfg.kivi_path is None
 
 
 def test_fp16_cache_with_the_compression_pass():
@@ -43,12 +47,14 @@ def test_fp16_cache_with_the_compression_pass():
     assert cfg.kv_kivi.enabled and cfg.kv_kivi.bits == 4 and cfg.kv_kivi.residual_length == 32
     assert cfg.compression_pass and not cfg.paged_kivi
     assert CF.validate(cfg) is None
+    assert cfg.kivi_path == "pass"
+    assert CF.parse(FP16_PASS.replace('"cuda"', '"cpu"')).kivi_path is None
 
 
 def test_paged_kivi_cache():
     cfg = CF.parse(PAGED)
     assert cfg.paged_kivi and cfg.paged_bits == 4 and not cfg.compression_pass
-    assert CF.validate(cfg) is None
+    assert CF.validate(cfg) is None and cfg.kivi_path == "paged"
     cfg2 = CF.parse(PAGED.replace("kivi4", "kivi2"))
     assert cfg2.paged_bits == 2 and CF.validate(cfg2) is None
 
@@ -59,6 +65,8 @@ def test_paged_kivi_cache():
     ('[inference.kv_cache]\ntype_k = "kivi4"\ntype_v = "f16"', "both type_k and type_v"),
     ('[inference.kv_cache]\ntype_k = "kivi4"\ntype_v = "kivi2"', "both type_k and type_v"),
     (PAGED.replace("group_size = 128", "group_size = 96"), "group_size must be"),
+    (PAGED.replace('backend = "cuda"', 'backend = "cpu"'), 'need inference.backend = "cuda"'),
+    ('[inference]\nbackend = "vulkan"', "backend 'vulkan' is not recognised"),
 ])
 def test_validation_messages(text, msg):
     assert msg in CF.validate(CF.parse(text))

@@ -1,8 +1,9 @@
 """The config switches that select this path, read the way the reference reads
-them (src/config.cpp: parse_kv_cache :78-86, the kv_kivi block :215-224,
-validation :562-568; defaults from include/truellm/config_schema.h:46-50,
-121-129).
+them (src/host/config/config.cpp: backend :143, parse_kv_cache :78-86, the
+kv_kivi block :215-224, validation :558-568; defaults from
+include/truellm/config_schema.h:46-50, 121-129, 204).
 
+    [inference]                       backend: "cpu" | "ggml" | "cuda"
     [inference.compression.kv_kivi]   enabled, bits, residual_length, (group_size)
     [inference.kv_cache]              type_k / type_v: "f16" | "q8_0" | "q4_0" and,
                                       for this path, "kivi4" | "kivi2"
@@ -54,6 +55,20 @@ class KvCacheConfig:
 class PathConfig:
     kv_kivi: KiviConfig = field(default_factory=KiviConfig)
     kv_cache: KvCacheConfig = field(default_factory=KvCacheConfig)
+    backend: str = "cpu"         # inference.backend (config_schema.h:204)
+
+    @property
+    def kivi_path(self) -> Optional[str]:
+        """Which KIVI path the config selects: "paged" (the paged KIVI cache),
+        "pass" (the per-vector pass over the fp16 cache, built whenever
+        kv_kivi is enabled, cuda_engine.cpp:193-200 -- the CUDA engine does
+        not read kv_cache.type_k/type_v) or None (the CPU/ggml backends,
+        whose quantised caches are q8_0/q4_0)."""
+        if self.backend != "cuda":
+            return None
+        if self.paged_kivi:
+            return "paged"
+        return "pass" if self.compression_pass else None
 
     @property
     def paged_kivi(self) -> bool:
@@ -90,6 +105,7 @@ def parse(doc: Union[str, Path, Mapping[str, Any]]) -> PathConfig:
         data = dict(doc)
     cfg = PathConfig()
     inf = data.get("inference", {})
+    cfg.backend = _get(inf, "backend", cfg.backend, str)
     kc = inf.get("kv_cache")
     if kc is not None:
         cfg.kv_cache.type_k = _get(kc, "type_k", cfg.kv_cache.type_k, str)
@@ -111,6 +127,8 @@ def parse(doc: Union[str, Path, Mapping[str, Any]]) -> PathConfig:
 def validate(cfg: PathConfig) -> Optional[str]:
     """The reference's checks on these keys (config.cpp:562-568), extended with
     the paged KIVI types; returns the error message or None."""
+    if cfg.backend not in ("cpu", "ggml", "cuda"):
+        return f"inference.backend '{cfg.backend}' is not recognised (cpu|ggml|cuda)"
     for name, val in (("type_k", cfg.kv_cache.type_k), ("type_v", cfg.kv_cache.type_v)):
         if val not in KV_CACHE_TYPES:
             return (f"inference.kv_cache.{name} '{val}' is not recognised "
@@ -123,6 +141,8 @@ def validate(cfg: PathConfig) -> Optional[str]:
             return "inference.compression.kv_kivi.group_size must be 16, 32, 64 or 128"
         if cfg.kv_kivi.residual_length < 0:
             return "inference.compression.kv_kivi.residual_length must be >= 0"
+        if cfg.backend != "cuda":
+            return 'inference.kv_cache: kivi4/kivi2 need inference.backend = "cuda"'
     return None
 
 
