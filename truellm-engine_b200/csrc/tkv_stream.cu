@@ -58,6 +58,11 @@ namespace tkv {
 #ifndef TKV_STREAM_STAGES
 #define TKV_STREAM_STAGES 3
 #endif
+// most quantised pages per ring stage and softmax step (capped by the pages
+// of one key group)
+#ifndef TKV_STREAM_PAGES
+#define TKV_STREAM_PAGES 2
+#endif
 // pages between folds of the value-zero correction into the accumulator
 // (WarpState::fold): bounds the code offset a long run carries in fp32
 #ifndef TKV_STREAM_FOLD_PAGES
@@ -81,7 +86,10 @@ static_assert(kFoldPages % 2 == 0, "folds fall on step boundaries (1 or 2 pages 
 template <int D, int BITS, int G>
 struct SFmt {
   using F = Fmt<D, BITS, G>;
-  static constexpr int META_OFF = F::NP * F::BODY;
+  static constexpr int NP = F::PPG < TKV_STREAM_PAGES ? F::PPG : TKV_STREAM_PAGES;
+  static_assert(F::PPG % NP == 0, "steps do not straddle key groups");
+  static_assert(NP <= 4, "at most four page copies per stage");
+  static constexpr int META_OFF = NP * F::BODY;
   // The key-group meta arrives as MCH chunks of 16 bytes; each thread reads
   // the CH channel words of its tig chunk, so a 16-byte pad after every tig
   // chunk puts the four tig chunks in different banks.
@@ -285,7 +293,7 @@ __global__ void __launch_bounds__(32 * kWPC, kWarpsPerSM / kWPC)
     decode_stream_kernel(StreamArgs a) {
   using F = Fmt<D, BITS, G>;
   using SF = SFmt<D, BITS, G>;
-  constexpr int NP = F::NP, NVG = F::NVG, PPG = F::PPG, ST = SF::ST, SB = SF::SB;
+  constexpr int NP = SF::NP, NVG = F::NVG, PPG = F::PPG, ST = SF::ST, SB = SF::SB;
   extern __shared__ __align__(128) uint8_t smem_all[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
   const int wid = blockIdx.x * kWPC + warp;
@@ -469,12 +477,16 @@ __global__ void __launch_bounds__(32 * kWPC, kWarpsPerSM / kWPC)
       }
       const int p0 = __shfl_sync(0xffffffffu, pid, pg - pgb);
       const int p1 = NP > 1 ? __shfl_sync(0xffffffffu, pid, pg - pgb + 1) : p0;
+      const int p2 = NP > 2 ? __shfl_sync(0xffffffffu, pid, pg - pgb + 2) : p0;
+      const int p3 = NP > 3 ? __shfl_sync(0xffffffffu, pid, pg - pgb + 3) : p0;
       const uint8_t* ph = a.pool + static_cast<int64_t>(d.h) * F::PB;
       const int64_t ps = static_cast<int64_t>(Hkv) * F::PB;
       if (lane == 0) {
         mbar_arrive_expect_tx(bar, NP * F::BODY);
         bulk_g2s_hint(dst, ph + p0 * ps, F::BODY, bar, pol);
         if (NP > 1) bulk_g2s_hint(dst + F::BODY, ph + p1 * ps, F::BODY, bar, pol);
+        if (NP > 2) bulk_g2s_hint(dst + 2 * F::BODY, ph + p2 * ps, F::BODY, bar, pol);
+        if (NP > 3) bulk_g2s_hint(dst + 3 * F::BODY, ph + p3 * ps, F::BODY, bar, pol);
       }
       if (pg == gs || isu == d.u0) {
         // the group's key meta: lane l brings chunk l of [D][step, zero]
