@@ -352,7 +352,8 @@ def decode_plan(args, wl, ops, torch, dev, rank, world):
         part = DecodePart(ops, wl, torch, w, dev, "one sequence")
         dec = SH.TokenSplitDecoder(1, w.Hq, w.D, part.max_ctx, w.residual, w.group, dev)
         alg = wl.token_split_bytes(w, dec.lo, dec.hi, dec.last)
-        return ([part], 1, "strong", f"token-split x{world} (all-gather of partials + merge)",
+        return ([part], 1, "strong",
+                f"token-split x{world} (partials stored to every GPU over NVLink, then merged)",
                 alg, dec, w)
     # config5: 256 sequences balanced by tokens; sequences 0-127 INT4, 128-255 INT2
     w = make_workload(wl, "config5", 0)
@@ -388,8 +389,9 @@ def run_kivi(args):
         args, wl, ops, torch, dev, rank, world)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
-    # the token split is launch-bound (range decode, reduce, two all-gathers,
-    # merge per step): its step is captured once in a CUDA graph and replayed
+    # the token split is launch-bound (range decode, reduce + publish to the
+    # peers, wait + merge per step): its step is captured once in a CUDA graph
+    # and replayed
     graph = None
     if dec is not None:
         p0 = parts[0]
@@ -564,9 +566,9 @@ def run_kivi(args):
     achieved = alg_bytes / t_split / 1e9
     traffic = (ncu_traffic(f"decode_stream_{args.workload}", "decode_stream",
                            "dram_bytes_per_launch") if world == 1 else None)
-    # our kernel launches per step: the token split runs three (split kernel
-    # and reduce of the range, merge) besides NCCL's all-gathers; otherwise one
-    # or two per decode call (ops.decode_launches)
+    # our kernel launches per step: the token split runs three (range decode,
+    # its reduce + publish to the peers, wait + merge); otherwise one or two
+    # per decode call (ops.decode_launches)
     n_launch = (3 if dec is not None else
                 sum(ops.decode_launches(p.w.B, p.w.Hq, p.max_ctx) for p in parts))
 
@@ -608,7 +610,7 @@ def run_kivi(args):
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": traffic,
                          "kernel": "decode_stream_kernel<128,%d,128>%s" % (
-                             w.bits, " (range) + stream_merge_kernel + all-gather + merge_kernel"
+                             w.bits, " (range) + stream_merge_kernel (publish) + ex_merge_kernel"
                              if dec is not None else
                              " + stream_merge_kernel" if n_launch > len(parts) else
                              " (merge fused)"),
@@ -618,9 +620,11 @@ def run_kivi(args):
             "clocks": clocks,
         }
         print(json.dumps(line))
-    if graph is not None:  # a graph holding NCCL calls goes before the group
+    if graph is not None:  # a graph holding collectives goes before the group
         torch.cuda.synchronize()
         del graph
+    if dec is not None:  # peer mappings are released collectively
+        dec.close()
     if world > 1 or dist.is_initialized():
         dist.barrier()
         dist.destroy_process_group()

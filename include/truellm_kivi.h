@@ -273,9 +273,8 @@ TKV_API int tkv_paged_decode_partials(const tkv_cache_t* cache, const void* q, i
  * with no token in the range gets m = -inf, l = 0, o = 0.  No counterpart in
  * the reference (paged_attention_v2.cu keeps every partition on one GPU).
  * workspace: tkv_decode_range_workspace_bytes(num_seqs, num_q_heads, D,
- * split_lo, split_hi) bytes (a smaller one of at least the 512-token-split
- * size makes the launch keep 512-token splits), 16-byte aligned, zeroed once
- * as for tkv_paged_decode (every call leaves its counters zero).  Two
+ * split_lo, split_hi) bytes, 16-byte aligned, zeroed once as for
+ * tkv_paged_decode (every call leaves its counters zero).  Two
  * launches. */
 TKV_API int tkv_paged_decode_range(const tkv_cache_t* cache, const void* q, int q_dtype,
                                    const int32_t* block_tables, int max_blocks_per_seq,
@@ -306,6 +305,66 @@ TKV_API int tkv_paged_prefill(const tkv_cache_t* cache, const void* q, int q_dty
  * (paged_attention_v2.cu:132-170) into out [num_seqs, num_q_heads, D]. */
 TKV_API int tkv_merge_partials(const float* part_ml, const float* part_o, int n_slots, int num_seqs,
                        int num_q_heads, int head_dim, void* out, int out_dtype, void* stream);
+
+/* ---------------------------------------------------------------- */
+/* Token-split decode over peer memory (GPUs of one node)             */
+/* ---------------------------------------------------------------- */
+/* Replaces the all-gather of split-KV partials that a token-split decode
+ * needs (the reference's collective plumbing, multi_gpu.cpp:200-230, has no
+ * split-KV path): every GPU stores its one-slot partial straight into every
+ * peer's exchange buffer over NVLink from the kernel that reduces it, raises
+ * a flag there, and merges the slots of all GPUs once their flags are up.
+ * No NCCL call and no multicast.
+ *
+ * Exchange buffer of one GPU (tkv_exchange_buffer_bytes, allocated with
+ * tkv_device_alloc so it can be shared, zeroed): a 256-byte header (flags
+ * [2][TKV_MAX_PEERS] u32 written by the peers, then this GPU's step and
+ * arrival counters) and two parity sets of world x num_seqs x num_q_heads
+ * rows of (m, l, pad, pad, o[D]) f32.  Consecutive steps alternate sets, so a
+ * GPU may run one step ahead of a peer without overwriting what the peer has
+ * not merged yet. */
+#define TKV_MAX_PEERS 8
+#define TKV_IPC_HANDLE_BYTES 64
+
+typedef struct tkv_exchange {
+  int world;                    /* GPUs in the exchange, 1..TKV_MAX_PEERS        */
+  int rank;                     /* this GPU's index in [0, world)                 */
+  void* buffers[TKV_MAX_PEERS]; /* buffers[r]: GPU r's exchange buffer as mapped
+                                   in this process (buffers[rank] = own)          */
+} tkv_exchange_t;
+
+TKV_API size_t tkv_exchange_buffer_bytes(int world, int num_seqs, int num_q_heads,
+                                         int head_dim);
+/* Zeroed device memory that can be shared with other processes
+ * (cudaMalloc + cudaMemset), and its release. */
+TKV_API int tkv_device_alloc(size_t bytes, void** ptr);
+TKV_API int tkv_device_free(void* ptr);
+/* CUDA IPC: the TKV_IPC_HANDLE_BYTES handle of an allocation from
+ * tkv_device_alloc, opened in another process on the same node (peer access
+ * enabled), and closed. */
+TKV_API int tkv_ipc_get_handle(const void* ptr, void* handle);
+TKV_API int tkv_ipc_open_handle(const void* handle, void** ptr);
+TKV_API int tkv_ipc_close_handle(void* ptr);
+
+/* This GPU's share of the token split (the arguments of
+ * tkv_paged_decode_range), reduced to one partial per (sequence, q head) and
+ * published to every GPU of the exchange.  A GPU whose range is empty
+ * (split_hi == split_lo and include_residual == 0) publishes empty partials.
+ * Every GPU of the exchange makes the same calls in the same order. */
+TKV_API int tkv_exchange_decode_range(const tkv_cache_t* cache, const void* q, int q_dtype,
+                                      const int32_t* block_tables, int max_blocks_per_seq,
+                                      const int32_t* seq_lens, const int32_t* seq_slots,
+                                      int num_seqs, int num_q_heads, float scale, int split_lo,
+                                      int split_hi, int include_residual,
+                                      const tkv_exchange_t* ex, void* workspace,
+                                      size_t workspace_bytes, int* err_flag, void* stream);
+/* Waits (bounded: about 2 s, then TKV_ERR_TIMEOUT in *err_flag and a zero
+ * output) until every GPU has published this step, merges the world slots by
+ * log-sum-exp into out [num_seqs, num_q_heads, head_dim] and advances this
+ * GPU's step.  One launch. */
+TKV_API int tkv_exchange_merge(const tkv_exchange_t* ex, int num_seqs, int num_q_heads,
+                               int head_dim, void* out, int out_dtype, int* err_flag,
+                               void* stream);
 
 /* ---------------------------------------------------------------- */
 /* Page allocator (host)                                              */

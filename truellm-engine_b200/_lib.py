@@ -27,6 +27,8 @@ TKV_ERR_BAD_LENGTH = 0x4
 TKV_ERR_TIMEOUT = 0x8
 
 TKV_NOALLOC_SCRATCH_BYTES = 16 << 20
+TKV_MAX_PEERS = 8
+TKV_IPC_HANDLE_BYTES = 64
 
 
 class TkvFormat(C.Structure):
@@ -44,6 +46,11 @@ class TkvCache(C.Structure):
         ("pool", C.c_void_p), ("ring", C.c_void_p), ("num_pages", C.c_int32),
         ("max_seqs", C.c_int32), ("fmt", TkvFormat),
     ]
+
+
+class TkvExchange(C.Structure):
+    _fields_ = [("world", C.c_int32), ("rank", C.c_int32),
+                ("buffers", C.c_void_p * TKV_MAX_PEERS)]
 
 
 class TruellmKernelManifest(C.Structure):
@@ -95,6 +102,17 @@ SIGNATURES = {
                                       _i32, _i32, _f32, _i32, _i32, _i32, _vp, _vp, _vp, _sz,
                                       _vp, _vp]),
     "tkv_merge_partials": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _i32, _vp]),
+    "tkv_exchange_buffer_bytes": (_sz, [_i32, _i32, _i32, _i32]),
+    "tkv_device_alloc": (_i32, [_sz, C.POINTER(_vp)]),
+    "tkv_device_free": (_i32, [_vp]),
+    "tkv_ipc_get_handle": (_i32, [_vp, _vp]),
+    "tkv_ipc_open_handle": (_i32, [_vp, C.POINTER(_vp)]),
+    "tkv_ipc_close_handle": (_i32, [_vp]),
+    "tkv_exchange_decode_range": (_i32, [C.POINTER(TkvCache), _vp, _i32, _vp, _i32, _vp, _vp,
+                                         _i32, _i32, _f32, _i32, _i32, _i32,
+                                         C.POINTER(TkvExchange), _vp, _sz, _vp, _vp]),
+    "tkv_exchange_merge": (_i32, [C.POINTER(TkvExchange), _i32, _i32, _i32, _vp, _i32, _vp,
+                                  _vp]),
     "tkv_paged_prefill": (_i32, [C.POINTER(TkvCache), _vp, _i32, _vp, _i32, _vp, _vp, _i32, _vp,
                                  _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp]),
     "tkv_allocator_create": (_i32, [C.POINTER(TkvFormat), _i32, _i32, _i32, C.POINTER(_vp)]),

@@ -391,6 +391,124 @@ int tkv_paged_decode_range(const tkv_cache_t* cache, const void* q, int q_dtype,
                               workspace_bytes, out_ml, as_stream(stream));
 }
 
+// ---------------------------------------------------------------------------
+// token split over peer memory
+// ---------------------------------------------------------------------------
+static_assert(TKV_MAX_PEERS == kMaxPeers, "exchange struct and kernels agree");
+static_assert(sizeof(cudaIpcMemHandle_t) == TKV_IPC_HANDLE_BYTES, "IPC handle size");
+static_assert(kExStateOff >= 2 * kMaxPeers * 4 && kExStateOff + 12 <= kExHeader, "header layout");
+
+size_t tkv_exchange_buffer_bytes(int world, int num_seqs, int num_q_heads, int head_dim) {
+  if (world < 1 || world > kMaxPeers || num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0)
+    return 0;
+  return kExHeader + 2ull * static_cast<size_t>(world) * static_cast<size_t>(num_seqs) *
+                         static_cast<size_t>(num_q_heads) * (kExRowPad + head_dim) * sizeof(float);
+}
+
+// The device view of an exchange; TKV_OK when it is well formed.
+static int ex_pub(ExPub& x, const tkv_exchange_t* ex, int num_seqs, int num_q_heads, int D) {
+  if (!ex || ex->world < 1 || ex->world > kMaxPeers || ex->rank < 0 || ex->rank >= ex->world)
+    return TKV_INVALID_ARGUMENT;
+  if (num_seqs <= 0 || num_q_heads <= 0 || static_cast<long long>(num_seqs) * num_q_heads >
+                                               static_cast<long long>(INT_MAX))
+    return TKV_INVALID_ARGUMENT;
+  memset(&x, 0, sizeof(x));
+  for (int r = 0; r < ex->world; ++r) {
+    if (!ex->buffers[r] || !aligned16(ex->buffers[r])) return TKV_INVALID_ARGUMENT;
+    x.set0[r] = reinterpret_cast<float*>(static_cast<uint8_t*>(ex->buffers[r]) + kExHeader);
+    x.flags[r] = static_cast<uint32_t*>(ex->buffers[r]);
+  }
+  x.state = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ex->buffers[ex->rank]) + kExStateOff);
+  x.world = ex->world;
+  x.rank = ex->rank;
+  x.rows = num_seqs * num_q_heads;
+  x.rs = kExRowPad + D;
+  x.set_floats = static_cast<long long>(ex->world) * x.rows * x.rs;
+  return TKV_OK;
+}
+
+int tkv_device_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return TKV_INVALID_ARGUMENT;
+  *ptr = nullptr;
+  if (cudaMalloc(ptr, bytes) != cudaSuccess) return TKV_OUT_OF_MEMORY;
+  if (cudaMemset(*ptr, 0, bytes) != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return TKV_BACKEND_ERROR;
+  }
+  return TKV_OK;
+}
+
+int tkv_device_free(void* ptr) {
+  if (!ptr) return TKV_OK;
+  return cudaFree(ptr) == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
+}
+
+int tkv_ipc_get_handle(const void* ptr, void* handle) {
+  if (!ptr || !handle) return TKV_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)) != cudaSuccess) return TKV_BACKEND_ERROR;
+  memcpy(handle, &h, sizeof(h));
+  return TKV_OK;
+}
+
+int tkv_ipc_open_handle(const void* handle, void** ptr) {
+  if (!handle || !ptr) return TKV_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess
+             ? TKV_OK
+             : TKV_BACKEND_ERROR;
+}
+
+int tkv_ipc_close_handle(void* ptr) {
+  if (!ptr) return TKV_INVALID_ARGUMENT;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
+}
+
+int tkv_exchange_decode_range(const tkv_cache_t* cache, const void* q, int q_dtype,
+                              const int32_t* block_tables, int max_blocks_per_seq,
+                              const int32_t* seq_lens, const int32_t* seq_slots, int num_seqs,
+                              int num_q_heads, float scale, int split_lo, int split_hi,
+                              int include_residual, const tkv_exchange_t* ex, void* workspace,
+                              size_t workspace_bytes, int* err_flag, void* stream) {
+  if (!cache_ok(cache) || split_lo < 0 || split_hi < split_lo) return TKV_INVALID_ARGUMENT;
+  const int D = cache->fmt.head_dim;
+  ExPub pub;
+  int st = ex_pub(pub, ex, num_seqs, num_q_heads, D);
+  if (st != TKV_OK) return st;
+  if (split_hi == split_lo && !include_residual)  // nothing here: empty partials
+    return launch_ex_publish_empty(pub, D, as_stream(stream));
+  if (!workspace || !aligned16(workspace) ||
+      workspace_bytes < stream_workspace_bytes(num_seqs, num_q_heads, D))
+    return TKV_INVALID_ARGUMENT;
+  StreamArgs a;
+  st = stream_args(a, cache, q, q_dtype, block_tables, max_blocks_per_seq, seq_lens, seq_slots,
+                   num_seqs, num_q_heads, scale, err_flag);
+  if (st != TKV_OK) return st;
+  constexpr int kMaxSplit = INT_MAX / kSplitPages;
+  a.pg_lo = split_lo < kMaxSplit ? split_lo * kSplitPages : INT_MAX;
+  a.pg_hi = split_hi < kMaxSplit ? split_hi * kSplitPages : INT_MAX;
+  a.include_residual = include_residual ? 1 : 0;
+  a.mode = kStreamPartials;
+  a.out = nullptr;
+  a.out_dtype = TKV_F32;
+  return launch_stream_decode(a, D, cache->fmt.bits, cache->fmt.group_size, workspace,
+                              workspace_bytes, nullptr, as_stream(stream), &pub);
+}
+
+int tkv_exchange_merge(const tkv_exchange_t* ex, int num_seqs, int num_q_heads, int head_dim,
+                       void* out, int out_dtype, int* err_flag, void* stream) {
+  if (!out || (head_dim != 64 && head_dim != 128)) return TKV_INVALID_ARGUMENT;
+  if (out_dtype != TKV_F32 && out_dtype != TKV_F16 && out_dtype != TKV_BF16)
+    return TKV_NOT_IMPLEMENTED;
+  ExPub pub;
+  const int st = ex_pub(pub, ex, num_seqs, num_q_heads, head_dim);
+  if (st != TKV_OK) return st;
+  return launch_ex_merge(pub, head_dim, out, out_dtype, err_flag, as_stream(stream));
+}
+
 int tkv_paged_prefill(const tkv_cache_t* cache, const void* q, int q_dtype, void* out,
                       int out_dtype, const int32_t* cu_q, const int32_t* block_tables,
                       int max_blocks_per_seq, const int32_t* seq_lens, const int32_t* seq_slots,

@@ -371,14 +371,82 @@ struct StreamArgs {
   int* err;
 };
 
+// Token-split exchange over peer memory (tkv_exchange.cu).  Exchange buffer
+// of one GPU: [header 256 B: u32 flags[2][kMaxPeers] (flags[s][r] = step + 1
+// once GPU r has published step `step` of parity s), u32 counters at
+// kExStateOff: step, publish arrivals, merge arrivals][set 0][set 1]; a set
+// holds world x rows rows of kExRowPad + D floats: (m log2, l, -, -, o[D]).
+constexpr int kMaxPeers = 8;
+constexpr int kExHeader = 256;
+constexpr int kExStateOff = 128;
+constexpr int kExRowPad = 4;
+struct ExPub {
+  float* set0[kMaxPeers];      // each GPU's set 0 (its buffer + kExHeader), mapped here
+  uint32_t* flags[kMaxPeers];  // each GPU's flags[2][kMaxPeers]
+  uint32_t* state;             // this GPU's counters: [0] step, [1] publish and [2] merge arrivals
+  int world, rank, rows, rs;   // rows = num_seqs * num_q_heads; rs = kExRowPad + D floats
+  long long set_floats;        // world * rows * rs
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+
+// Stores the reduced row (M, L, O) of row i0 into slot `rank` of every GPU's
+// set (step parity) -- called by all threads of a CTA for their channels --
+// then counts the CTA; the last CTA of the launch raises this GPU's flag on
+// every GPU.  `step` is the exchange step read at kernel start.
+__device__ __forceinline__ void ex_store_row(const ExPub& x, uint32_t step, int64_t i0, int c,
+                                             float o) {
+  const long long off = (step & 1u) * x.set_floats + (static_cast<long long>(x.rank) * x.rows + i0) * x.rs;
+  for (int r = 0; r < x.world; ++r) x.set0[r][off + kExRowPad + c] = o;
+}
+__device__ __forceinline__ void ex_store_ml(const ExPub& x, uint32_t step, int64_t i0, float m,
+                                            float l) {
+  const long long off = (step & 1u) * x.set_floats + (static_cast<long long>(x.rank) * x.rows + i0) * x.rs;
+  for (int r = 0; r < x.world; ++r) {
+    x.set0[r][off] = m;
+    x.set0[r][off + 1] = l;
+  }
+}
+__device__ __forceinline__ void ex_signal(const ExPub& x, uint32_t step) {
+  __threadfence_system();  // this thread's peer stores before the CTA's arrival
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int n = gridDim.x * gridDim.y;
+    if (atomicAdd(&x.state[1], 1u) == n - 1) {
+      x.state[1] = 0u;
+      __threadfence_system();  // every CTA's stores (ordered by their fences) before the flags
+      for (int r = 0; r < x.world; ++r)
+        st_release_sys(&x.flags[r][(step & 1u) * kMaxPeers + x.rank], step + 1u);
+    }
+  }
+}
+
 // Workspace of the stream decode for these sizes (the query functions' value).
 size_t stream_workspace_bytes(int num_seqs, int num_q_heads, int head_dim);
 // Launches the stream decode: fused (one launch) or partials + merge (two
-// launches; out_ml != nullptr: the merge writes unnormalised (M, L) and O).
+// launches; out_ml != nullptr: the merge writes unnormalised (M, L) and O;
+// pub != nullptr: the merge publishes them to the exchange instead).
 int launch_stream_decode(StreamArgs a, int head_dim, int bits, int group, void* workspace,
-                         size_t workspace_bytes, float* out_ml, cudaStream_t stream);
+                         size_t workspace_bytes, float* out_ml, cudaStream_t stream,
+                         const ExPub* pub = nullptr);
 // 1 or 2: the launches tkv_paged_decode makes for these sizes.
 int stream_decode_launches(int num_seqs, int num_q_heads);
+// tkv_exchange.cu: empty partials of a GPU without splits; the wait + merge.
+int launch_ex_publish_empty(const ExPub& pub, int head_dim, cudaStream_t stream);
+int launch_ex_merge(const ExPub& pub, int head_dim, void* out, int out_dtype, int* err,
+                    cudaStream_t stream);
 
 int launch_ref_kivi(int mode, const void* in, void* out, int n_vecs, int head_dim, int n_outliers,
                     int group_size, cudaStream_t stream);

@@ -821,15 +821,20 @@ __global__ void __launch_bounds__(32 * kWPC, kWarpsPerSM / kWPC)
 // sequence); warp w merges a block of the pair's slots (merge_heads with
 // RED), then the warps' results are combined in shared memory with the same
 // log-sum-exp rule.  out_ml != nullptr: the unnormalised (M, L) to out_ml and
-// O to out (f32, the tkv_paged_decode_range output); else O / L to out.
+// O to out (f32, the tkv_paged_decode_range output); pub.world > 0: the same
+// unnormalised row into this GPU's slot on every GPU of the exchange, then
+// the flag (tkv_exchange_decode_range); else O / L to out.
 // ---------------------------------------------------------------------------
 constexpr int kStreamMergeWarps = 8;
 
 __global__ void __launch_bounds__(32 * kStreamMergeWarps)
     stream_merge_kernel(const int2* __restrict__ pair_info, const float* __restrict__ part_ml,
                         const float* __restrict__ part_o, int num_q_heads, int grp, int D,
-                        void* __restrict__ out, int out_dtype, float* __restrict__ out_ml) {
+                        void* __restrict__ out, int out_dtype, float* __restrict__ out_ml,
+                        ExPub pub) {
   __shared__ float s_ml[kStreamMergeWarps][2];
+  const bool publish = pub.world > 0;
+  const uint32_t step = publish ? *reinterpret_cast<volatile uint32_t*>(pub.state) : 0u;
   __shared__ float s_o[kStreamMergeWarps][128];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hq = blockIdx.x, b = blockIdx.y;
@@ -863,7 +868,9 @@ __global__ void __launch_bounds__(32 * kStreamMergeWarps)
       if (m != -INFINITY) acc = fmaf(s_o[w][c], fast_exp2(m - M), acc);
     }
     const int64_t oi = i0 * D + c;
-    if (out_ml) {
+    if (publish) {
+      ex_store_row(pub, step, i0, c, acc);
+    } else if (out_ml) {
       static_cast<float*>(out)[oi] = acc;
     } else {
       const float v = acc * inv;
@@ -875,7 +882,10 @@ __global__ void __launch_bounds__(32 * kStreamMergeWarps)
         static_cast<__half*>(out)[oi] = __float2half_rn(v);
     }
   }
-  if (out_ml && threadIdx.x == 0) {
+  if (publish) {
+    if (threadIdx.x == 0) ex_store_ml(pub, step, i0, M, L);
+    ex_signal(pub, step);
+  } else if (out_ml && threadIdx.x == 0) {
     out_ml[i0 * 2 + 0] = M;
     out_ml[i0 * 2 + 1] = L;
   }
@@ -962,7 +972,8 @@ int stream_decode_launches(int num_seqs, int num_q_heads) {
 }
 
 int launch_stream_decode(StreamArgs a, int head_dim, int bits, int group, void* workspace,
-                         size_t workspace_bytes, float* out_ml, cudaStream_t stream) {
+                         size_t workspace_bytes, float* out_ml, cudaStream_t stream,
+                         const ExPub* pub) {
   const size_t hdr = header_bytes(a.num_seqs, a.num_q_heads);
   const size_t slot_bytes = static_cast<size_t>(a.grp) * (head_dim + 2) * sizeof(float);
   if (workspace_bytes < hdr + slot_bytes) return TKV_INVALID_ARGUMENT;
@@ -986,7 +997,7 @@ int launch_stream_decode(StreamArgs a, int head_dim, int bits, int group, void* 
   dim3 grid(a.num_q_heads, a.num_seqs);
   stream_merge_kernel<<<grid, 32 * kStreamMergeWarps, 0, stream>>>(
       a.pair_info, a.part_ml, a.part_o, a.num_q_heads, a.grp, head_dim, a.out,
-      out_ml ? TKV_F32 : a.out_dtype, out_ml);
+      out_ml ? TKV_F32 : a.out_dtype, out_ml, pub ? *pub : ExPub{});
   return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
 }
 

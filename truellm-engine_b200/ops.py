@@ -341,6 +341,85 @@ def merge_partials(part_ml: torch.Tensor, part_o: torch.Tensor, out: torch.Tenso
 
 
 # ---------------------------------------------------------------------------
+# token split over peer memory (tkv_exchange_*)
+# ---------------------------------------------------------------------------
+def exchange_buffer_bytes(world: int, num_seqs: int, num_q_heads: int, head_dim: int) -> int:
+    return int(L.lib().tkv_exchange_buffer_bytes(world, num_seqs, num_q_heads, head_dim))
+
+
+class DeviceBuffer:
+    """Zeroed device memory from tkv_device_alloc (shareable over CUDA IPC) on
+    the current device; freed by close()."""
+
+    def __init__(self, nbytes: int):
+        p = C.c_void_p()
+        L.check("tkv_device_alloc", L.lib().tkv_device_alloc(int(nbytes), C.byref(p)))
+        self.ptr, self.nbytes = int(p.value), int(nbytes)
+
+    def close(self) -> None:
+        if self.ptr:
+            L.check("tkv_device_free", L.lib().tkv_device_free(C.c_void_p(self.ptr)))
+            self.ptr = 0
+
+
+def ipc_handle(ptr: int) -> bytes:
+    h = (C.c_char * L.TKV_IPC_HANDLE_BYTES)()
+    L.check("tkv_ipc_get_handle", L.lib().tkv_ipc_get_handle(C.c_void_p(ptr), h))
+    return bytes(h)
+
+
+def ipc_open(handle: bytes) -> int:
+    h = (C.c_char * L.TKV_IPC_HANDLE_BYTES).from_buffer_copy(handle)
+    p = C.c_void_p()
+    L.check("tkv_ipc_open_handle", L.lib().tkv_ipc_open_handle(h, C.byref(p)))
+    return int(p.value)
+
+
+def ipc_close(ptr: int) -> None:
+    L.check("tkv_ipc_close_handle", L.lib().tkv_ipc_close_handle(C.c_void_p(ptr)))
+
+
+def exchange_struct(world: int, rank: int, buffers) -> L.TkvExchange:
+    ex = L.TkvExchange()
+    ex.world, ex.rank = int(world), int(rank)
+    for r, b in enumerate(buffers):
+        ex.buffers[r] = int(b)
+    return ex
+
+
+def exchange_decode_range(cache: KiviPagedCache, q: torch.Tensor, block_tables: torch.Tensor,
+                          seq_lens: torch.Tensor, split_lo: int, split_hi: int,
+                          include_residual: bool, ex: L.TkvExchange,
+                          workspace: Optional[torch.Tensor], scale: Optional[float] = None,
+                          seq_slots: Optional[torch.Tensor] = None,
+                          err: Optional[torch.Tensor] = None, stream=None) -> None:
+    """This GPU's range of a token split (see paged_decode_range), reduced and
+    stored into every GPU's exchange buffer, flag raised."""
+    _need_cuda(q, block_tables, seq_lens)
+    B, Hq, D = q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    c = cache.c_struct()
+    ws_bytes = 0 if workspace is None else int(workspace.numel() * workspace.element_size())
+    L.check("tkv_exchange_decode_range", L.lib().tkv_exchange_decode_range(
+        C.byref(c), _ptr(q.contiguous()), _DT[q.dtype], _ptr(block_tables),
+        int(block_tables.shape[1]), _ptr(seq_lens), _ptr(seq_slots), B, Hq, float(scale),
+        int(split_lo), int(split_hi), int(bool(include_residual)), C.byref(ex), _ptr(workspace),
+        ws_bytes, _ptr(err), C.c_void_p(_stream(stream))))
+
+
+def exchange_merge(ex: L.TkvExchange, out: torch.Tensor, err: Optional[torch.Tensor] = None,
+                   stream=None) -> torch.Tensor:
+    """Waits for every GPU's partials of this step and merges them into out
+    [B, Hq, D] (f32, f16 or bf16)."""
+    _need_cuda(out)
+    B, Hq, D = out.shape
+    L.check("tkv_exchange_merge", L.lib().tkv_exchange_merge(
+        C.byref(ex), B, Hq, D, _ptr(out), _DT[out.dtype], _ptr(err), C.c_void_p(_stream(stream))))
+    return out
+
+
+# ---------------------------------------------------------------------------
 # page and ring-row moves (copy_blocks / swap_blocks, cache_kernels.cu:107-168)
 # ---------------------------------------------------------------------------
 def _mapping(mapping: torch.Tensor) -> int:

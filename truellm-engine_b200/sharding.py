@@ -12,16 +12,21 @@ the work of one sequence is split by tokens):
 * by tokens of one sequence (long context) -- each rank owns a contiguous
   range of the 512-token quantised splits (`split_ranges`; the fp16 residual
   window belongs to the last rank).  Each rank computes its range and reduces
-  it to one unnormalised partial per q head in the same launch
-  (`tkv_paged_decode_range`), the one-slot partials are all-gathered, and
-  every rank merges them with the log-sum-exp rule of paged_attention_v2.cu
-  :132-170 (`tkv_merge_partials`).  The exchange is `(m, l)` plus `o[D]` fp32
-  per q head per rank: kilobytes per step.
+  it to one unnormalised partial per q head; the kernel that reduces it
+  stores it straight into every rank's exchange buffer over NVLink (CUDA IPC
+  mappings, `PeerExchange`) and raises a flag, and one more kernel per rank
+  waits for all flags and merges the world slots with the log-sum-exp rule of
+  paged_attention_v2.cu:132-170 (`tkv_exchange_decode_range`,
+  `tkv_exchange_merge`).  The exchange is `(m, l)` plus `o[D]` fp32 per q head
+  per rank: kilobytes per step.  The same layout over NCCL (all-gather of the
+  one-slot partials of `tkv_paged_decode_range`, then `tkv_merge_partials`)
+  remains as `exchange="nccl"`.
 
 The functions here are plain host logic over torch tensors and
-`torch.distributed`; `TokenSplitDecoder` calls the CUDA entry points and
-therefore needs the library and CUDA tensors, while `gather_slots` and the
-planning helpers also run on CPU tensors with the gloo backend.
+`torch.distributed`; `TokenSplitDecoder` and `PeerExchange` call the CUDA
+entry points and therefore need the library and CUDA tensors (the group of a
+`PeerExchange` only swaps IPC handles, so gloo serves), while `gather_slots`
+and the planning helpers also run on CPU tensors with the gloo backend.
 """
 from __future__ import annotations
 
@@ -112,22 +117,72 @@ def gather_slots(part_ml: torch.Tensor, part_o: torch.Tensor,
     return ml, o
 
 
+class PeerExchange:
+    """One exchange buffer per rank (`tkv_device_alloc`), mapped into every
+    other rank of `group` over CUDA IPC: the `tkv_exchange_t` of this rank.
+    The group only carries the IPC handles (any backend).  `close()` unmaps
+    and frees (collective)."""
+
+    def __init__(self, batch: int, n_q_heads: int, head_dim: int,
+                 group: Optional[dist.ProcessGroup] = None):
+        self.ops = importlib.import_module("truellm-engine_b200.ops")
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        nbytes = self.ops.exchange_buffer_bytes(self.world, batch, n_q_heads, head_dim)
+        if nbytes == 0:
+            raise ValueError(f"no exchange for world {self.world}")
+        self.own = self.ops.DeviceBuffer(nbytes)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, self.ops.ipc_handle(self.own.ptr), group=group)
+        self.opened = {r: self.ops.ipc_open(h) for r, h in enumerate(handles) if r != self.rank}
+        buffers = [self.own.ptr if r == self.rank else self.opened[r] for r in range(self.world)]
+        self.ex = self.ops.exchange_struct(self.world, self.rank, buffers)
+        dist.barrier(group=group)  # every mapping exists before any rank publishes
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no rank still stores into a buffer
+        for p in self.opened.values():
+            self.ops.ipc_close(p)
+        self.opened = {}
+        dist.barrier(group=self.group)
+        self.own.close()
+
+
+def local_exchanges(world: int, batch: int, n_q_heads: int, head_dim: int):
+    """`world` exchanges whose buffers all live on the current GPU, for one
+    process that plays every rank in turn (each rank's publish before any
+    merge, so no kernel waits on one that has not run).  Returns (structs,
+    buffers); close the buffers when done."""
+    ops = importlib.import_module("truellm-engine_b200.ops")
+    nbytes = ops.exchange_buffer_bytes(world, batch, n_q_heads, head_dim)
+    bufs = [ops.DeviceBuffer(nbytes) for _ in range(world)]
+    return [ops.exchange_struct(world, r, [b.ptr for b in bufs]) for r in range(world)], bufs
+
+
 class TokenSplitDecoder:
     """Decode of sequences whose quantised splits are spread over the ranks
     of `group` by `split_ranges` (each rank's cache must hold the pages of its
     range; the last rank also holds the fp16 residual window).
 
-    Every rank computes its range and reduces it inside the same launch to one
-    partial per (sequence, q head) (`tkv_paged_decode_range`); the one-slot
-    partials of all ranks are all-gathered (`(2 + D) * 4` bytes per q head per
-    rank) and every rank merges them into `out` (`tkv_merge_partials`).
-    Buffers are allocated once per (batch, heads, context) shape.
+    exchange="peer" (default): every rank reduces its range to one partial
+    per (sequence, q head) and stores it into every rank's exchange buffer
+    over NVLink (`tkv_exchange_decode_range`), then merges the world slots
+    once all have arrived (`tkv_exchange_merge`): two launches per step per
+    rank, no NCCL.  exchange="nccl": the one-slot partials of
+    `tkv_paged_decode_range` are all-gathered (`(2 + D) * 4` bytes per q head
+    per rank) and merged by `tkv_merge_partials`.  Buffers are allocated once
+    per (batch, heads, context) shape; `close()` releases the peer mappings.
     """
 
     def __init__(self, batch: int, n_q_heads: int, head_dim: int, max_context_len: int,
                  residual: int, group_size: int, device,
-                 group: Optional[dist.ProcessGroup] = None):
+                 group: Optional[dist.ProcessGroup] = None, exchange: str = "peer"):
         self.ops = importlib.import_module("truellm-engine_b200.ops")
+        if exchange not in ("peer", "nccl"):
+            raise ValueError(f"exchange must be 'peer' or 'nccl', not {exchange!r}")
+        self.exchange = exchange
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -135,6 +190,8 @@ class TokenSplitDecoder:
         self.lo, self.hi = split_ranges(n, self.world)[self.rank]
         self.last = self.rank == self.world - 1
         self.active = self.hi > self.lo or self.last
+        self.peer = (PeerExchange(batch, n_q_heads, head_dim, group)
+                     if exchange == "peer" else None)
         shape = (1, batch, n_q_heads)
         self.part_ml = torch.empty(shape + (2,), dtype=torch.float32, device=device)
         self.part_o = torch.zeros(shape + (head_dim,), dtype=torch.float32, device=device)
@@ -147,9 +204,19 @@ class TokenSplitDecoder:
         self.all_o = torch.empty((self.world,) + shape[1:] + (head_dim,), dtype=torch.float32,
                                  device=device)
 
+    def close(self) -> None:
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
+
     def __call__(self, cache, q: torch.Tensor, block_tables: torch.Tensor,
                  seq_lens: torch.Tensor, out: torch.Tensor, scale: Optional[float] = None,
                  err: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        if self.peer is not None:
+            self.ops.exchange_decode_range(
+                cache, q, block_tables, seq_lens, self.lo, self.hi, self.last, self.peer.ex,
+                self.ws, scale=scale, err=err, stream=stream)
+            return self.ops.exchange_merge(self.peer.ex, out, err=err, stream=stream)
         if self.active:
             self.ops.paged_decode_range(
                 cache, q, block_tables, seq_lens, self.lo, self.hi, self.last,
