@@ -58,6 +58,8 @@ def parse():
                     choices=["config2", "config3", "config4", "config4b", "config5", "prefill"])
     ap.add_argument("--impl", default="kivi", choices=["kivi", "reference"])
     ap.add_argument("--cpu-sample", type=int, default=64, help="sequences in the CPU sample")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="token split (config4b): partials over peer memory or NCCL all-gathers")
     return ap.parse_args()
 
 
@@ -350,11 +352,12 @@ def decode_plan(args, wl, ops, torch, dev, rank, world):
     if name == "config4b":  # run B: one sequence split by tokens over the ranks
         w = wl.config4(seed=4000, B=1)
         part = DecodePart(ops, wl, torch, w, dev, "one sequence")
-        dec = SH.TokenSplitDecoder(1, w.Hq, w.D, part.max_ctx, w.residual, w.group, dev)
+        dec = SH.TokenSplitDecoder(1, w.Hq, w.D, part.max_ctx, w.residual, w.group, dev,
+                                   exchange=args.exchange)
         alg = wl.token_split_bytes(w, dec.lo, dec.hi, dec.last)
-        return ([part], 1, "strong",
-                f"token-split x{world} (partials stored to every GPU over NVLink, then merged)",
-                alg, dec, w)
+        how = ("partials stored to every GPU over NVLink, then merged" if args.exchange == "peer"
+               else "NCCL all-gather of partials, then merged")
+        return ([part], 1, "strong", f"token-split x{world} ({how})", alg, dec, w)
     # config5: 256 sequences balanced by tokens; sequences 0-127 INT4, 128-255 INT2
     w = make_workload(wl, "config5", 0)
     mine = SH.balance_sequences(w.lengths, world)[rank]
@@ -610,7 +613,8 @@ def run_kivi(args):
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": traffic,
                          "kernel": "decode_stream_kernel<128,%d,128>%s" % (
-                             w.bits, " (range) + stream_merge_kernel (publish) + ex_merge_kernel"
+                             w.bits, (" (range) + stream_merge_kernel (publish) + ex_merge_kernel" if args.exchange == "peer"
+                              else " (range) + stream_merge_kernel + all-gather + merge_kernel")
                              if dec is not None else
                              " + stream_merge_kernel" if n_launch > len(parts) else
                              " (merge fused)"),

@@ -420,9 +420,11 @@ __device__ __forceinline__ void ex_store_ml(const ExPub& x, uint32_t step, int64
   }
 }
 __device__ __forceinline__ void ex_signal(const ExPub& x, uint32_t step) {
-  __threadfence_system();  // this thread's peer stores before the CTA's arrival
+  // the barrier orders the CTA's peer stores before thread 0's system fence
+  // (fences are cumulative), which orders them before the CTA's arrival
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const unsigned int n = gridDim.x * gridDim.y;
     if (atomicAdd(&x.state[1], 1u) == n - 1) {
       x.state[1] = 0u;

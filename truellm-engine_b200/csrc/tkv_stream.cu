@@ -44,9 +44,10 @@ namespace tkv {
 #ifndef TKV_STREAM_RC_COST
 #define TKV_STREAM_RC_COST 2
 #endif
-// fewest cost units per warp: small calls use fewer warps
+// fewest cost units per warp: small calls use fewer warps (a warp alone on
+// its SM runs a step in about 2 us, so short chains keep small calls short)
 #ifndef TKV_STREAM_MIN_COST
-#define TKV_STREAM_MIN_COST 32
+#define TKV_STREAM_MIN_COST 8
 #endif
 // independent warps per CTA, and resident warps per SM the register budget targets
 #ifndef TKV_STREAM_WPC
