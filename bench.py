@@ -355,7 +355,8 @@ def decode_plan(args, wl, ops, torch, dev, rank, world):
         dec = SH.TokenSplitDecoder(1, w.Hq, w.D, part.max_ctx, w.residual, w.group, dev,
                                    exchange=args.exchange)
         alg = wl.token_split_bytes(w, dec.lo, dec.hi, dec.last)
-        how = ("partials stored to every GPU over NVLink, then merged" if args.exchange == "peer"
+        how = ("one-call decode" if world == 1 else
+               "partials stored to every GPU over NVLink, then merged" if args.exchange == "peer"
                else "NCCL all-gather of partials, then merged")
         return ([part], 1, "strong", f"token-split x{world} ({how})", alg, dec, w)
     # config5: 256 sequences balanced by tokens; sequences 0-127 INT4, 128-255 INT2
@@ -572,7 +573,7 @@ def run_kivi(args):
     # our kernel launches per step: the token split runs three (range decode,
     # its reduce + publish to the peers, wait + merge); otherwise one or two
     # per decode call (ops.decode_launches)
-    n_launch = (3 if dec is not None else
+    n_launch = (3 if dec is not None and not dec.single else
                 sum(ops.decode_launches(p.w.B, p.w.Hq, p.max_ctx) for p in parts))
 
     line = None
@@ -615,7 +616,7 @@ def run_kivi(args):
                          "kernel": "decode_stream_kernel<128,%d,128>%s" % (
                              w.bits, (" (range) + stream_merge_kernel (publish) + ex_merge_kernel" if args.exchange == "peer"
                               else " (range) + stream_merge_kernel + all-gather + merge_kernel")
-                             if dec is not None else
+                             if dec is not None and not dec.single else
                              " + stream_merge_kernel" if n_launch > len(parts) else
                              " (merge fused)"),
                          "alg_bytes_per_launch": alg_bytes,

@@ -826,7 +826,10 @@ __global__ void __launch_bounds__(32 * kWPC, kWarpsPerSM / kWPC)
 // unnormalised row into this GPU's slot on every GPU of the exchange, then
 // the flag (tkv_exchange_decode_range); else O / L to out.
 // ---------------------------------------------------------------------------
-constexpr int kStreamMergeWarps = 8;
+#ifndef TKV_STREAM_MERGE_WARPS
+#define TKV_STREAM_MERGE_WARPS 8
+#endif
+constexpr int kStreamMergeWarps = TKV_STREAM_MERGE_WARPS;
 
 __global__ void __launch_bounds__(32 * kStreamMergeWarps)
     stream_merge_kernel(const int2* __restrict__ pair_info, const float* __restrict__ part_ml,

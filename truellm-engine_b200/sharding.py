@@ -166,6 +166,7 @@ class TokenSplitDecoder:
     of `group` by `split_ranges` (each rank's cache must hold the pages of its
     range; the last rank also holds the fp16 residual window).
 
+    One rank: the one-call decode (`tkv_paged_decode`).
     exchange="peer" (default): every rank reduces its range to one partial
     per (sequence, q head) and stores it into every rank's exchange buffer
     over NVLink (`tkv_exchange_decode_range`), then merges the world slots
@@ -190,15 +191,20 @@ class TokenSplitDecoder:
         self.lo, self.hi = split_ranges(n, self.world)[self.rank]
         self.last = self.rank == self.world - 1
         self.active = self.hi > self.lo or self.last
+        # one GPU: no split to exchange, the one-call decode
+        self.single = self.world == 1
+        self.max_context_len = max_context_len
         self.peer = (PeerExchange(batch, n_q_heads, head_dim, group)
-                     if exchange == "peer" else None)
+                     if exchange == "peer" and not self.single else None)
         shape = (1, batch, n_q_heads)
         self.part_ml = torch.empty(shape + (2,), dtype=torch.float32, device=device)
         self.part_o = torch.zeros(shape + (head_dim,), dtype=torch.float32, device=device)
         self.part_ml[..., 0] = float("-inf")  # a rank without splits contributes nothing
         self.part_ml[..., 1] = 0.0
         self.ws = torch.zeros(max(16, self.ops.decode_range_workspace_bytes(
-            batch, n_q_heads, head_dim, self.lo, self.hi)), dtype=torch.uint8, device=device)
+            batch, n_q_heads, head_dim, self.lo, self.hi),
+            self.ops.decode_workspace_bytes(batch, n_q_heads, head_dim, max_context_len)),
+            dtype=torch.uint8, device=device)
         self.all_ml = torch.empty((self.world,) + shape[1:] + (2,), dtype=torch.float32,
                                   device=device)
         self.all_o = torch.empty((self.world,) + shape[1:] + (head_dim,), dtype=torch.float32,
@@ -212,6 +218,10 @@ class TokenSplitDecoder:
     def __call__(self, cache, q: torch.Tensor, block_tables: torch.Tensor,
                  seq_lens: torch.Tensor, out: torch.Tensor, scale: Optional[float] = None,
                  err: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        if self.single:
+            return self.ops.paged_decode(cache, q, block_tables, seq_lens, self.max_context_len,
+                                         scale=scale, out=out, workspace=self.ws, err=err,
+                                         stream=stream)
         if self.peer is not None:
             self.ops.exchange_decode_range(
                 cache, q, block_tables, seq_lens, self.lo, self.hi, self.last, self.peer.ex,
