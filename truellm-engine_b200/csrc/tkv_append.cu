@@ -49,7 +49,11 @@ __device__ __forceinline__ bool append_lengths_ok(const AppendArgs& a, int L, in
          (int64_t)L + (c1 - c0) <= (int64_t)a.max_blocks * kPage;
 }
 
-constexpr int kFlushThreads = 128;
+// threads of a flush CTA (one CTA per key group, K or V, kv head, sequence)
+#ifndef TKV_FLUSH_THREADS
+#define TKV_FLUSH_THREADS 128
+#endif
+constexpr int kFlushThreads = TKV_FLUSH_THREADS;
 
 
 __device__ __forceinline__ float h2f(uint16_t h) {
