@@ -28,9 +28,14 @@
 // same order; ring tiles (the fp16 window) are scattered into that order.
 // The next tile's code words are loaded into registers before the current
 // tile's MMAs, so their latency overlaps them.
+#include <atomic>
+
 #include "tkv_frag.cuh"
+#include "tkv_umma.cuh"
 
 namespace tkv {
+
+constexpr int kMaxPrefillDevices = 64;
 
 namespace {
 
@@ -432,6 +437,488 @@ __global__ void __launch_bounds__(32 * NW, 2) prefill_cta_kernel(PrefillArgs a) 
   }
 }
 
+// ---------------------------------------------------------------------------
+// The same attention on the 5th-generation tensor cores (tcgen05): one CTA of
+// 4 warps per 128 query rows of a (sequence, kv head) (the MMA's M), 64-token
+// KV tiles.  Per tile the CTA's threads dequantise the tile's four 16-token
+// pages (or fp16 ring chunks) exactly, as above, straight into the K-major
+// shared-memory operand layouts of tkv_umma.cuh: K [64 tokens][D channels]
+// (channels in the code-unpack order, Q staged in the same order) and V^T
+// [D channels][64 tokens].  One thread issues S = Q K^T (D/16 MMAs, N = 64)
+// into tensor memory; each thread then owns one query row: it loads the row's
+// 64 scores with tcgen05.ld, masks them causally, runs the online softmax
+// (exp2 domain, lazy rescale: when a warp's running maxima move, its rows of O
+// are rescaled in tensor memory) and stores the row's weights P as f16 into a
+// third operand tile; one thread issues O += P V (4 MMAs, N = D) into tensor
+// memory.  The next tile's code words are loaded into registers while S is
+// computed and the softmax runs; two CTAs per SM overlap one CTA's MMAs with
+// the other's CUDA-core work.  Tensor memory: S in columns [0, 64), O in
+// [64, 64 + D).
+// ---------------------------------------------------------------------------
+constexpr int kUmmaRows = 128;  // query rows per CTA
+constexpr int kUmmaTN = 64;     // tokens per KV tile
+
+template <int D>
+struct UmmaSmem {
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + kUmmaRows * D * 2;
+  static constexpr int V_OFF = K_OFF + kUmmaTN * D * 2;
+  static constexpr int P_OFF = V_OFF + D * kUmmaTN * 2;
+  static constexpr int BAR_OFF = P_OFF + kUmmaRows * kUmmaTN * 2;
+  static constexpr int BYTES = BAR_OFF + 32;
+  static constexpr uint32_t TCOLS = kUmmaTN + D <= 128 ? 128u : 256u;
+};
+
+template <int D, int BITS, int G>
+__global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
+  using F = Fmt<D, BITS, G>;
+  using SM = UmmaSmem<D>;
+  constexpr int NT = 128, TN = kUmmaTN, NSUB = TN / kPage;
+  constexpr int WPR = D * BITS / 32;          // key-code words per token row
+  constexpr int CPW = 32 / BITS;              // channels per key word
+  constexpr int HP = CPW / 2;                 // f16 pairs per key word
+  constexpr int KW = kPage * WPR;             // key (and value) code words per page
+  constexpr int KPT = (KW + NT - 1) / NT;     // code words per thread
+  constexpr int MVEC = CPW / 4;               // 16-byte key-meta vectors per word's channels
+  constexpr int VMW = BITS == 4 ? 4 : 8;      // value (step, zero) words per value word
+  constexpr int RV = 2 * D;                   // 16-byte vectors per ring K (or V) block
+  constexpr int RPT = (RV + NT - 1) / NT;
+  constexpr int PSLOT = KPT * (2 + VMW), RSLOT = RPT * 8;
+  constexpr int SLOT = PSLOT > RSLOT ? PSLOT : RSLOT;  // registers of one 16-token sub-tile
+  // key groups of one tile: sub-tile s uses key meta km[s / PPG] (G < 64) or km[0]
+  constexpr int NKM = F::PPG >= NSUB ? 1 : NSUB / F::PPG;
+  static_assert(F::PPG % NSUB == 0 || NSUB % F::PPG == 0, "tiles and key groups nest");
+  static_assert(NT % WPR == 0, "a thread's key words share their channels");
+  static_assert(KPT * NT == KW || KW < NT, "code words per thread");
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* const Qs = smem + SM::Q_OFF;
+  uint8_t* const Ks = smem + SM::K_OFF;
+  uint8_t* const Vs = smem + SM::V_OFF;
+  uint8_t* const Ps = smem + SM::P_OFF;
+  uint64_t* const bars = reinterpret_cast<uint64_t*>(smem + SM::BAR_OFF);  // S done, O done
+  uint32_t* const tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  const int tid = threadIdx.x, warp = tid >> 5;
+
+  const int64_t bid = blockIdx.x;
+  const int rt = a.n_rt - 1 - (int)(bid % a.n_rt);
+  const int bh = (int)(bid / a.n_rt);
+  const int b = bh / a.n_kv_heads, h = bh - b * a.n_kv_heads;
+  const int L = a.seq_lens[b];
+  const int q0 = a.cu_q[b], n = a.cu_q[b + 1] - q0;
+  if (L < 0 || L > a.max_blocks * kPage || n < 0 || n > L || n > a.max_q || q0 < 0 ||
+      q0 + n > a.total_q) {
+    if (rt == 0 && h == 0 && tid == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
+    return;
+  }
+  const int rows = n * a.grp, r0 = rt * kUmmaRows;
+  if (r0 >= rows) return;
+  const int rho = r0 + tid;
+  const bool valid = rho < rows;
+  const int qi = valid ? rho / a.grp : 0;
+  const int plim = valid ? L - n + qi : -1;  // causal limit of this thread's row
+  const int kv_end = L - n + min(rows - 1, r0 + kUmmaRows - 1) / a.grp + 1;
+  const int64_t qrow = ((int64_t)(q0 + qi) * a.num_q_heads + h * a.grp + (valid ? rho % a.grp : 0)) * D;
+  const int nq = nq_len(L, a.residual, G);
+  const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
+  const int n_pages = min(nq, (kv_end + kPage - 1) / kPage * kPage) / kPage;
+  const int n_chunks = kv_end > nq ? (kv_end - nq + kPage - 1) / kPage : 0;
+  const int n16 = n_pages + n_chunks;
+  const int n_tiles = (n16 + NSUB - 1) / NSUB;
+
+  const int n_read = min(nq / kPage, (n_pages + F::PPG - 1) / F::PPG * F::PPG);
+  bool bad = false;
+  for (int p = tid; p < n_read; p += NT) {
+    const int ph = bt[p];
+    bad |= ph < 0 || ph >= a.num_pages;
+  }
+  if (__syncthreads_or(bad)) {
+    if (tid == 0) set_err(a.err, TKV_ERR_BAD_PAGE);
+    return;
+  }
+  int row = 0;
+  if (n_chunks > 0) {
+    row = a.seq_slots ? a.seq_slots[b] : b;
+    if (row < 0 || row >= a.max_seqs) {
+      if (tid == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
+      return;
+    }
+  }
+
+  // ---- tensor memory, barriers, the Q operand ----
+  if (warp == 0) umma::alloc(tslot, SM::TCOLS);
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+#pragma unroll
+  for (int k8 = 0; k8 < D; k8 += 8) {
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c0 = kchan_at<BITS>(k8 + 2 * e), c1 = kchan_at<BITS>(k8 + 2 * e + 1);
+      w[e] = pack_h2(valid ? load_qv(a, qrow + c0) : 0.f, valid ? load_qv(a, qrow + c1) : 0.f);
+    }
+    *reinterpret_cast<uint4*>(Qs + umma::umma_off(tid, k8, D)) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  umma::fence_smem_to_async();
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *tslot;
+  const uint32_t tS = tmem, tO = tmem + TN;
+  const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+
+  const uint8_t* pool_h = a.pool + (int64_t)h * F::PB;
+  const int64_t page_stride = (int64_t)a.n_kv_heads * F::PB;
+  constexpr int CHUNK = 2 * F::RBLK;
+  const uint8_t* ring_base =
+      reinterpret_cast<const uint8_t*>(a.ring) +
+      (((int64_t)row * a.n_kv_heads + h) * (a.ring_cap / kPage)) * CHUNK;
+  const int kc0 = (tid % WPR) * CPW;  // first channel (tile order) of this thread's key words
+
+  // ---- registers of the next tile: NSUB sub-tiles of code words or ring vectors ----
+  uint32_t reg[NSUB][SLOT];
+  uint4 km[NKM][MVEC];
+  uint4 kml[MVEC];  // key meta of the group the previous tile ended in
+#pragma unroll
+  for (int v = 0; v < MVEC; ++v) kml[v] = make_uint4(0, 0, 0, 0);
+  auto load_tile = [&](int jt) {
+#pragma unroll
+    for (int s = 0; s < NSUB; ++s) {
+      const int j = jt * NSUB + s;
+      if (j < n_pages) {
+        const uint8_t* pg = pool_h + (int64_t)bt[j] * page_stride;
+#pragma unroll
+        for (int k = 0; k < KPT; ++k) {
+          const int u = tid + k * NT;
+          if (u >= KW) continue;
+          reg[s][k * (2 + VMW)] = __ldg(reinterpret_cast<const uint32_t*>(pg) + u);
+          const int l = u & 31, w = u >> 5;
+          reg[s][k * (2 + VMW) + 1] = __ldg(reinterpret_cast<const uint32_t*>(
+              pg + F::V_CODES_OFF + ((w / F::VW) * 32 + l) * 4 * F::VW + (w % F::VW) * 4));
+          const uint32_t* vmp = reinterpret_cast<const uint32_t*>(pg + F::V_META_OFF);
+          const int t0 = 2 * (l & 3);
+#pragma unroll
+          for (int x = 0; x < VMW; ++x) {
+            const int mb = BITS == 4 ? w : 2 * w + (x >> 2);
+            const int t = t0 + (x & 1) + 8 * ((x >> 1) & 1);
+            reg[s][k * (2 + VMW) + 2 + x] = __ldg(vmp + t * F::NVG + (16 * mb) / G);
+          }
+        }
+        const int ki = F::PPG >= NSUB ? 0 : s / (F::PPG >= NSUB ? 1 : F::PPG);
+        if (j % F::PPG == 0) {  // a new key group: this thread's channels
+          const int grp = j / F::PPG;
+#pragma unroll
+          for (int v = 0; v < MVEC; ++v) {
+            const int off = 4 * (kc0 + 4 * v);
+            const int ph = bt[grp * F::PPG + off / F::KMS];
+            km[ki][v] = __ldg(reinterpret_cast<const uint4*>(pool_h + (int64_t)ph * page_stride +
+                                                             F::BODY + off % F::KMS));
+          }
+        } else if (s == 0) {  // the group the previous tile ended in
+#pragma unroll
+          for (int v = 0; v < MVEC; ++v) km[0][v] = kml[v];
+        }
+      } else if (j < n16) {
+        const int t0 = nq + (j - n_pages) * kPage;
+        const uint8_t* ck = ring_base + (int64_t)((t0 % a.ring_cap) / kPage) * CHUNK;
+#pragma unroll
+        for (int k = 0; k < RPT; ++k) {
+          const int u = tid + k * NT;
+          if (u >= RV) continue;
+          const uint4 x = __ldg(reinterpret_cast<const uint4*>(ck) + u);
+          const uint4 y = __ldg(reinterpret_cast<const uint4*>(ck + F::RBLK) + u);
+          reg[s][8 * k + 0] = x.x; reg[s][8 * k + 1] = x.y; reg[s][8 * k + 2] = x.z; reg[s][8 * k + 3] = x.w;
+          reg[s][8 * k + 4] = y.x; reg[s][8 * k + 5] = y.y; reg[s][8 * k + 6] = y.z; reg[s][8 * k + 7] = y.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < MVEC; ++v) kml[v] = km[NKM - 1][v];
+  };
+
+  // dequantise the registers of tile jt into the K and V^T operand tiles
+  auto store_tile = [&](int jt) {
+#pragma unroll
+    for (int s = 0; s < NSUB; ++s) {
+      const int j = jt * NSUB + s;
+      const int tb = s * kPage;  // the sub-tile's first token in the tile
+      if (j < n_pages) {
+        const int ki = F::PPG >= NSUB ? 0 : s / (F::PPG >= NSUB ? 1 : F::PPG);
+        uint32_t mw[CPW];
+#pragma unroll
+        for (int v = 0; v < MVEC; ++v) {
+          mw[4 * v + 0] = km[ki][v].x; mw[4 * v + 1] = km[ki][v].y;
+          mw[4 * v + 2] = km[ki][v].z; mw[4 * v + 3] = km[ki][v].w;
+        }
+        uint32_t sp[HP], zp[HP];
+#pragma unroll
+        for (int i = 0; i < HP; ++i) {
+          sp[i] = __byte_perm(mw[i], mw[i + HP], 0x5410);
+          zp[i] = __byte_perm(mw[i], mw[i + HP], 0x7632);
+        }
+#pragma unroll
+        for (int k = 0; k < KPT; ++k) {
+          const int u = tid + k * NT;
+          if (u >= KW) continue;
+          const uint32_t x = reg[s][k * (2 + VMW)], x8 = x >> 8;
+          uint32_t hv[HP];
+#pragma unroll
+          for (int i = 0; i < HP; ++i) {
+            uint32_t c;
+            if (BITS == 4) {
+              c = (i & 1) ? code_pair<0x00F000F0u>(i < 2 ? x : x8)
+                          : code_pair<0x000F000Fu>(i < 2 ? x : x8);
+            } else {
+              const uint32_t y = i < 4 ? x : x8;
+              c = (i & 3) == 0 ? code_pair<0x00030003u>(y)
+                : (i & 3) == 1 ? code_pair<0x000C000Cu>(y)
+                : (i & 3) == 2 ? code_pair<0x00300030u>(y)
+                               : code_pair<0x00C000C0u>(y);
+            }
+            hv[i] = hfma2(c, sp[i], zp[i]);
+          }
+#pragma unroll
+          for (int q = 0; q < HP / 4; ++q)
+            *reinterpret_cast<uint4*>(Ks + umma::umma_off(tb + u / WPR, kc0 + 8 * q, D)) =
+                make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
+          // value word (lane l, word w): channels 16mb+gl and 16mb+8+gl, tokens
+          // tl, tl+1, tl+8, tl+9
+          const int l = u & 31, w = u >> 5, gl = l >> 2, tl = 2 * (l & 3);
+#pragma unroll
+          for (int half = 0; half < (BITS == 4 ? 1 : 2); ++half) {
+            const int mb = BITS == 4 ? w : 2 * w + half;
+            const uint32_t* m4 = &reg[s][k * (2 + VMW) + 2 + 4 * half];
+            const uint32_t s01 = __byte_perm(m4[0], m4[1], 0x5410), z01 = __byte_perm(m4[0], m4[1], 0x7632);
+            const uint32_t s89 = __byte_perm(m4[2], m4[3], 0x5410), z89 = __byte_perm(m4[2], m4[3], 0x7632);
+            uint32_t r[4];
+            if (BITS == 4 || half == 0)
+              value_frag<BITS, 0>(&reg[s][k * (2 + VMW) + 1], r);
+            else
+              value_frag<BITS, (BITS == 2 ? 1 : 0)>(&reg[s][k * (2 + VMW) + 1], r);
+            const uint32_t v0 = hfma2(hfma2(r[0], VCode<BITS>::kMul, VCode<BITS>::kAddLo), s01, z01);
+            const uint32_t v1 = hfma2(hfma2(r[1], VCode<BITS>::kMul, VCode<BITS>::kAddLo), s01, z01);
+            const uint32_t v2 = hfma2(hfma2(r[2], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
+            const uint32_t v3 = hfma2(hfma2(r[3], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
+            *reinterpret_cast<uint32_t*>(Vs + umma::umma_off(16 * mb + gl, tb + tl, TN)) = v0;
+            *reinterpret_cast<uint32_t*>(Vs + umma::umma_off(16 * mb + 8 + gl, tb + tl, TN)) = v1;
+            *reinterpret_cast<uint32_t*>(Vs + umma::umma_off(16 * mb + gl, tb + tl + 8, TN)) = v2;
+            *reinterpret_cast<uint32_t*>(Vs + umma::umma_off(16 * mb + 8 + gl, tb + tl + 8, TN)) = v3;
+          }
+        }
+      } else if (j < n16) {
+        const int t0 = nq + (j - n_pages) * kPage;
+#pragma unroll
+        for (int k = 0; k < RPT; ++k) {
+          const int u = tid + k * NT;
+          if (u >= RV) continue;
+          const int c16 = u >> 5, l = u & 31;
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const uint32_t kx = reg[s][8 * k + r], vx = reg[s][8 * k + 4 + r];
+            // K block: word r holds channels cc, cc+1 of token t
+            const int t = 8 * (r & 1) + (l >> 2), cc = 8 * (r >> 1) + 2 * (l & 3);
+            const int c = 16 * c16 + cc;
+            *reinterpret_cast<uint16_t*>(Ks + umma::umma_off(tb + t, kpos<BITS>(c), D)) =
+                static_cast<uint16_t>(kx & 0xffffu);
+            *reinterpret_cast<uint16_t*>(Ks + umma::umma_off(tb + t, kpos<BITS>(c + 1), D)) =
+                static_cast<uint16_t>(kx >> 16);
+            // V block: word r holds tokens tv, tv+1 of channel 16c16 + cv;
+            // tokens past the end (stale ring slots) become 0
+            const int tv = 8 * (r >> 1) + 2 * (l & 3), cv = 8 * (r & 1) + (l >> 2);
+            const uint32_t msk = (t0 + tv < L ? 0x0000ffffu : 0u) | (t0 + tv + 1 < L ? 0xffff0000u : 0u);
+            *reinterpret_cast<uint32_t*>(Vs + umma::umma_off(16 * c16 + cv, tb + tv, TN)) = vx & msk;
+          }
+        }
+      } else {
+        // past the last token of the CTA's rows: zero K rows and V^T columns
+        for (int i = tid; i < kPage * D / 8; i += NT) {
+          const int t = i / (D / 8), c8 = (i % (D / 8)) * 8;
+          *reinterpret_cast<uint4*>(Ks + umma::umma_off(tb + t, c8, D)) = make_uint4(0, 0, 0, 0);
+        }
+        for (int i = tid; i < D * 2; i += NT) {
+          const int c = i >> 1, t8 = (i & 1) * 8;
+          *reinterpret_cast<uint4*>(Vs + umma::umma_off(c, tb + t8, TN)) = make_uint4(0, 0, 0, 0);
+        }
+      }
+    }
+  };
+
+  constexpr uint32_t idS = umma::idesc_f16(kUmmaRows, TN, false);
+  constexpr uint32_t idO = umma::idesc_f16(kUmmaRows, D, false);
+  const float alpha = a.alpha;
+  float m_run = -INFINITY, l_run = 0.f;
+  bool ok = true;
+  load_tile(0);
+  for (int jt = 0; jt < n_tiles && ok; ++jt) {
+    if (jt > 0) {  // the previous tile's O += P V has read V^T and P
+      ok = mbar_wait(&bars[1], (jt - 1) & 1, a.err);
+      umma::fence_after_sync();
+      if (!__syncthreads_and(ok)) {
+        ok = false;
+        break;
+      }
+    }
+    store_tile(jt);
+    umma::fence_smem_to_async();
+    umma::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      umma::fence_after_sync();
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk)
+        umma::mma_f16(tS, umma::smem_desc(smem_u32(Qs) + 256 * kk, 128, 16 * D),
+                      umma::smem_desc(smem_u32(Ks) + 256 * kk, 128, 16 * D), idS, kk > 0);
+      umma::commit(&bars[0]);
+    }
+    if (jt + 1 < n_tiles) load_tile(jt + 1);  // in flight during S and the softmax
+    ok = mbar_wait(&bars[0], jt & 1, a.err);
+    umma::fence_after_sync();
+    if (!__syncthreads_and(ok)) {
+      ok = false;
+      break;
+    }
+    // the row's scores in two 32-column halves: a pass for the maximum, then
+    // one for the weights (tensor memory is read twice, the registers once)
+    const int tile0 = jt * TN;
+    const bool masked = tile0 + TN - 1 > plim;
+    auto load_half = [&](int hf, float (&x)[32]) {
+      umma::ld32(tS + lane_base + 32 * hf, x);
+      umma::wait_ld();
+      if (masked) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) x[c] = tile0 + 32 * hf + c <= plim ? x[c] : -INFINITY;
+      }
+    };
+    float mx = -INFINITY;
+#pragma unroll
+    for (int hf = 0; hf < TN / 32; ++hf) {
+      float x[32];
+      load_half(hf, x);
+#pragma unroll
+      for (int c = 0; c < 32; ++c) mx = fmaxf(mx, x[c]);
+    }
+    mx *= alpha;  // alpha > 0 keeps the order
+    const bool need = mx > m_run + kLazyLog2;
+    if (__any_sync(0xffffffffu, need)) {
+      const float mnew = need ? fmaxf(m_run, mx) : m_run;
+      const float f = m_run == -INFINITY ? 0.f : fast_exp2(m_run - mnew);
+      l_run *= f;
+      m_run = mnew;
+      if (jt > 0) {  // this warp's rows of O in tensor memory
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          float o[32];
+          umma::ld32(tO + lane_base + c0, o);
+          umma::wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c] *= f;
+          umma::st32(tO + lane_base + c0, o);
+        }
+        umma::wait_st();
+      }
+    }
+    const float nb = m_run == -INFINITY ? 0.f : -m_run;
+    float sum = 0.f;
+#pragma unroll
+    for (int hf = 0; hf < TN / 32; ++hf) {
+      float x[32];
+      load_half(hf, x);
+#pragma unroll
+      for (int c8 = 0; c8 < 32; c8 += 8) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = fast_exp2(fmaf(x[c8 + 2 * e], alpha, nb));
+          const float p1 = fast_exp2(fmaf(x[c8 + 2 * e + 1], alpha, nb));
+          sum += p0 + p1;
+          w[e] = pack_h2(p0, p1);
+        }
+        *reinterpret_cast<uint4*>(Ps + umma::umma_off(tid, 32 * hf + c8, TN)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    l_run += sum;
+    umma::fence_smem_to_async();
+    umma::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      umma::fence_after_sync();
+#pragma unroll
+      for (int kk = 0; kk < TN / 16; ++kk)
+        umma::mma_f16(tO, umma::smem_desc(smem_u32(Ps) + 256 * kk, 128, 16 * TN),
+                      umma::smem_desc(smem_u32(Vs) + 256 * kk, 128, 16 * TN), idO,
+                      jt > 0 || kk > 0);
+      umma::commit(&bars[1]);
+    }
+  }
+  if (ok && n_tiles > 0) {
+    ok = mbar_wait(&bars[1], (n_tiles - 1) & 1, a.err);
+    umma::fence_after_sync();
+  }
+  if (__syncthreads_and(ok) && n_tiles > 0) {
+    // ---- normalise and write this thread's row ----
+    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+#pragma unroll
+    for (int c0 = 0; c0 < D; c0 += 32) {
+      float o[32];
+      umma::ld32(tO + lane_base + c0, o);
+      umma::wait_ld();
+      if (valid) {
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+          const int64_t oi = qrow + c0 + c;
+          if (a.out_dtype == TKV_F32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + oi);
+            dst[0] = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+            dst[1] = make_float4(o[c + 4] * inv, o[c + 5] * inv, o[c + 6] * inv, o[c + 7] * inv);
+          } else if (a.out_dtype == TKV_BF16) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __nv_bfloat162 hh = __floats2bfloat162_rn(o[c + 2 * e] * inv, o[c + 2 * e + 1] * inv);
+              w[e] = *reinterpret_cast<const uint32_t*>(&hh);
+            }
+            *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + oi) =
+                make_uint4(w[0], w[1], w[2], w[3]);
+          } else {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) w[e] = pack_h2(o[c + 2 * e] * inv, o[c + 2 * e + 1] * inv);
+            *reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + oi) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+    }
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  if (warp == 0) umma::dealloc(tmem, SM::TCOLS);
+}
+
+template <int D, int BITS, int G>
+static int launch_prefill_umma_t(PrefillArgs a, cudaStream_t stream) {
+  using SM = UmmaSmem<D>;
+  const int64_t tiles = ((int64_t)a.max_q * a.grp + kUmmaRows - 1) / kUmmaRows;
+  const int64_t blocks = (int64_t)a.num_seqs * a.n_kv_heads * tiles;
+  if (blocks <= 0) return TKV_OK;
+  if (blocks > 0x7fffffffLL) return TKV_INVALID_ARGUMENT;
+  static std::atomic<int> attr_set[kMaxPrefillDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return TKV_BACKEND_ERROR;
+  if (dev < 0 || dev >= kMaxPrefillDevices || !attr_set[dev].load(std::memory_order_relaxed)) {
+    if (cudaFuncSetAttribute(prefill_umma_kernel<D, BITS, G>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, SM::BYTES) != cudaSuccess)
+      return TKV_BACKEND_ERROR;
+    if (dev >= 0 && dev < kMaxPrefillDevices) attr_set[dev].store(1, std::memory_order_relaxed);
+  }
+  a.n_rt = (int)tiles;
+  prefill_umma_kernel<D, BITS, G><<<(unsigned)blocks, 128, SM::BYTES, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
+}
+
 constexpr int kPrefillWarps = 4;  // 16 query rows each: 64 rows per CTA
 
 template <int D, int BITS, int G>
@@ -446,13 +933,18 @@ static int launch_prefill_t(PrefillArgs a, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
 }
 
+#ifdef TKV_PREFILL_MMA_SYNC
+#define TKV_PREFILL_LAUNCH launch_prefill_t
+#else
+#define TKV_PREFILL_LAUNCH launch_prefill_umma_t
+#endif
 template <int D, int BITS>
 static int launch_prefill_g(const PrefillArgs& a, int G, cudaStream_t stream) {
   switch (G) {
-    case 16: return launch_prefill_t<D, BITS, 16>(a, stream);
-    case 32: return launch_prefill_t<D, BITS, 32>(a, stream);
-    case 64: return launch_prefill_t<D, BITS, 64>(a, stream);
-    case 128: return launch_prefill_t<D, BITS, 128>(a, stream);
+    case 16: return TKV_PREFILL_LAUNCH<D, BITS, 16>(a, stream);
+    case 32: return TKV_PREFILL_LAUNCH<D, BITS, 32>(a, stream);
+    case 64: return TKV_PREFILL_LAUNCH<D, BITS, 64>(a, stream);
+    case 128: return TKV_PREFILL_LAUNCH<D, BITS, 128>(a, stream);
     default: return TKV_NOT_IMPLEMENTED;
   }
 }
