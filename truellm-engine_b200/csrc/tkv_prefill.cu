@@ -439,8 +439,9 @@ __global__ void __launch_bounds__(32 * NW, 2) prefill_cta_kernel(PrefillArgs a) 
 
 // ---------------------------------------------------------------------------
 // The same attention on the 5th-generation tensor cores (tcgen05): one CTA of
-// 4 warps per 128 query rows of a (sequence, kv head) (the MMA's M), 64-token
-// KV tiles.  Per tile the CTA's threads dequantise the tile's four 16-token
+// two warpgroups per 256 query rows of a (sequence, kv head), each warpgroup
+// owning 128 rows (the MMA's M) and its own S and O in tensor memory; 64-token
+// KV tiles shared by both.  Per tile the CTA's threads dequantise the tile's four 16-token
 // pages (or fp16 ring chunks) exactly, as above, straight into the K-major
 // shared-memory operand layouts of tkv_umma.cuh: K [64 tokens][D channels]
 // (channels in the code-unpack order, Q staged in the same order) and V^T
@@ -448,32 +449,43 @@ __global__ void __launch_bounds__(32 * NW, 2) prefill_cta_kernel(PrefillArgs a) 
 // into tensor memory; each thread then owns one query row: it loads the row's
 // 64 scores with tcgen05.ld, masks them causally, runs the online softmax
 // (exp2 domain, lazy rescale: when a warp's running maxima move, its rows of O
-// are rescaled in tensor memory) and stores the row's weights P as f16 into a
-// third operand tile; one thread issues O += P V (4 MMAs, N = D) into tensor
-// memory.  The next tile's code words are loaded into registers while S is
-// computed and the softmax runs; two CTAs per SM overlap one CTA's MMAs with
-// the other's CUDA-core work.  Tensor memory: S in columns [0, 64), O in
-// [64, 64 + D).
+// are rescaled in tensor memory) and stores the row's weights P as f16 into
+// its warpgroup's P tile; one thread of the warpgroup issues O += P V (4 MMAs,
+// N = D) into tensor memory.  Software pipeline: while tile j's softmax runs,
+// S of tile j+1 is on the tensor cores (its K already dequantised), and
+// O += P V of tile j runs while tile j+1's successor is dequantised; the next
+// tile's code words are loaded into registers one tile ahead.  Tensor memory
+// per warpgroup (256 columns): S of even and odd tiles in [0, 128), O in
+// [128, 128 + D).
 // ---------------------------------------------------------------------------
-constexpr int kUmmaRows = 128;  // query rows per CTA
+constexpr int kUmmaRows = 128;  // query rows per warpgroup (the MMA's M)
+constexpr int kUmmaWG = 2;      // warpgroups per CTA
 constexpr int kUmmaTN = 64;     // tokens per KV tile
+constexpr int kUmmaThreads = 128 * kUmmaWG;
 
 template <int D>
 struct UmmaSmem {
-  static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = Q_OFF + kUmmaRows * D * 2;
-  static constexpr int V_OFF = K_OFF + kUmmaTN * D * 2;
-  static constexpr int P_OFF = V_OFF + D * kUmmaTN * 2;
-  static constexpr int BAR_OFF = P_OFF + kUmmaRows * kUmmaTN * 2;
-  static constexpr int BYTES = BAR_OFF + 32;
-  static constexpr uint32_t TCOLS = kUmmaTN + D <= 128 ? 128u : 256u;
+  // K double-, V triple- and P double-buffered: tile j+1 is dequantised and
+  // its S issued while tile j's softmax runs, and O += P_j V_j runs while
+  // tile j+2 is dequantised
+  static constexpr int K_BYTES = kUmmaTN * D * 2, V_BYTES = D * kUmmaTN * 2;
+  static constexpr int P_BYTES = kUmmaRows * kUmmaTN * 2, Q_BYTES = kUmmaRows * D * 2;
+  static constexpr int Q_OFF = 0;  // one Q operand per warpgroup
+  static constexpr int K_OFF = Q_OFF + kUmmaWG * Q_BYTES;
+  static constexpr int V_OFF = K_OFF + 2 * K_BYTES;
+  static constexpr int P_OFF = V_OFF + 3 * V_BYTES;  // [warpgroup][2]
+  static constexpr int BAR_OFF = P_OFF + 2 * kUmmaWG * P_BYTES;
+  static constexpr int BYTES = BAR_OFF + 64;
+  // tensor memory: per warpgroup 256 columns, S of even and odd tiles, then O
+  static constexpr uint32_t TWG = 256, TCOLS = 512;
+  static_assert(2 * kUmmaTN + D <= TWG, "a warpgroup's S and O fit its columns");
 };
 
 template <int D, int BITS, int G>
-__global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
+__global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillArgs a) {
   using F = Fmt<D, BITS, G>;
   using SM = UmmaSmem<D>;
-  constexpr int NT = 128, TN = kUmmaTN, NSUB = TN / kPage;
+  constexpr int NT = kUmmaThreads, TN = kUmmaTN, NSUB = TN / kPage;
   constexpr int WPR = D * BITS / 32;          // key-code words per token row
   constexpr int CPW = 32 / BITS;              // channels per key word
   constexpr int HP = CPW / 2;                 // f16 pairs per key word
@@ -495,9 +507,12 @@ __global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
   uint8_t* const Ks = smem + SM::K_OFF;
   uint8_t* const Vs = smem + SM::V_OFF;
   uint8_t* const Ps = smem + SM::P_OFF;
-  uint64_t* const bars = reinterpret_cast<uint64_t*>(smem + SM::BAR_OFF);  // S done, O done
-  uint32_t* const tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  // bars[b]: S of tiles j = b (mod 2) done (both warpgroups); bars[2 + 2 w + b]:
+  // warpgroup w's O += P_j V_j of those tiles done
+  uint64_t* const bars = reinterpret_cast<uint64_t*>(smem + SM::BAR_OFF);
+  uint32_t* const tslot = reinterpret_cast<uint32_t*>(bars + 6);
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int wg = tid >> 7, wt = tid & 127;  // warpgroup, row in the warpgroup
 
   const int64_t bid = blockIdx.x;
   const int rt = a.n_rt - 1 - (int)(bid % a.n_rt);
@@ -510,13 +525,13 @@ __global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
     if (rt == 0 && h == 0 && tid == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
     return;
   }
-  const int rows = n * a.grp, r0 = rt * kUmmaRows;
+  const int rows = n * a.grp, r0 = rt * kUmmaThreads;
   if (r0 >= rows) return;
   const int rho = r0 + tid;
   const bool valid = rho < rows;
   const int qi = valid ? rho / a.grp : 0;
   const int plim = valid ? L - n + qi : -1;  // causal limit of this thread's row
-  const int kv_end = L - n + min(rows - 1, r0 + kUmmaRows - 1) / a.grp + 1;
+  const int kv_end = L - n + min(rows - 1, r0 + kUmmaThreads - 1) / a.grp + 1;
   const int64_t qrow = ((int64_t)(q0 + qi) * a.num_q_heads + h * a.grp + (valid ? rho % a.grp : 0)) * D;
   const int nq = nq_len(L, a.residual, G);
   const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
@@ -547,8 +562,7 @@ __global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
   // ---- tensor memory, barriers, the Q operand ----
   if (warp == 0) umma::alloc(tslot, SM::TCOLS);
   if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+    for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
   }
 #pragma unroll
@@ -559,15 +573,16 @@ __global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
       const int c0 = kchan_at<BITS>(k8 + 2 * e), c1 = kchan_at<BITS>(k8 + 2 * e + 1);
       w[e] = pack_h2(valid ? load_qv(a, qrow + c0) : 0.f, valid ? load_qv(a, qrow + c1) : 0.f);
     }
-    *reinterpret_cast<uint4*>(Qs + umma::umma_off(tid, k8, D)) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(Qs + wg * SM::Q_BYTES + umma::umma_off(wt, k8, D)) =
+        make_uint4(w[0], w[1], w[2], w[3]);
   }
   umma::fence_smem_to_async();
   umma::fence_before_sync();
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = *tslot;
-  const uint32_t tS = tmem, tO = tmem + TN;
-  const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+  const uint32_t tS = tmem + wg * SM::TWG, tO = tS + 2 * TN;  // this warpgroup's columns
+  const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
 
   const uint8_t* pool_h = a.pool + (int64_t)h * F::PB;
   const int64_t page_stride = (int64_t)a.n_kv_heads * F::PB;
@@ -639,7 +654,7 @@ __global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
   };
 
   // dequantise the registers of tile jt into the K and V^T operand tiles
-  auto store_tile = [&](int jt) {
+  auto store_tile = [&](int jt, uint8_t* kd, uint8_t* vd) {
 #pragma unroll
     for (int s = 0; s < NSUB; ++s) {
       const int j = jt * NSUB + s;
@@ -681,7 +696,7 @@ __global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
           }
 #pragma unroll
           for (int q = 0; q < HP / 4; ++q)
-            *reinterpret_cast<uint4*>(Ks + umma::umma_off(tb + u / WPR, kc0 + 8 * q, D)) =
+            *reinterpret_cast<uint4*>(kd + umma::umma_off(tb + u / WPR, kc0 + 8 * q, D)) =
                 make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
           // value word (lane l, word w): channels 16mb+gl and 16mb+8+gl, tokens
           // tl, tl+1, tl+8, tl+9
@@ -701,10 +716,10 @@ __global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
             const uint32_t v1 = hfma2(hfma2(r[1], VCode<BITS>::kMul, VCode<BITS>::kAddLo), s01, z01);
             const uint32_t v2 = hfma2(hfma2(r[2], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
             const uint32_t v3 = hfma2(hfma2(r[3], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
-            *reinterpret_cast<uint32_t*>(Vs + umma::umma_off(16 * mb + gl, tb + tl, TN)) = v0;
-            *reinterpret_cast<uint32_t*>(Vs + umma::umma_off(16 * mb + 8 + gl, tb + tl, TN)) = v1;
-            *reinterpret_cast<uint32_t*>(Vs + umma::umma_off(16 * mb + gl, tb + tl + 8, TN)) = v2;
-            *reinterpret_cast<uint32_t*>(Vs + umma::umma_off(16 * mb + 8 + gl, tb + tl + 8, TN)) = v3;
+            *reinterpret_cast<uint32_t*>(vd + umma::umma_off(16 * mb + gl, tb + tl, TN)) = v0;
+            *reinterpret_cast<uint32_t*>(vd + umma::umma_off(16 * mb + 8 + gl, tb + tl, TN)) = v1;
+            *reinterpret_cast<uint32_t*>(vd + umma::umma_off(16 * mb + gl, tb + tl + 8, TN)) = v2;
+            *reinterpret_cast<uint32_t*>(vd + umma::umma_off(16 * mb + 8 + gl, tb + tl + 8, TN)) = v3;
           }
         }
       } else if (j < n16) {
@@ -720,26 +735,26 @@ __global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
             // K block: word r holds channels cc, cc+1 of token t
             const int t = 8 * (r & 1) + (l >> 2), cc = 8 * (r >> 1) + 2 * (l & 3);
             const int c = 16 * c16 + cc;
-            *reinterpret_cast<uint16_t*>(Ks + umma::umma_off(tb + t, kpos<BITS>(c), D)) =
+            *reinterpret_cast<uint16_t*>(kd + umma::umma_off(tb + t, kpos<BITS>(c), D)) =
                 static_cast<uint16_t>(kx & 0xffffu);
-            *reinterpret_cast<uint16_t*>(Ks + umma::umma_off(tb + t, kpos<BITS>(c + 1), D)) =
+            *reinterpret_cast<uint16_t*>(kd + umma::umma_off(tb + t, kpos<BITS>(c + 1), D)) =
                 static_cast<uint16_t>(kx >> 16);
             // V block: word r holds tokens tv, tv+1 of channel 16c16 + cv;
             // tokens past the end (stale ring slots) become 0
             const int tv = 8 * (r >> 1) + 2 * (l & 3), cv = 8 * (r & 1) + (l >> 2);
             const uint32_t msk = (t0 + tv < L ? 0x0000ffffu : 0u) | (t0 + tv + 1 < L ? 0xffff0000u : 0u);
-            *reinterpret_cast<uint32_t*>(Vs + umma::umma_off(16 * c16 + cv, tb + tv, TN)) = vx & msk;
+            *reinterpret_cast<uint32_t*>(vd + umma::umma_off(16 * c16 + cv, tb + tv, TN)) = vx & msk;
           }
         }
       } else {
         // past the last token of the CTA's rows: zero K rows and V^T columns
         for (int i = tid; i < kPage * D / 8; i += NT) {
           const int t = i / (D / 8), c8 = (i % (D / 8)) * 8;
-          *reinterpret_cast<uint4*>(Ks + umma::umma_off(tb + t, c8, D)) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(kd + umma::umma_off(tb + t, c8, D)) = make_uint4(0, 0, 0, 0);
         }
         for (int i = tid; i < D * 2; i += NT) {
           const int c = i >> 1, t8 = (i & 1) * 8;
-          *reinterpret_cast<uint4*>(Vs + umma::umma_off(c, tb + t8, TN)) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(vd + umma::umma_off(c, tb + t8, TN)) = make_uint4(0, 0, 0, 0);
         }
       }
     }
@@ -750,41 +765,71 @@ __global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
   const float alpha = a.alpha;
   float m_run = -INFINITY, l_run = 0.f;
   bool ok = true;
-  load_tile(0);
-  for (int jt = 0; jt < n_tiles && ok; ++jt) {
-    if (jt > 0) {  // the previous tile's O += P V has read V^T and P
-      ok = mbar_wait(&bars[1], (jt - 1) & 1, a.err);
+  // A parity wait on an mbarrier targets the oldest of its phases not yet
+  // known to be complete, at most one phase behind: tile j's S and O MMAs
+  // commit to barriers of parity class j & 1, phase j >> 1.
+  auto wait_o = [&](int j, int w) {  // warpgroup w's O += P_j V_j (and its MMAs before) done
+    ok = mbar_wait(&bars[2 + 2 * w + (j & 1)], (j >> 1) & 1, a.err) && ok;
+    umma::fence_after_sync();
+  };
+  auto issue_s = [&](int j) {  // S_j = Q K_j^T of both warpgroups into their S[j & 1]
+    if (tid == 0) {
       umma::fence_after_sync();
+      const uint32_t kb = smem_u32(Ks + (j & 1) * SM::K_BYTES);
+#pragma unroll
+      for (int w = 0; w < kUmmaWG; ++w)
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma::mma_f16(tmem + w * SM::TWG + (j & 1) * TN,
+                        umma::smem_desc(smem_u32(Qs + w * SM::Q_BYTES) + 256 * kk, 128, 16 * D),
+                        umma::smem_desc(kb + 256 * kk, 128, 16 * D), idS, kk > 0);
+      umma::commit(&bars[j & 1]);
+    }
+  };
+  if (n_tiles > 0) {
+    load_tile(0);
+    store_tile(0, Ks, Vs);
+    if (n_tiles > 1) load_tile(1);
+    umma::fence_smem_to_async();
+    umma::fence_before_sync();
+    __syncthreads();
+    issue_s(0);
+  }
+  for (int jt = 0; jt < n_tiles; ++jt) {
+    const int b = jt & 1;
+    if (jt >= 2) {
+      // the P buffer b of this warpgroup, and when tile jt+1 is dequantised
+      // below, the V^T buffer (jt + 1) % 3 read by both warpgroups.  A wait on
+      // the other warpgroup's barrier is made only before the CTA-wide barrier
+      // of this iteration, which keeps that warpgroup from completing a second
+      // phase of it first (in the last tile there is no such barrier).
+      if (jt + 1 < n_tiles) {
+        wait_o(jt - 2, 0);
+        wait_o(jt - 2, 1);
+      } else {
+        wait_o(jt - 2, wg);
+      }
+    }
+    if (jt + 1 < n_tiles) {
+      store_tile(jt + 1, Ks + ((jt + 1) & 1) * SM::K_BYTES, Vs + ((jt + 1) % 3) * SM::V_BYTES);
+      if (jt + 2 < n_tiles) load_tile(jt + 2);  // in flight during this tile's softmax
+      umma::fence_smem_to_async();
+      umma::fence_before_sync();
       if (!__syncthreads_and(ok)) {
         ok = false;
         break;
       }
+      issue_s(jt + 1);
     }
-    store_tile(jt);
-    umma::fence_smem_to_async();
-    umma::fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {
-      umma::fence_after_sync();
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk)
-        umma::mma_f16(tS, umma::smem_desc(smem_u32(Qs) + 256 * kk, 128, 16 * D),
-                      umma::smem_desc(smem_u32(Ks) + 256 * kk, 128, 16 * D), idS, kk > 0);
-      umma::commit(&bars[0]);
-    }
-    if (jt + 1 < n_tiles) load_tile(jt + 1);  // in flight during S and the softmax
-    ok = mbar_wait(&bars[0], jt & 1, a.err);
+    ok = mbar_wait(&bars[b], (jt >> 1) & 1, a.err) && ok;
     umma::fence_after_sync();
-    if (!__syncthreads_and(ok)) {
-      ok = false;
-      break;
-    }
     // the row's scores in two 32-column halves: a pass for the maximum, then
     // one for the weights (tensor memory is read twice, the registers once)
+    const uint32_t tSj = tS + b * TN;
     const int tile0 = jt * TN;
     const bool masked = tile0 + TN - 1 > plim;
     auto load_half = [&](int hf, float (&x)[32]) {
-      umma::ld32(tS + lane_base + 32 * hf, x);
+      umma::ld32(tSj + lane_base + 32 * hf, x);
       umma::wait_ld();
       if (masked) {
 #pragma unroll
@@ -806,7 +851,8 @@ __global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
       const float f = m_run == -INFINITY ? 0.f : fast_exp2(m_run - mnew);
       l_run *= f;
       m_run = mnew;
-      if (jt > 0) {  // this warp's rows of O in tensor memory
+      if (jt > 0) {  // this warp's rows of O in tensor memory, once O += P V of tile jt-1 is in
+        wait_o(jt - 1, wg);
 #pragma unroll
         for (int c0 = 0; c0 < D; c0 += 32) {
           float o[32];
@@ -820,6 +866,7 @@ __global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
       }
     }
     const float nb = m_run == -INFINITY ? 0.f : -m_run;
+    uint8_t* const pd = Ps + (2 * wg + b) * SM::P_BYTES;
     float sum = 0.f;
 #pragma unroll
     for (int hf = 0; hf < TN / 32; ++hf) {
@@ -835,28 +882,26 @@ __global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
           sum += p0 + p1;
           w[e] = pack_h2(p0, p1);
         }
-        *reinterpret_cast<uint4*>(Ps + umma::umma_off(tid, 32 * hf + c8, TN)) =
+        *reinterpret_cast<uint4*>(pd + umma::umma_off(wt, 32 * hf + c8, TN)) =
             make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
     l_run += sum;
     umma::fence_smem_to_async();
     umma::fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {
+    // this warpgroup's 128 threads only (named barrier 1 + wg)
+    asm volatile("bar.sync %0, %1;\n" ::"r"(1 + wg), "r"(128) : "memory");
+    if (wt == 0) {  // O += P_jt V_jt of this warpgroup
       umma::fence_after_sync();
+      const uint32_t vb = smem_u32(Vs + (jt % 3) * SM::V_BYTES);
 #pragma unroll
       for (int kk = 0; kk < TN / 16; ++kk)
-        umma::mma_f16(tO, umma::smem_desc(smem_u32(Ps) + 256 * kk, 128, 16 * TN),
-                      umma::smem_desc(smem_u32(Vs) + 256 * kk, 128, 16 * TN), idO,
-                      jt > 0 || kk > 0);
-      umma::commit(&bars[1]);
+        umma::mma_f16(tO, umma::smem_desc(smem_u32(pd) + 256 * kk, 128, 16 * TN),
+                      umma::smem_desc(vb + 256 * kk, 128, 16 * TN), idO, jt > 0 || kk > 0);
+      umma::commit(&bars[2 + 2 * wg + b]);
     }
   }
-  if (ok && n_tiles > 0) {
-    ok = mbar_wait(&bars[1], (n_tiles - 1) & 1, a.err);
-    umma::fence_after_sync();
-  }
+  if (ok && n_tiles > 0) wait_o(n_tiles - 1, wg);
   if (__syncthreads_and(ok) && n_tiles > 0) {
     // ---- normalise and write this thread's row ----
     const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
@@ -901,7 +946,7 @@ __global__ void __launch_bounds__(128, 2) prefill_umma_kernel(PrefillArgs a) {
 template <int D, int BITS, int G>
 static int launch_prefill_umma_t(PrefillArgs a, cudaStream_t stream) {
   using SM = UmmaSmem<D>;
-  const int64_t tiles = ((int64_t)a.max_q * a.grp + kUmmaRows - 1) / kUmmaRows;
+  const int64_t tiles = ((int64_t)a.max_q * a.grp + kUmmaThreads - 1) / kUmmaThreads;
   const int64_t blocks = (int64_t)a.num_seqs * a.n_kv_heads * tiles;
   if (blocks <= 0) return TKV_OK;
   if (blocks > 0x7fffffffLL) return TKV_INVALID_ARGUMENT;
@@ -915,7 +960,7 @@ static int launch_prefill_umma_t(PrefillArgs a, cudaStream_t stream) {
     if (dev >= 0 && dev < kMaxPrefillDevices) attr_set[dev].store(1, std::memory_order_relaxed);
   }
   a.n_rt = (int)tiles;
-  prefill_umma_kernel<D, BITS, G><<<(unsigned)blocks, 128, SM::BYTES, stream>>>(a);
+  prefill_umma_kernel<D, BITS, G><<<(unsigned)blocks, kUmmaThreads, SM::BYTES, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
 }
 
