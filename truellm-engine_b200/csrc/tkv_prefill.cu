@@ -590,7 +590,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
   const uint8_t* ring_base =
       reinterpret_cast<const uint8_t*>(a.ring) +
       (((int64_t)row * a.n_kv_heads + h) * (a.ring_cap / kPage)) * CHUNK;
-  const int kc0 = (tid % WPR) * CPW;  // first channel (tile order) of this thread's key words
+  // Key code words are taken token-fastest: thread tid holds word column
+  // tid / 16 (channels kc0.. in tile order) of token tid % 16 of a page, so
+  // the 16-byte stores of 8 consecutive lanes fill one 128-byte core matrix
+  // of the K operand (no bank conflicts).
+  static_assert(KW <= NT, "one key word per thread and page");
+  const int kc0 = (tid / kPage) * CPW;
 
   // ---- registers of the next tile: NSUB sub-tiles of code words or ring vectors ----
   uint32_t reg[NSUB][SLOT];
@@ -598,17 +603,47 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
   uint4 kml[MVEC];  // key meta of the group the previous tile ended in
 #pragma unroll
   for (int v = 0; v < MVEC; ++v) kml[v] = make_uint4(0, 0, 0, 0);
+  // page ids of the next tile load_tile reads, and of the pages holding this
+  // thread's key meta for the key groups starting in it: loaded one call
+  // ahead, so the code-word loads never wait on a block-table load
+  int pid_n[NSUB], mid_n[NKM][MVEC];
+  auto fetch_ids = [&](int jt) {
+#pragma unroll
+    for (int s = 0; s < NSUB; ++s) {
+      const int j = jt * NSUB + s;
+      pid_n[s] = j < n_pages ? bt[j] : 0;
+    }
+#pragma unroll
+    for (int g = 0; g < NKM; ++g) {
+      const int j = jt * NSUB + (F::PPG >= NSUB ? 0 : g * F::PPG);
+      // threads without a key word (tid >= KW) have kc0 >= D: they fetch no meta
+      const bool starts = tid < KW && j < n_pages && j % F::PPG == 0;
+#pragma unroll
+      for (int v = 0; v < MVEC; ++v)
+        mid_n[g][v] = starts ? bt[j + (4 * (kc0 + 4 * v)) / F::KMS] : 0;
+    }
+  };
+  fetch_ids(0);
   auto load_tile = [&](int jt) {
+    int pid[NSUB], mid[NKM][MVEC];
+#pragma unroll
+    for (int s = 0; s < NSUB; ++s) pid[s] = pid_n[s];
+#pragma unroll
+    for (int g = 0; g < NKM; ++g)
+#pragma unroll
+      for (int v = 0; v < MVEC; ++v) mid[g][v] = mid_n[g][v];
+    fetch_ids(jt + 1);
 #pragma unroll
     for (int s = 0; s < NSUB; ++s) {
       const int j = jt * NSUB + s;
       if (j < n_pages) {
-        const uint8_t* pg = pool_h + (int64_t)bt[j] * page_stride;
+        const uint8_t* pg = pool_h + (int64_t)pid[s] * page_stride;
 #pragma unroll
         for (int k = 0; k < KPT; ++k) {
           const int u = tid + k * NT;
           if (u >= KW) continue;
-          reg[s][k * (2 + VMW)] = __ldg(reinterpret_cast<const uint32_t*>(pg) + u);
+          reg[s][k * (2 + VMW)] =
+              __ldg(reinterpret_cast<const uint32_t*>(pg) + (u % kPage) * WPR + u / kPage);
           const int l = u & 31, w = u >> 5;
           reg[s][k * (2 + VMW) + 1] = __ldg(reinterpret_cast<const uint32_t*>(
               pg + F::V_CODES_OFF + ((w / F::VW) * 32 + l) * 4 * F::VW + (w % F::VW) * 4));
@@ -622,14 +657,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
           }
         }
         const int ki = F::PPG >= NSUB ? 0 : s / (F::PPG >= NSUB ? 1 : F::PPG);
-        if (j % F::PPG == 0) {  // a new key group: this thread's channels
-          const int grp = j / F::PPG;
+        if (j % F::PPG == 0 && tid < KW) {  // a new key group: this thread's channels
 #pragma unroll
           for (int v = 0; v < MVEC; ++v) {
             const int off = 4 * (kc0 + 4 * v);
-            const int ph = bt[grp * F::PPG + off / F::KMS];
-            km[ki][v] = __ldg(reinterpret_cast<const uint4*>(pool_h + (int64_t)ph * page_stride +
-                                                             F::BODY + off % F::KMS));
+            km[ki][v] = __ldg(reinterpret_cast<const uint4*>(
+                pool_h + (int64_t)mid[ki][v] * page_stride + F::BODY + off % F::KMS));
           }
         } else if (s == 0) {  // the group the previous tile ended in
 #pragma unroll
@@ -696,7 +729,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
           }
 #pragma unroll
           for (int q = 0; q < HP / 4; ++q)
-            *reinterpret_cast<uint4*>(kd + umma::umma_off(tb + u / WPR, kc0 + 8 * q, D)) =
+            *reinterpret_cast<uint4*>(kd + umma::umma_off(tb + u % kPage, kc0 + 8 * q, D)) =
                 make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
           // value word (lane l, word w): channels 16mb+gl and 16mb+8+gl, tokens
           // tl, tl+1, tl+8, tl+9
@@ -828,21 +861,25 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
     const uint32_t tSj = tS + b * TN;
     const int tile0 = jt * TN;
     const bool masked = tile0 + TN - 1 > plim;
-    auto load_half = [&](int hf, float (&x)[32]) {
-      umma::ld32(tSj + lane_base + 32 * hf, x);
+    static_assert(TN == 64, "the row's scores are read as two 32-column halves");
+    auto load_row = [&](float (&x0)[32], float (&x1)[32]) {  // both halves, one wait
+      umma::ld32(tSj + lane_base, x0);
+      umma::ld32(tSj + lane_base + 32, x1);
       umma::wait_ld();
       if (masked) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) x[c] = tile0 + 32 * hf + c <= plim ? x[c] : -INFINITY;
+        for (int c = 0; c < 32; ++c) {
+          x0[c] = tile0 + c <= plim ? x0[c] : -INFINITY;
+          x1[c] = tile0 + 32 + c <= plim ? x1[c] : -INFINITY;
+        }
       }
     };
     float mx = -INFINITY;
+    {
+      float x0[32], x1[32];
+      load_row(x0, x1);
 #pragma unroll
-    for (int hf = 0; hf < TN / 32; ++hf) {
-      float x[32];
-      load_half(hf, x);
-#pragma unroll
-      for (int c = 0; c < 32; ++c) mx = fmaxf(mx, x[c]);
+      for (int c = 0; c < 32; ++c) mx = fmaxf(mx, fmaxf(x0[c], x1[c]));
     }
     mx *= alpha;  // alpha > 0 keeps the order
     const bool need = mx > m_run + kLazyLog2;
@@ -868,10 +905,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
     const float nb = m_run == -INFINITY ? 0.f : -m_run;
     uint8_t* const pd = Ps + (2 * wg + b) * SM::P_BYTES;
     float sum = 0.f;
+    float xr[2][32];
+    load_row(xr[0], xr[1]);
 #pragma unroll
-    for (int hf = 0; hf < TN / 32; ++hf) {
-      float x[32];
-      load_half(hf, x);
+    for (int hf = 0; hf < 2; ++hf) {
+      const float (&x)[32] = xr[hf];
 #pragma unroll
       for (int c8 = 0; c8 < 32; c8 += 8) {
         uint32_t w[4];
