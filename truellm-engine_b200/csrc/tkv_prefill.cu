@@ -596,6 +596,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
   // of the K operand (no bank conflicts).
   static_assert(KW <= NT, "one key word per thread and page");
   const int kc0 = (tid / kPage) * CPW;
+  // this thread's store offsets in the operand tiles (sub-tile, half and
+  // neighbour offsets are compile-time): its key word (token tid % 16,
+  // channels kc0..), its value word's first (channel, token) pair, its P row
+  const uint32_t k_off = umma::umma_off(tid % kPage, tid < KW ? kc0 : 0, D);
+  const uint32_t v_off = umma::umma_off(16 * (BITS == 4 ? (tid >> 5) : 2 * (tid >> 5)) + ((tid & 31) >> 2),
+                                        2 * (tid & 3), TN);
+  const uint32_t p_off = umma::umma_off(wt, 0, TN);
 
   // ---- registers of the next tile: NSUB sub-tiles of code words or ring vectors ----
   uint32_t reg[NSUB][SLOT];
@@ -649,11 +656,25 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
               pg + F::V_CODES_OFF + ((w / F::VW) * 32 + l) * 4 * F::VW + (w % F::VW) * 4));
           const uint32_t* vmp = reinterpret_cast<const uint32_t*>(pg + F::V_META_OFF);
           const int t0 = 2 * (l & 3);
+          if constexpr (F::NVG == 1) {
+            // one value group per token: (step, zero) of tokens t0, t0+1 and
+            // t0+8, t0+9 as two 8-byte loads (the same for both 2-bit halves)
+            const uint2 m0 = __ldg(reinterpret_cast<const uint2*>(vmp + t0));
+            const uint2 m1 = __ldg(reinterpret_cast<const uint2*>(vmp + t0 + 8));
 #pragma unroll
-          for (int x = 0; x < VMW; ++x) {
-            const int mb = BITS == 4 ? w : 2 * w + (x >> 2);
-            const int t = t0 + (x & 1) + 8 * ((x >> 1) & 1);
-            reg[s][k * (2 + VMW) + 2 + x] = __ldg(vmp + t * F::NVG + (16 * mb) / G);
+            for (int x = 0; x < VMW; x += 4) {
+              reg[s][k * (2 + VMW) + 2 + x] = m0.x;
+              reg[s][k * (2 + VMW) + 3 + x] = m0.y;
+              reg[s][k * (2 + VMW) + 4 + x] = m1.x;
+              reg[s][k * (2 + VMW) + 5 + x] = m1.y;
+            }
+          } else {
+#pragma unroll
+            for (int x = 0; x < VMW; ++x) {
+              const int mb = BITS == 4 ? w : 2 * w + (x >> 2);
+              const int t = t0 + (x & 1) + 8 * ((x >> 1) & 1);
+              reg[s][k * (2 + VMW) + 2 + x] = __ldg(vmp + t * F::NVG + (16 * mb) / G);
+            }
           }
         }
         const int ki = F::PPG >= NSUB ? 0 : s / (F::PPG >= NSUB ? 1 : F::PPG);
@@ -729,7 +750,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
           }
 #pragma unroll
           for (int q = 0; q < HP / 4; ++q)
-            *reinterpret_cast<uint4*>(kd + umma::umma_off(tb + u % kPage, kc0 + 8 * q, D)) =
+            *reinterpret_cast<uint4*>(kd + k_off + s * 32 * D + q * 128) =
                 make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
           // value word (lane l, word w): channels 16mb+gl and 16mb+8+gl, tokens
           // tl, tl+1, tl+8, tl+9
@@ -749,10 +770,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
             const uint32_t v1 = hfma2(hfma2(r[1], VCode<BITS>::kMul, VCode<BITS>::kAddLo), s01, z01);
             const uint32_t v2 = hfma2(hfma2(r[2], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
             const uint32_t v3 = hfma2(hfma2(r[3], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
-            *reinterpret_cast<uint32_t*>(vd + umma::umma_off(16 * mb + gl, tb + tl, TN)) = v0;
-            *reinterpret_cast<uint32_t*>(vd + umma::umma_off(16 * mb + 8 + gl, tb + tl, TN)) = v1;
-            *reinterpret_cast<uint32_t*>(vd + umma::umma_off(16 * mb + gl, tb + tl + 8, TN)) = v2;
-            *reinterpret_cast<uint32_t*>(vd + umma::umma_off(16 * mb + 8 + gl, tb + tl + 8, TN)) = v3;
+            // rows 16 mb + gl (+8), tokens tb + tl (+8): v_off plus constants
+            uint8_t* const vp = vd + v_off + s * 256 + half * 32 * TN;
+            *reinterpret_cast<uint32_t*>(vp) = v0;
+            *reinterpret_cast<uint32_t*>(vp + 16 * TN) = v1;
+            *reinterpret_cast<uint32_t*>(vp + 128) = v2;
+            *reinterpret_cast<uint32_t*>(vp + 16 * TN + 128) = v3;
           }
         }
       } else if (j < n16) {
@@ -904,7 +927,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
     }
     const float nb = m_run == -INFINITY ? 0.f : -m_run;
     uint8_t* const pd = Ps + (2 * wg + b) * SM::P_BYTES;
-    float sum = 0.f;
+    float2 sum2 = make_float2(0.f, 0.f);
+    const float2 al2 = make_float2(alpha, alpha), nb2 = make_float2(nb, nb);
     float xr[2][32];
     load_row(xr[0], xr[1]);
 #pragma unroll
@@ -915,16 +939,16 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = fast_exp2(fmaf(x[c8 + 2 * e], alpha, nb));
-          const float p1 = fast_exp2(fmaf(x[c8 + 2 * e + 1], alpha, nb));
-          sum += p0 + p1;
-          w[e] = pack_h2(p0, p1);
+          const float2 y = ffma2(make_float2(x[c8 + 2 * e], x[c8 + 2 * e + 1]), al2, nb2);
+          const float2 pp = make_float2(fast_exp2(y.x), fast_exp2(y.y));
+          sum2 = fadd2(sum2, pp);
+          w[e] = pack_h2(pp.x, pp.y);
         }
-        *reinterpret_cast<uint4*>(pd + umma::umma_off(wt, 32 * hf + c8, TN)) =
+        *reinterpret_cast<uint4*>(pd + p_off + (32 * hf + c8) * 16) =
             make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
-    l_run += sum;
+    l_run += sum2.x + sum2.y;
     umma::fence_smem_to_async();
     umma::fence_before_sync();
     // this warpgroup's 128 threads only (named barrier 1 + wg)
