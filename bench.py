@@ -172,7 +172,7 @@ CSRC = ROOT / "truellm-engine_b200" / "csrc"
 KERNEL_SOURCES = {
     "decode_stream": ["tkv_stream.cu", "tkv_decode_common.cuh", "tkv_frag.cuh", "tkv_common.cuh"],
     "append": ["tkv_append.cu", "tkv_common.cuh"],
-    "prefill": ["tkv_prefill.cu", "tkv_frag.cuh", "tkv_common.cuh"],
+    "prefill": ["tkv_prefill.cu", "tkv_umma.cuh", "tkv_frag.cuh", "tkv_common.cuh"],
 }
 
 
@@ -786,8 +786,7 @@ def run_append(args):
     alg = wl.append_algorithmic_bytes(w)
     peak, peak_kind = peaks()
     achieved = alg / t_call / 1e9
-    tp = ROOT / "profiles" / "append_config3.json"
-    traffic = json.loads(tp.read_text()).get("dram_bytes_per_call") if tp.exists() else None
+    traffic = ncu_traffic("append_config3", "append", "dram_bytes_per_call")
     if rank == 0:
         cpu = None
         if world == 1:
@@ -994,8 +993,7 @@ def run_prefill(args):
     peak = float(pk.get("bf16_tflops", 1590.0))
     peak_kind = "measured (cuBLAS bf16 burst)" if "bf16_tflops" in pk else "fallback"
     achieved = flops / t_call / 1e12
-    tp = ROOT / "profiles" / "prefill_cta_chunk512.json"
-    traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch") if tp.exists() else None
+    traffic = ncu_traffic("prefill_umma_chunk512", "prefill", "dram_bytes_per_launch")
     if rank == 0:
         cpu = None
         if world == 1:
@@ -1029,7 +1027,7 @@ def run_prefill(args):
                     "h2d_bytes_per_step": q.numel() * 2, "d2h_bytes_per_step": out.numel() * 2},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                          "unit": "TFLOP/s", "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": traffic, "kernel": "prefill_cta_kernel<128,4,128,4>",
+                         "traffic": traffic, "kernel": "prefill_umma_kernel<128,4,128>",
                          "flops_per_launch": flops, "kernel_ms": t_call * 1e3},
             "cpu_baseline": cpu,
             "clocks": clocks,

@@ -10,24 +10,17 @@
 // score = scale * q.k, kv head = q head / (Hq/Hkv), max-subtracted softmax,
 // fp32 accumulation.
 //
-// A CTA of 4 warps owns 64 query rows of one (sequence, kv head): rows
-// rho = i * grp + j (token i, q head j of the kv head's group), 16 per warp,
-// so the grp q heads of a kv head share every dequantised page.  Per 16-token
-// tile the CTA's threads dequantise the page's codes -- exactly, to the fp16
-// values the reference decompress writes, fp16(code * step + zero) for keys
-// (per channel) and values (per token) -- into a K tile [16][D] and a V^T
-// tile [D][16] in shared memory (double-buffered, one __syncthreads per tile);
-// each warp then runs
-//   * S = Q K^T on mma.m16n8k16 (A = its 16 query rows as exact fp16, B from
-//     the K tile by ldmatrix), causal mask per row;
-//   * online softmax per row in the exp2 domain (lazy rescale, as decode);
-//   * O += P V (P from the S accumulators without shuffles, B from the V^T
-//     tile by ldmatrix).
-// Key channels sit in the tile in the order a code word unpacks into f16
-// pairs ((c, c+4) for 4-bit words, (c, c+8) for 2-bit), and Q is loaded in the
-// same order; ring tiles (the fp16 window) are scattered into that order.
-// The next tile's code words are loaded into registers before the current
-// tile's MMAs, so their latency overlaps them.
+// The query rows of one (sequence, kv head) are rho = i * grp + j (token i,
+// q head j of the kv head's group), so the grp q heads of a kv head share
+// every dequantised page.  Keys and values are dequantised exactly, to the
+// fp16 values the reference decompress writes, fp16(code * step + zero) for
+// keys (per channel) and values (per token), and the contractions run on the
+// 5th-generation tensor cores (tcgen05.mma, operands in shared memory, S and
+// O accumulators in tensor memory); prefill_umma_kernel below describes the
+// pipeline.  Key channels sit in the operand in the order a code word unpacks
+// into f16 pairs ((c, c+4) for 4-bit words, (c, c+8) for 2-bit), and Q is
+// staged in the same order; ring tiles (the fp16 window) are scattered into
+// that order.
 #include <atomic>
 
 #include "tkv_frag.cuh"
@@ -38,67 +31,6 @@ namespace tkv {
 constexpr int kMaxPrefillDevices = 64;
 
 namespace {
-
-// S accumulators after the mask for tokens t0 + 8*nt + 2*tig + e against the
-// rows' causal limits pa (row g) and pb (row g+8).
-__device__ __forceinline__ void causal_mask(float (&s)[2][4], int t0, int tig, int pa, int pb) {
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-    const int t = t0 + 8 * nt + 2 * tig;
-    s[nt][0] = t <= pa ? s[nt][0] : -INFINITY;
-    s[nt][1] = t + 1 <= pa ? s[nt][1] : -INFINITY;
-    s[nt][2] = t <= pb ? s[nt][2] : -INFINITY;
-    s[nt][3] = t + 1 <= pb ? s[nt][3] : -INFINITY;
-  }
-}
-
-template <int D>
-struct RowState {
-  float m[2];          // running max (log2 units) of rows g, g+8
-  float l[2];          // this lane's partial sums of p
-  float o[D / 8][4];   // O fragments: n-tile nt covers channels 8nt..8nt+7
-};
-
-// Online-softmax step for one 16-token tile; s holds raw scores on entry
-// (-inf where masked) and the unnormalised weights on return.
-template <int D>
-__device__ __forceinline__ void row_softmax(RowState<D>& st, float (&s)[2][4], float alpha) {
-  float t[2];
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    float x = fmaxf(fmaxf(s[0][2 * r], s[0][2 * r + 1]), fmaxf(s[1][2 * r], s[1][2 * r + 1]));
-    x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
-    x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
-    t[r] = x * alpha;
-  }
-  const bool need = t[0] > st.m[0] + kLazyLog2 || t[1] > st.m[1] + kLazyLog2;
-  if (__any_sync(0xffffffffu, need)) {
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const float mnew = fmaxf(st.m[r], t[r]);
-      const float f = st.m[r] == -INFINITY ? 0.f : fast_exp2(st.m[r] - mnew);
-      st.l[r] *= f;
-#pragma unroll
-      for (int nt = 0; nt < D / 8; ++nt) {
-        st.o[nt][2 * r] *= f;
-        st.o[nt][2 * r + 1] *= f;
-      }
-      st.m[r] = mnew;
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const float nbase = st.m[r] == -INFINITY ? 0.f : -st.m[r];
-    float sum = 0.f;
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      s[nt][2 * r] = fast_exp2(fmaf(s[nt][2 * r], alpha, nbase));
-      s[nt][2 * r + 1] = fast_exp2(fmaf(s[nt][2 * r + 1], alpha, nbase));
-      sum += s[nt][2 * r] + s[nt][2 * r + 1];
-    }
-    st.l[r] += sum;
-  }
-}
 
 __device__ __forceinline__ float load_qv(const PrefillArgs& a, int64_t idx) {
   if (a.q_bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.q)[idx]);
@@ -120,14 +52,6 @@ template <> struct VCode<2> {
 
 namespace {
 
-__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                        uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];\n"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(smem_u32(p))
-               : "memory");
-}
-
 // Position of key channel c in the shared K tile (inverse of the unpack order).
 template <int BITS>
 __device__ __forceinline__ constexpr int kpos(int c) {
@@ -143,306 +67,12 @@ __device__ __forceinline__ constexpr int kchan_at(int p) {
 
 }  // namespace
 
-template <int D, int BITS, int G, int NW>
-__global__ void __launch_bounds__(32 * NW, 2) prefill_cta_kernel(PrefillArgs a) {
-  using F = Fmt<D, BITS, G>;
-  constexpr int NT = 32 * NW, NKB = D / 16;
-  constexpr int WPR = D * BITS / 32;          // key-code words per token row
-  constexpr int CPW = 32 / BITS;              // channels per key word
-  constexpr int HP = CPW / 2;                 // f16 pairs per key word
-  constexpr int KW = kPage * WPR;             // key (and value) code words per page
-  constexpr int KPT = (KW + NT - 1) / NT;     // code words per thread
-  constexpr int MVEC = CPW / 4;               // 16-byte key-meta vectors per word's channels
-  constexpr int VMW = BITS == 4 ? 4 : 8;      // value (step, zero) words per value word
-  constexpr int RV = 2 * D;                   // 16-byte vectors per ring K (or V) block
-  constexpr int RPT = (RV + NT - 1) / NT;
-  constexpr int KS = D + 8, VS = kPage + 8;   // padded row strides (halves)
-  static_assert(NT % WPR == 0, "a thread's key words share their channels");
-  __shared__ __align__(16) __half Kt[2][kPage][KS];
-  __shared__ __align__(16) __half Vt[2][D][VS];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tig = lane & 3;
-
-  const int64_t bid = blockIdx.x;
-  const int rt = a.n_rt - 1 - (int)(bid % a.n_rt);
-  const int bh = (int)(bid / a.n_rt);
-  const int b = bh / a.n_kv_heads, h = bh - b * a.n_kv_heads;
-  const int L = a.seq_lens[b];
-  const int q0 = a.cu_q[b], n = a.cu_q[b + 1] - q0;
-  // n > max_q: the grid has row tiles for max_q tokens only, so the chunk's
-  // later rows would stay unwritten; flag the sequence instead
-  if (L < 0 || L > a.max_blocks * kPage || n < 0 || n > L || n > a.max_q || q0 < 0 ||
-      q0 + n > a.total_q) {
-    if (rt == 0 && h == 0 && tid == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
-    return;
-  }
-  const int rows = n * a.grp, r0 = rt * 16 * NW;
-  if (r0 >= rows) return;
-  const int ra = r0 + 16 * warp + g, rb = ra + 8;
-  const bool va = ra < rows, vb = rb < rows;
-  const int ia = va ? ra / a.grp : n - 1, ib = vb ? rb / a.grp : n - 1;
-  const int pa = L - n + ia, pb = L - n + ib;
-  const int kv_end = L - n + min(rows - 1, r0 + 16 * NW - 1) / a.grp + 1;
-  const int64_t qa = ((int64_t)(q0 + ia) * a.num_q_heads + h * a.grp + (va ? ra % a.grp : 0)) * D;
-  const int64_t qb = ((int64_t)(q0 + ib) * a.num_q_heads + h * a.grp + (vb ? rb % a.grp : 0)) * D;
-  const int nq = nq_len(L, a.residual, G);
-  const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
-  const int n_pages = min(nq, (kv_end + kPage - 1) / kPage * kPage) / kPage;
-  const int n_chunks = kv_end > nq ? (kv_end - nq + kPage - 1) / kPage : 0;
-  const int n_tiles = n_pages + n_chunks;
-
-  // every page read (the tiles' pages and their groups' key meta) in range
-  const int n_read = min(nq / kPage, (n_pages + F::PPG - 1) / F::PPG * F::PPG);
-  bool bad = false;
-  for (int p = tid; p < n_read; p += NT) {
-    const int ph = bt[p];
-    bad |= ph < 0 || ph >= a.num_pages;
-  }
-  if (__syncthreads_or(bad)) {
-    if (tid == 0) set_err(a.err, TKV_ERR_BAD_PAGE);
-    return;
-  }
-  int row = 0;
-  if (n_chunks > 0) {
-    row = a.seq_slots ? a.seq_slots[b] : b;
-    if (row < 0 || row >= a.max_seqs) {
-      if (tid == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
-      return;
-    }
-  }
-
-  // A operand: this warp's rows g, g+8 as exact f16, channels in tile order
-  uint32_t aq[NKB][4];
-#pragma unroll
-  for (int kb = 0; kb < NKB; ++kb)
-#pragma unroll
-    for (int hi = 0; hi < 2; ++hi) {
-      const int c0 = kchan_at<BITS>(16 * kb + 8 * hi + 2 * tig);
-      const int c1 = kchan_at<BITS>(16 * kb + 8 * hi + 2 * tig + 1);
-      aq[kb][2 * hi + 0] = pack_h2(va ? load_qv(a, qa + c0) : 0.f, va ? load_qv(a, qa + c1) : 0.f);
-      aq[kb][2 * hi + 1] = pack_h2(vb ? load_qv(a, qb + c0) : 0.f, vb ? load_qv(a, qb + c1) : 0.f);
-    }
-
-  const uint8_t* pool_h = a.pool + (int64_t)h * F::PB;
-  const int64_t page_stride = (int64_t)a.n_kv_heads * F::PB;
-  constexpr int CHUNK = 2 * F::RBLK;
-  const uint8_t* ring_base =
-      reinterpret_cast<const uint8_t*>(a.ring) +
-      (((int64_t)row * a.n_kv_heads + h) * (a.ring_cap / kPage)) * CHUNK;
-  const int kc0 = (tid % WPR) * CPW;  // first channel of this thread's key words
-
-  // ---------------- registers of the next tile ----------------
-  uint32_t kw[KPT], vw[KPT], vm[KPT][VMW];
-  uint4 km[MVEC];
-  uint4 rk[RPT], rv[RPT];
-  auto load_tile = [&](int j) {
-    if (j < n_pages) {
-      const uint8_t* pg = pool_h + (int64_t)bt[j] * page_stride;
-#pragma unroll
-      for (int k = 0; k < KPT; ++k) {
-        const int u = tid + k * NT;
-        if (u >= KW) continue;
-        kw[k] = __ldg(reinterpret_cast<const uint32_t*>(pg) + u);
-        const int l = u & 31, w = u >> 5;
-        vw[k] = __ldg(reinterpret_cast<const uint32_t*>(
-            pg + F::V_CODES_OFF + ((w / F::VW) * 32 + l) * 4 * F::VW + (w % F::VW) * 4));
-        const uint32_t* vmp = reinterpret_cast<const uint32_t*>(pg + F::V_META_OFF);
-        const int t0 = 2 * (l & 3);
-#pragma unroll
-        for (int x = 0; x < VMW; ++x) {
-          // 4-bit: tokens t0, t0+1, t0+8, t0+9 of m-block w; 2-bit: the same
-          // for m-blocks 2w (x < 4) and 2w+1
-          const int mb = BITS == 4 ? w : 2 * w + (x >> 2);
-          const int t = t0 + (x & 1) + 8 * ((x >> 1) & 1);
-          vm[k][x] = __ldg(vmp + t * F::NVG + (16 * mb) / G);
-        }
-      }
-      if (j % F::PPG == 0 && tid < KW) {  // a new key group: this thread's channels
-        const int grp = j / F::PPG;
-#pragma unroll
-        for (int v = 0; v < MVEC; ++v) {
-          const int off = 4 * (kc0 + 4 * v);
-          const int ph = bt[grp * F::PPG + off / F::KMS];
-          km[v] = __ldg(reinterpret_cast<const uint4*>(pool_h + (int64_t)ph * page_stride +
-                                                        F::BODY + off % F::KMS));
-        }
-      }
-    } else {
-      const int t0 = nq + (j - n_pages) * kPage;
-      const uint8_t* ck = ring_base + (int64_t)((t0 % a.ring_cap) / kPage) * CHUNK;
-#pragma unroll
-      for (int k = 0; k < RPT; ++k) {
-        const int u = tid + k * NT;
-        if (u >= RV) continue;
-        rk[k] = __ldg(reinterpret_cast<const uint4*>(ck) + u);
-        rv[k] = __ldg(reinterpret_cast<const uint4*>(ck + F::RBLK) + u);
-      }
-    }
-  };
-  auto store_tile = [&](int j, int buf) {
-    if (j < n_pages) {
-      uint32_t mw[CPW];
-#pragma unroll
-      for (int v = 0; v < MVEC; ++v) {
-        mw[4 * v + 0] = km[v].x; mw[4 * v + 1] = km[v].y;
-        mw[4 * v + 2] = km[v].z; mw[4 * v + 3] = km[v].w;
-      }
-      uint32_t sp[HP], zp[HP];
-#pragma unroll
-      for (int i = 0; i < HP; ++i) {
-        sp[i] = __byte_perm(mw[i], mw[i + HP], 0x5410);
-        zp[i] = __byte_perm(mw[i], mw[i + HP], 0x7632);
-      }
-#pragma unroll
-      for (int k = 0; k < KPT; ++k) {
-        const int u = tid + k * NT;
-        if (u >= KW) continue;
-        const uint32_t x = kw[k], x8 = kw[k] >> 8;
-        uint32_t hv[HP];
-#pragma unroll
-        for (int i = 0; i < HP; ++i) {
-          uint32_t c;
-          if (BITS == 4) {
-            c = (i & 1) ? code_pair<0x00F000F0u>(i < 2 ? x : x8)
-                        : code_pair<0x000F000Fu>(i < 2 ? x : x8);
-          } else {
-            const uint32_t y = i < 4 ? x : x8;
-            c = (i & 3) == 0 ? code_pair<0x00030003u>(y)
-              : (i & 3) == 1 ? code_pair<0x000C000Cu>(y)
-              : (i & 3) == 2 ? code_pair<0x00300030u>(y)
-                             : code_pair<0x00C000C0u>(y);
-          }
-          hv[i] = hfma2(c, sp[i], zp[i]);
-        }
-        __half* dst = &Kt[buf][u / WPR][kc0];
-#pragma unroll
-        for (int q = 0; q < HP / 4; ++q)
-          reinterpret_cast<uint4*>(dst)[q] = make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2],
-                                                        hv[4 * q + 3]);
-        // value word (lane l, word w): channels 16mb+gl and 16mb+8+gl, tokens
-        // tl, tl+1, tl+8, tl+9
-        const int l = u & 31, w = u >> 5, gl = l >> 2, tl = 2 * (l & 3);
-#pragma unroll
-        for (int half = 0; half < (BITS == 4 ? 1 : 2); ++half) {
-          const int mb = BITS == 4 ? w : 2 * w + half;
-          const uint32_t* m4 = &vm[k][4 * half];
-          const uint32_t s01 = __byte_perm(m4[0], m4[1], 0x5410), z01 = __byte_perm(m4[0], m4[1], 0x7632);
-          const uint32_t s89 = __byte_perm(m4[2], m4[3], 0x5410), z89 = __byte_perm(m4[2], m4[3], 0x7632);
-          uint32_t r[4];
-          if (BITS == 4 || half == 0)
-            value_frag<BITS, 0>(&vw[k], r);
-          else
-            value_frag<BITS, (BITS == 2 ? 1 : 0)>(&vw[k], r);
-          const uint32_t v0 = hfma2(hfma2(r[0], VCode<BITS>::kMul, VCode<BITS>::kAddLo), s01, z01);
-          const uint32_t v1 = hfma2(hfma2(r[1], VCode<BITS>::kMul, VCode<BITS>::kAddLo), s01, z01);
-          const uint32_t v2 = hfma2(hfma2(r[2], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
-          const uint32_t v3 = hfma2(hfma2(r[3], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
-          *reinterpret_cast<uint32_t*>(&Vt[buf][16 * mb + gl][tl]) = v0;
-          *reinterpret_cast<uint32_t*>(&Vt[buf][16 * mb + 8 + gl][tl]) = v1;
-          *reinterpret_cast<uint32_t*>(&Vt[buf][16 * mb + gl][tl + 8]) = v2;
-          *reinterpret_cast<uint32_t*>(&Vt[buf][16 * mb + 8 + gl][tl + 8]) = v3;
-        }
-      }
-    } else {
-      const int t0 = nq + (j - n_pages) * kPage;
-#pragma unroll
-      for (int k = 0; k < RPT; ++k) {
-        const int u = tid + k * NT;
-        if (u >= RV) continue;
-        const int c16 = u >> 5, l = u & 31;
-        const uint32_t kx[4] = {rk[k].x, rk[k].y, rk[k].z, rk[k].w};
-        const uint32_t vx[4] = {rv[k].x, rv[k].y, rv[k].z, rv[k].w};
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          // K block: word r holds channels cc, cc+1 of token t
-          const int t = 8 * (r & 1) + (l >> 2), cc = 8 * (r >> 1) + 2 * (l & 3);
-          const int c = 16 * c16 + cc;
-          Kt[buf][t][kpos<BITS>(c)] = __ushort_as_half(static_cast<unsigned short>(kx[r] & 0xffffu));
-          Kt[buf][t][kpos<BITS>(c + 1)] = __ushort_as_half(static_cast<unsigned short>(kx[r] >> 16));
-          // V block: word r holds tokens tv, tv+1 of channel 16c16 + cv; tokens
-          // past the end (stale ring slots) become 0
-          const int tv = 8 * (r >> 1) + 2 * (l & 3), cv = 8 * (r & 1) + (l >> 2);
-          const uint32_t msk = (t0 + tv < L ? 0x0000ffffu : 0u) | (t0 + tv + 1 < L ? 0xffff0000u : 0u);
-          *reinterpret_cast<uint32_t*>(&Vt[buf][16 * c16 + cv][tv]) = vx[r] & msk;
-        }
-      }
-    }
-  };
-
-  RowState<D> st;
-  st.m[0] = st.m[1] = -INFINITY;
-  st.l[0] = st.l[1] = 0.f;
-#pragma unroll
-  for (int nt = 0; nt < D / 8; ++nt) st.o[nt][0] = st.o[nt][1] = st.o[nt][2] = st.o[nt][3] = 0.f;
-  const float alpha = a.alpha;
-  const int mi = lane >> 3, mr = lane & 7;
-
-  load_tile(0);
-  store_tile(0, 0);
-  __syncthreads();
-  for (int j = 0; j < n_tiles; ++j) {
-    const int buf = j & 1;
-    if (j + 1 < n_tiles) load_tile(j + 1);  // in flight during this tile's MMAs
-    // ---- S = Q K^T over the tile's 16 tokens ----
-    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-    for (int kb = 0; kb < NKB; ++kb) {
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4(&Kt[buf][(mi >> 1) * 8 + mr][16 * kb + (mi & 1) * 8], b0, b1, b2, b3);
-      mma16816(s[0], aq[kb][0], aq[kb][1], aq[kb][2], aq[kb][3], b0, b1);
-      mma16816(s[1], aq[kb][0], aq[kb][1], aq[kb][2], aq[kb][3], b2, b3);
-    }
-    const int t0 = j < n_pages ? j * kPage : nq + (j - n_pages) * kPage;
-    if (t0 + kPage - 1 > min(pa, pb)) causal_mask(s, t0, tig, pa, pb);
-    row_softmax<D>(st, s, alpha);
-    // ---- O += P V ----
-    const uint32_t a0 = pack_h2(s[0][0], s[0][1]);
-    const uint32_t a1 = pack_h2(s[0][2], s[0][3]);
-    const uint32_t a2 = pack_h2(s[1][0], s[1][1]);
-    const uint32_t a3 = pack_h2(s[1][2], s[1][3]);
-#pragma unroll
-    for (int mb = 0; mb < D / 16; ++mb) {
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4(&Vt[buf][16 * mb + (mi >> 1) * 8 + mr][(mi & 1) * 8], b0, b1, b2, b3);
-      mma16816(st.o[2 * mb], a0, a1, a2, a3, b0, b1);
-      mma16816(st.o[2 * mb + 1], a0, a1, a2, a3, b2, b3);
-    }
-    if (j + 1 < n_tiles) store_tile(j + 1, buf ^ 1);
-    __syncthreads();
-  }
-
-  // ---- normalise and write this warp's rows ----
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    st.l[r] += __shfl_xor_sync(0xffffffffu, st.l[r], 1);
-    st.l[r] += __shfl_xor_sync(0xffffffffu, st.l[r], 2);
-  }
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    if (!(r == 0 ? va : vb)) continue;
-    const float inv = 1.f / st.l[r];
-    const int64_t ob = r == 0 ? qa : qb;
-#pragma unroll
-    for (int nt = 0; nt < D / 8; ++nt) {
-      const float o0 = st.o[nt][2 * r] * inv, o1 = st.o[nt][2 * r + 1] * inv;
-      const int64_t oi = ob + 8 * nt + 2 * tig;
-      if (a.out_dtype == TKV_F32) {
-        *reinterpret_cast<float2*>(static_cast<float*>(a.out) + oi) = make_float2(o0, o1);
-      } else if (a.out_dtype == TKV_BF16) {
-        *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(a.out) + oi) =
-            __floats2bfloat162_rn(o0, o1);
-      } else {
-        *reinterpret_cast<__half2*>(static_cast<__half*>(a.out) + oi) = __floats2half2_rn(o0, o1);
-      }
-    }
-  }
-}
-
 // ---------------------------------------------------------------------------
-// The same attention on the 5th-generation tensor cores (tcgen05): one CTA of
+// Chunked prefill on the 5th-generation tensor cores (tcgen05): one CTA of
 // two warpgroups per 256 query rows of a (sequence, kv head), each warpgroup
 // owning 128 rows (the MMA's M) and its own S and O in tensor memory; 64-token
-// KV tiles shared by both.  Per tile the CTA's threads dequantise the tile's four 16-token
-// pages (or fp16 ring chunks) exactly, as above, straight into the K-major
+// KV tiles shared by both.  Per tile the CTA's threads dequantise the tile's
+// four 16-token pages (or fp16 ring chunks) exactly straight into the K-major
 // shared-memory operand layouts of tkv_umma.cuh: K [64 tokens][D channels]
 // (channels in the code-unpack order, Q staged in the same order) and V^T
 // [D channels][64 tokens].  One thread issues S = Q K^T (D/16 MMAs, N = 64)
@@ -458,6 +88,13 @@ __global__ void __launch_bounds__(32 * NW, 2) prefill_cta_kernel(PrefillArgs a) 
 // per warpgroup (256 columns): S of even and odd tiles in [0, 128), O in
 // [128, 128 + D).
 // ---------------------------------------------------------------------------
+// Lazy rescale of the tcgen05 prefill: a row's running maximum (log2 units)
+// moves only when a tile's maximum exceeds it by more than this, so the O
+// rescale in tensor memory (a read and a write of the row's D columns) is
+// rare.  The weights written to the f16 P operand are then at most 2^8 = 256,
+// well inside the f16 range, and f16 keeps the same relative precision at any
+// magnitude.
+constexpr float kPrefillLazyLog2 = 8.0f;
 constexpr int kUmmaRows = 128;  // query rows per warpgroup (the MMA's M)
 constexpr int kUmmaWG = 2;      // warpgroups per CTA
 constexpr int kUmmaTN = 64;     // tokens per KV tile
@@ -709,24 +346,31 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
 
   // dequantise the registers of tile jt into the K and V^T operand tiles
   auto store_tile = [&](int jt, uint8_t* kd, uint8_t* vd) {
+    // the (step, zero) f16 pairs of this thread's key channels, once per key
+    // group of the tile (not per 16-token page)
+    uint32_t spk[NKM][HP], zpk[NKM][HP];
+#pragma unroll
+    for (int ki = 0; ki < NKM; ++ki) {
+      uint32_t mw[CPW];
+#pragma unroll
+      for (int v = 0; v < MVEC; ++v) {
+        mw[4 * v + 0] = km[ki][v].x; mw[4 * v + 1] = km[ki][v].y;
+        mw[4 * v + 2] = km[ki][v].z; mw[4 * v + 3] = km[ki][v].w;
+      }
+#pragma unroll
+      for (int i = 0; i < HP; ++i) {
+        spk[ki][i] = __byte_perm(mw[i], mw[i + HP], 0x5410);
+        zpk[ki][i] = __byte_perm(mw[i], mw[i + HP], 0x7632);
+      }
+    }
 #pragma unroll
     for (int s = 0; s < NSUB; ++s) {
       const int j = jt * NSUB + s;
       const int tb = s * kPage;  // the sub-tile's first token in the tile
       if (j < n_pages) {
         const int ki = F::PPG >= NSUB ? 0 : s / (F::PPG >= NSUB ? 1 : F::PPG);
-        uint32_t mw[CPW];
-#pragma unroll
-        for (int v = 0; v < MVEC; ++v) {
-          mw[4 * v + 0] = km[ki][v].x; mw[4 * v + 1] = km[ki][v].y;
-          mw[4 * v + 2] = km[ki][v].z; mw[4 * v + 3] = km[ki][v].w;
-        }
-        uint32_t sp[HP], zp[HP];
-#pragma unroll
-        for (int i = 0; i < HP; ++i) {
-          sp[i] = __byte_perm(mw[i], mw[i + HP], 0x5410);
-          zp[i] = __byte_perm(mw[i], mw[i + HP], 0x7632);
-        }
+        const uint32_t(&sp)[HP] = spk[ki];
+        const uint32_t(&zp)[HP] = zpk[ki];
 #pragma unroll
         for (int k = 0; k < KPT; ++k) {
           const int u = tid + k * NT;
@@ -752,12 +396,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
           for (int q = 0; q < HP / 4; ++q)
             *reinterpret_cast<uint4*>(kd + k_off + s * 32 * D + q * 128) =
                 make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
-          // value word (lane l, word w): channels 16mb+gl and 16mb+8+gl, tokens
-          // tl, tl+1, tl+8, tl+9
-          const int l = u & 31, w = u >> 5, gl = l >> 2, tl = 2 * (l & 3);
+          // value word (lane l, word w): channels 16mb + l/4 and 16mb + 8 + l/4
+          // (mb = w, or 2w + half for 2-bit codes), tokens 2(l%4), +1, +8, +9;
+          // v_off carries the lane's part of those offsets
 #pragma unroll
           for (int half = 0; half < (BITS == 4 ? 1 : 2); ++half) {
-            const int mb = BITS == 4 ? w : 2 * w + half;
             const uint32_t* m4 = &reg[s][k * (2 + VMW) + 2 + 4 * half];
             const uint32_t s01 = __byte_perm(m4[0], m4[1], 0x5410), z01 = __byte_perm(m4[0], m4[1], 0x7632);
             const uint32_t s89 = __byte_perm(m4[2], m4[3], 0x5410), z89 = __byte_perm(m4[2], m4[3], 0x7632);
@@ -879,8 +522,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
     }
     ok = mbar_wait(&bars[b], (jt >> 1) & 1, a.err) && ok;
     umma::fence_after_sync();
-    // the row's scores in two 32-column halves: a pass for the maximum, then
-    // one for the weights (tensor memory is read twice, the registers once)
+    // the row's 64 scores, read once from tensor memory as two 32-column halves
     const uint32_t tSj = tS + b * TN;
     const int tile0 = jt * TN;
     const bool masked = tile0 + TN - 1 > plim;
@@ -897,15 +539,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
         }
       }
     };
+    float xr[2][32];
+    load_row(xr[0], xr[1]);
     float mx = -INFINITY;
-    {
-      float x0[32], x1[32];
-      load_row(x0, x1);
 #pragma unroll
-      for (int c = 0; c < 32; ++c) mx = fmaxf(mx, fmaxf(x0[c], x1[c]));
-    }
+    for (int c = 0; c < 32; ++c) mx = fmaxf(mx, fmaxf(xr[0][c], xr[1][c]));
     mx *= alpha;  // alpha > 0 keeps the order
-    const bool need = mx > m_run + kLazyLog2;
+    const bool need = mx > m_run + kPrefillLazyLog2;
     if (__any_sync(0xffffffffu, need)) {
       const float mnew = need ? fmaxf(m_run, mx) : m_run;
       const float f = m_run == -INFINITY ? 0.f : fast_exp2(m_run - mnew);
@@ -913,14 +553,15 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
       m_run = mnew;
       if (jt > 0) {  // this warp's rows of O in tensor memory, once O += P V of tile jt-1 is in
         wait_o(jt - 1, wg);
+        // 16 columns at a time: the row's scores stay in registers meanwhile
 #pragma unroll
-        for (int c0 = 0; c0 < D; c0 += 32) {
-          float o[32];
-          umma::ld32(tO + lane_base + c0, o);
+        for (int c0 = 0; c0 < D; c0 += 16) {
+          float o[16];
+          umma::ld16(tO + lane_base + c0, o);
           umma::wait_ld();
 #pragma unroll
-          for (int c = 0; c < 32; ++c) o[c] *= f;
-          umma::st32(tO + lane_base + c0, o);
+          for (int c = 0; c < 16; ++c) o[c] *= f;
+          umma::st16(tO + lane_base + c0, o);
         }
         umma::wait_st();
       }
@@ -929,8 +570,6 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
     uint8_t* const pd = Ps + (2 * wg + b) * SM::P_BYTES;
     float2 sum2 = make_float2(0.f, 0.f);
     const float2 al2 = make_float2(alpha, alpha), nb2 = make_float2(nb, nb);
-    float xr[2][32];
-    load_row(xr[0], xr[1]);
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const float (&x)[32] = xr[hf];
@@ -1026,32 +665,13 @@ static int launch_prefill_umma_t(PrefillArgs a, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
 }
 
-constexpr int kPrefillWarps = 4;  // 16 query rows each: 64 rows per CTA
-
-template <int D, int BITS, int G>
-static int launch_prefill_t(PrefillArgs a, cudaStream_t stream) {
-  constexpr int NW = kPrefillWarps;
-  const int64_t tiles = ((int64_t)a.max_q * a.grp + 16 * NW - 1) / (16 * NW);
-  const int64_t blocks = (int64_t)a.num_seqs * a.n_kv_heads * tiles;
-  if (blocks <= 0) return TKV_OK;
-  if (blocks > 0x7fffffffLL) return TKV_INVALID_ARGUMENT;
-  a.n_rt = (int)tiles;
-  prefill_cta_kernel<D, BITS, G, NW><<<(unsigned)blocks, 32 * NW, 0, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
-}
-
-#ifdef TKV_PREFILL_MMA_SYNC
-#define TKV_PREFILL_LAUNCH launch_prefill_t
-#else
-#define TKV_PREFILL_LAUNCH launch_prefill_umma_t
-#endif
 template <int D, int BITS>
 static int launch_prefill_g(const PrefillArgs& a, int G, cudaStream_t stream) {
   switch (G) {
-    case 16: return TKV_PREFILL_LAUNCH<D, BITS, 16>(a, stream);
-    case 32: return TKV_PREFILL_LAUNCH<D, BITS, 32>(a, stream);
-    case 64: return TKV_PREFILL_LAUNCH<D, BITS, 64>(a, stream);
-    case 128: return TKV_PREFILL_LAUNCH<D, BITS, 128>(a, stream);
+    case 16: return launch_prefill_umma_t<D, BITS, 16>(a, stream);
+    case 32: return launch_prefill_umma_t<D, BITS, 32>(a, stream);
+    case 64: return launch_prefill_umma_t<D, BITS, 64>(a, stream);
+    case 128: return launch_prefill_umma_t<D, BITS, 128>(a, stream);
     default: return TKV_NOT_IMPLEMENTED;
   }
 }
