@@ -95,10 +95,26 @@ __device__ __forceinline__ constexpr int kchan_at(int p) {
 // well inside the f16 range, and f16 keeps the same relative precision at any
 // magnitude.
 constexpr float kPrefillLazyLog2 = 8.0f;
-constexpr int kUmmaRows = 128;  // query rows per warpgroup (the MMA's M)
-constexpr int kUmmaWG = 2;      // warpgroups per CTA
+constexpr int kUmmaRows = 128;  // query rows per softmax warpgroup (the MMA's M)
+constexpr int kUmmaWG = 2;      // softmax warpgroups per CTA
 constexpr int kUmmaTN = 64;     // tokens per KV tile
-constexpr int kUmmaThreads = 128 * kUmmaWG;
+constexpr int kUmmaSoftmax = 128 * kUmmaWG;  // softmax threads: one query row each
+constexpr int kUmmaProducers = 256;          // dequantising (producer) threads
+constexpr int kUmmaCtaThreads = kUmmaSoftmax + kUmmaProducers;
+// named barriers: 1, 2 the softmax warpgroups, 3 the producers (0 is __syncthreads)
+constexpr int kBarSoftmax = 1, kBarProducers = 3;
+
+// Named-barrier AND over `nthreads` threads (whole warps) of barrier `id`.
+__device__ __forceinline__ bool bar_and(int id, int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, %2, %3, q;\n\tselp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
 
 template <int D>
 struct UmmaSmem {
@@ -112,17 +128,17 @@ struct UmmaSmem {
   static constexpr int V_OFF = K_OFF + 2 * K_BYTES;
   static constexpr int P_OFF = V_OFF + 3 * V_BYTES;  // [warpgroup][2]
   static constexpr int BAR_OFF = P_OFF + 2 * kUmmaWG * P_BYTES;
-  static constexpr int BYTES = BAR_OFF + 64;
+  static constexpr int BYTES = BAR_OFF + 128;
   // tensor memory: per warpgroup 256 columns, S of even and odd tiles, then O
   static constexpr uint32_t TWG = 256, TCOLS = 512;
   static_assert(2 * kUmmaTN + D <= TWG, "a warpgroup's S and O fit its columns");
 };
 
 template <int D, int BITS, int G>
-__global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillArgs a) {
+__global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(PrefillArgs a) {
   using F = Fmt<D, BITS, G>;
   using SM = UmmaSmem<D>;
-  constexpr int NT = kUmmaThreads, TN = kUmmaTN, NSUB = TN / kPage;
+  constexpr int NT = kUmmaProducers, TN = kUmmaTN, NSUB = TN / kPage;
   constexpr int WPR = D * BITS / 32;          // key-code words per token row
   constexpr int CPW = 32 / BITS;              // channels per key word
   constexpr int HP = CPW / 2;                 // f16 pairs per key word
@@ -144,12 +160,22 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
   uint8_t* const Ks = smem + SM::K_OFF;
   uint8_t* const Vs = smem + SM::V_OFF;
   uint8_t* const Ps = smem + SM::P_OFF;
-  // bars[b]: S of tiles j = b (mod 2) done (both warpgroups); bars[2 + 2 w + b]:
-  // warpgroup w's O += P_j V_j of those tiles done
+  // Pipeline barriers (tile j uses parity class j % 2 or j % 3, phase j / 2 or j / 3):
+  //   sdone[b]     S_j = Q K_j^T of both softmax warpgroups done (commit)
+  //   odone[w][b]  warpgroup w's O += P_j V_j done (commit)
+  //   sfree[b]     both softmax warpgroups have read S_j (2 arrivals)
+  //   vready[v]    V_j stored (the producers' leader)
+  //   vfree[v]     both warpgroups' O += P_j V_j done (2 commits)
   uint64_t* const bars = reinterpret_cast<uint64_t*>(smem + SM::BAR_OFF);
-  uint32_t* const tslot = reinterpret_cast<uint32_t*>(bars + 6);
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int wg = tid >> 7, wt = tid & 127;  // warpgroup, row in the warpgroup
+  uint64_t* const sdone = bars;
+  uint64_t* const odone = bars + 2;  // [w * 2 + b]
+  uint64_t* const sfree = bars + 6;
+  uint64_t* const vready = bars + 8;
+  uint64_t* const vfree = bars + 11;
+  uint32_t* const tslot = reinterpret_cast<uint32_t*>(bars + 14);
+  const int ctid = threadIdx.x, warp = ctid >> 5;
+  const int wg = ctid >> 7, wt = ctid & 127;  // warpgroup, row in the warpgroup (softmax)
+  const bool producer = ctid >= kUmmaSoftmax;
 
   const int64_t bid = blockIdx.x;
   const int rt = a.n_rt - 1 - (int)(bid % a.n_rt);
@@ -159,16 +185,16 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
   const int q0 = a.cu_q[b], n = a.cu_q[b + 1] - q0;
   if (L < 0 || L > a.max_blocks * kPage || n < 0 || n > L || n > a.max_q || q0 < 0 ||
       q0 + n > a.total_q) {
-    if (rt == 0 && h == 0 && tid == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
+    if (rt == 0 && h == 0 && ctid == 0) set_err(a.err, TKV_ERR_BAD_LENGTH);
     return;
   }
-  const int rows = n * a.grp, r0 = rt * kUmmaThreads;
+  const int rows = n * a.grp, r0 = rt * kUmmaSoftmax;
   if (r0 >= rows) return;
-  const int rho = r0 + tid;
-  const bool valid = rho < rows;
+  const int rho = r0 + ctid;
+  const bool valid = !producer && rho < rows;
   const int qi = valid ? rho / a.grp : 0;
   const int plim = valid ? L - n + qi : -1;  // causal limit of this thread's row
-  const int kv_end = L - n + min(rows - 1, r0 + kUmmaThreads - 1) / a.grp + 1;
+  const int kv_end = L - n + min(rows - 1, r0 + kUmmaSoftmax - 1) / a.grp + 1;
   const int64_t qrow = ((int64_t)(q0 + qi) * a.num_q_heads + h * a.grp + (valid ? rho % a.grp : 0)) * D;
   const int nq = nq_len(L, a.residual, G);
   const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
@@ -179,460 +205,472 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
 
   const int n_read = min(nq / kPage, (n_pages + F::PPG - 1) / F::PPG * F::PPG);
   bool bad = false;
-  for (int p = tid; p < n_read; p += NT) {
+  for (int p = ctid; p < n_read; p += kUmmaCtaThreads) {
     const int ph = bt[p];
     bad |= ph < 0 || ph >= a.num_pages;
   }
   if (__syncthreads_or(bad)) {
-    if (tid == 0) set_err(a.err, TKV_ERR_BAD_PAGE);
+    if (ctid == 0) set_err(a.err, TKV_ERR_BAD_PAGE);
     return;
   }
   int row = 0;
   if (n_chunks > 0) {
     row = a.seq_slots ? a.seq_slots[b] : b;
     if (row < 0 || row >= a.max_seqs) {
-      if (tid == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
+      if (ctid == 0) set_err(a.err, TKV_ERR_BAD_SLOT);
       return;
     }
   }
 
-  // ---- tensor memory, barriers, the Q operand ----
+  // ---- tensor memory, barriers, the Q operand (softmax threads: one row each) ----
   if (warp == 0) umma::alloc(tslot, SM::TCOLS);
-  if (tid == 0) {
-    for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);
+  if (ctid == 0) {
+    for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);   // sdone, odone
+    for (int i = 6; i < 8; ++i) mbar_init(&bars[i], 2);   // sfree
+    for (int i = 8; i < 11; ++i) mbar_init(&bars[i], 1);  // vready
+    for (int i = 11; i < 14; ++i) mbar_init(&bars[i], 2); // vfree
     fence_mbar_init();
   }
+  if (!producer) {
 #pragma unroll
-  for (int k8 = 0; k8 < D; k8 += 8) {
-    uint32_t w[4];
+    for (int k8 = 0; k8 < D; k8 += 8) {
+      uint32_t w[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int c0 = kchan_at<BITS>(k8 + 2 * e), c1 = kchan_at<BITS>(k8 + 2 * e + 1);
-      w[e] = pack_h2(valid ? load_qv(a, qrow + c0) : 0.f, valid ? load_qv(a, qrow + c1) : 0.f);
+      for (int e = 0; e < 4; ++e) {
+        const int c0 = kchan_at<BITS>(k8 + 2 * e), c1 = kchan_at<BITS>(k8 + 2 * e + 1);
+        w[e] = pack_h2(valid ? load_qv(a, qrow + c0) : 0.f, valid ? load_qv(a, qrow + c1) : 0.f);
+      }
+      *reinterpret_cast<uint4*>(Qs + wg * SM::Q_BYTES + umma::umma_off(wt, k8, D)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
     }
-    *reinterpret_cast<uint4*>(Qs + wg * SM::Q_BYTES + umma::umma_off(wt, k8, D)) =
-        make_uint4(w[0], w[1], w[2], w[3]);
+    umma::fence_smem_to_async();
   }
-  umma::fence_smem_to_async();
   umma::fence_before_sync();
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = *tslot;
-  const uint32_t tS = tmem + wg * SM::TWG, tO = tS + 2 * TN;  // this warpgroup's columns
-  const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-
-  const uint8_t* pool_h = a.pool + (int64_t)h * F::PB;
-  const int64_t page_stride = (int64_t)a.n_kv_heads * F::PB;
-  constexpr int CHUNK = 2 * F::RBLK;
-  const uint8_t* ring_base =
-      reinterpret_cast<const uint8_t*>(a.ring) +
-      (((int64_t)row * a.n_kv_heads + h) * (a.ring_cap / kPage)) * CHUNK;
-  // Key code words are taken token-fastest: thread tid holds word column
-  // tid / 16 (channels kc0.. in tile order) of token tid % 16 of a page, so
-  // the 16-byte stores of 8 consecutive lanes fill one 128-byte core matrix
-  // of the K operand (no bank conflicts).
-  static_assert(KW <= NT, "one key word per thread and page");
-  const int kc0 = (tid / kPage) * CPW;
-  // this thread's store offsets in the operand tiles (sub-tile, half and
-  // neighbour offsets are compile-time): its key word (token tid % 16,
-  // channels kc0..), its value word's first (channel, token) pair, its P row
-  const uint32_t k_off = umma::umma_off(tid % kPage, tid < KW ? kc0 : 0, D);
-  const uint32_t v_off = umma::umma_off(16 * (BITS == 4 ? (tid >> 5) : 2 * (tid >> 5)) + ((tid & 31) >> 2),
-                                        2 * (tid & 3), TN);
-  const uint32_t p_off = umma::umma_off(wt, 0, TN);
-
-  // ---- registers of the next tile: NSUB sub-tiles of code words or ring vectors ----
-  uint32_t reg[NSUB][SLOT];
-  uint4 km[NKM][MVEC];
-  uint4 kml[MVEC];  // key meta of the group the previous tile ended in
-#pragma unroll
-  for (int v = 0; v < MVEC; ++v) kml[v] = make_uint4(0, 0, 0, 0);
-  // page ids of the next tile load_tile reads, and of the pages holding this
-  // thread's key meta for the key groups starting in it: loaded one call
-  // ahead, so the code-word loads never wait on a block-table load
-  int pid_n[NSUB], mid_n[NKM][MVEC];
-  auto fetch_ids = [&](int jt) {
-#pragma unroll
-    for (int s = 0; s < NSUB; ++s) {
-      const int j = jt * NSUB + s;
-      pid_n[s] = j < n_pages ? bt[j] : 0;
-    }
-#pragma unroll
-    for (int g = 0; g < NKM; ++g) {
-      const int j = jt * NSUB + (F::PPG >= NSUB ? 0 : g * F::PPG);
-      // threads without a key word (tid >= KW) have kc0 >= D: they fetch no meta
-      const bool starts = tid < KW && j < n_pages && j % F::PPG == 0;
-#pragma unroll
-      for (int v = 0; v < MVEC; ++v)
-        mid_n[g][v] = starts ? bt[j + (4 * (kc0 + 4 * v)) / F::KMS] : 0;
-    }
-  };
-  fetch_ids(0);
-  auto load_tile = [&](int jt) {
-    int pid[NSUB], mid[NKM][MVEC];
-#pragma unroll
-    for (int s = 0; s < NSUB; ++s) pid[s] = pid_n[s];
-#pragma unroll
-    for (int g = 0; g < NKM; ++g)
-#pragma unroll
-      for (int v = 0; v < MVEC; ++v) mid[g][v] = mid_n[g][v];
-    fetch_ids(jt + 1);
-#pragma unroll
-    for (int s = 0; s < NSUB; ++s) {
-      const int j = jt * NSUB + s;
-      if (j < n_pages) {
-        const uint8_t* pg = pool_h + (int64_t)pid[s] * page_stride;
-#pragma unroll
-        for (int k = 0; k < KPT; ++k) {
-          const int u = tid + k * NT;
-          if (u >= KW) continue;
-          reg[s][k * (2 + VMW)] =
-              __ldg(reinterpret_cast<const uint32_t*>(pg) + (u % kPage) * WPR + u / kPage);
-          const int l = u & 31, w = u >> 5;
-          reg[s][k * (2 + VMW) + 1] = __ldg(reinterpret_cast<const uint32_t*>(
-              pg + F::V_CODES_OFF + ((w / F::VW) * 32 + l) * 4 * F::VW + (w % F::VW) * 4));
-          const uint32_t* vmp = reinterpret_cast<const uint32_t*>(pg + F::V_META_OFF);
-          const int t0 = 2 * (l & 3);
-          if constexpr (F::NVG == 1) {
-            // one value group per token: (step, zero) of tokens t0, t0+1 and
-            // t0+8, t0+9 as two 8-byte loads (the same for both 2-bit halves)
-            const uint2 m0 = __ldg(reinterpret_cast<const uint2*>(vmp + t0));
-            const uint2 m1 = __ldg(reinterpret_cast<const uint2*>(vmp + t0 + 8));
-#pragma unroll
-            for (int x = 0; x < VMW; x += 4) {
-              reg[s][k * (2 + VMW) + 2 + x] = m0.x;
-              reg[s][k * (2 + VMW) + 3 + x] = m0.y;
-              reg[s][k * (2 + VMW) + 4 + x] = m1.x;
-              reg[s][k * (2 + VMW) + 5 + x] = m1.y;
-            }
-          } else {
-#pragma unroll
-            for (int x = 0; x < VMW; ++x) {
-              const int mb = BITS == 4 ? w : 2 * w + (x >> 2);
-              const int t = t0 + (x & 1) + 8 * ((x >> 1) & 1);
-              reg[s][k * (2 + VMW) + 2 + x] = __ldg(vmp + t * F::NVG + (16 * mb) / G);
-            }
-          }
-        }
-        const int ki = F::PPG >= NSUB ? 0 : s / (F::PPG >= NSUB ? 1 : F::PPG);
-        if (j % F::PPG == 0 && tid < KW) {  // a new key group: this thread's channels
-#pragma unroll
-          for (int v = 0; v < MVEC; ++v) {
-            const int off = 4 * (kc0 + 4 * v);
-            km[ki][v] = __ldg(reinterpret_cast<const uint4*>(
-                pool_h + (int64_t)mid[ki][v] * page_stride + F::BODY + off % F::KMS));
-          }
-        } else if (s == 0) {  // the group the previous tile ended in
-#pragma unroll
-          for (int v = 0; v < MVEC; ++v) km[0][v] = kml[v];
-        }
-      } else if (j < n16) {
-        const int t0 = nq + (j - n_pages) * kPage;
-        const uint8_t* ck = ring_base + (int64_t)((t0 % a.ring_cap) / kPage) * CHUNK;
-#pragma unroll
-        for (int k = 0; k < RPT; ++k) {
-          const int u = tid + k * NT;
-          if (u >= RV) continue;
-          const uint4 x = __ldg(reinterpret_cast<const uint4*>(ck) + u);
-          const uint4 y = __ldg(reinterpret_cast<const uint4*>(ck + F::RBLK) + u);
-          reg[s][8 * k + 0] = x.x; reg[s][8 * k + 1] = x.y; reg[s][8 * k + 2] = x.z; reg[s][8 * k + 3] = x.w;
-          reg[s][8 * k + 4] = y.x; reg[s][8 * k + 5] = y.y; reg[s][8 * k + 6] = y.z; reg[s][8 * k + 7] = y.w;
-        }
-      }
-    }
-#pragma unroll
-    for (int v = 0; v < MVEC; ++v) kml[v] = km[NKM - 1][v];
-  };
-
-  // dequantise the registers of tile jt into the K and V^T operand tiles
-  auto store_tile = [&](int jt, uint8_t* kd, uint8_t* vd) {
-    // the (step, zero) f16 pairs of this thread's key channels, once per key
-    // group of the tile (not per 16-token page)
-    uint32_t spk[NKM][HP], zpk[NKM][HP];
-#pragma unroll
-    for (int ki = 0; ki < NKM; ++ki) {
-      uint32_t mw[CPW];
-#pragma unroll
-      for (int v = 0; v < MVEC; ++v) {
-        mw[4 * v + 0] = km[ki][v].x; mw[4 * v + 1] = km[ki][v].y;
-        mw[4 * v + 2] = km[ki][v].z; mw[4 * v + 3] = km[ki][v].w;
-      }
-#pragma unroll
-      for (int i = 0; i < HP; ++i) {
-        spk[ki][i] = __byte_perm(mw[i], mw[i + HP], 0x5410);
-        zpk[ki][i] = __byte_perm(mw[i], mw[i + HP], 0x7632);
-      }
-    }
-#pragma unroll
-    for (int s = 0; s < NSUB; ++s) {
-      const int j = jt * NSUB + s;
-      const int tb = s * kPage;  // the sub-tile's first token in the tile
-      if (j < n_pages) {
-        const int ki = F::PPG >= NSUB ? 0 : s / (F::PPG >= NSUB ? 1 : F::PPG);
-        const uint32_t(&sp)[HP] = spk[ki];
-        const uint32_t(&zp)[HP] = zpk[ki];
-#pragma unroll
-        for (int k = 0; k < KPT; ++k) {
-          const int u = tid + k * NT;
-          if (u >= KW) continue;
-          const uint32_t x = reg[s][k * (2 + VMW)], x8 = x >> 8;
-          uint32_t hv[HP];
-#pragma unroll
-          for (int i = 0; i < HP; ++i) {
-            uint32_t c;
-            if (BITS == 4) {
-              c = (i & 1) ? code_pair<0x00F000F0u>(i < 2 ? x : x8)
-                          : code_pair<0x000F000Fu>(i < 2 ? x : x8);
-            } else {
-              const uint32_t y = i < 4 ? x : x8;
-              c = (i & 3) == 0 ? code_pair<0x00030003u>(y)
-                : (i & 3) == 1 ? code_pair<0x000C000Cu>(y)
-                : (i & 3) == 2 ? code_pair<0x00300030u>(y)
-                               : code_pair<0x00C000C0u>(y);
-            }
-            hv[i] = hfma2(c, sp[i], zp[i]);
-          }
-#pragma unroll
-          for (int q = 0; q < HP / 4; ++q)
-            *reinterpret_cast<uint4*>(kd + k_off + s * 32 * D + q * 128) =
-                make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
-          // value word (lane l, word w): channels 16mb + l/4 and 16mb + 8 + l/4
-          // (mb = w, or 2w + half for 2-bit codes), tokens 2(l%4), +1, +8, +9;
-          // v_off carries the lane's part of those offsets
-#pragma unroll
-          for (int half = 0; half < (BITS == 4 ? 1 : 2); ++half) {
-            const uint32_t* m4 = &reg[s][k * (2 + VMW) + 2 + 4 * half];
-            const uint32_t s01 = __byte_perm(m4[0], m4[1], 0x5410), z01 = __byte_perm(m4[0], m4[1], 0x7632);
-            const uint32_t s89 = __byte_perm(m4[2], m4[3], 0x5410), z89 = __byte_perm(m4[2], m4[3], 0x7632);
-            uint32_t r[4];
-            if (BITS == 4 || half == 0)
-              value_frag<BITS, 0>(&reg[s][k * (2 + VMW) + 1], r);
-            else
-              value_frag<BITS, (BITS == 2 ? 1 : 0)>(&reg[s][k * (2 + VMW) + 1], r);
-            const uint32_t v0 = hfma2(hfma2(r[0], VCode<BITS>::kMul, VCode<BITS>::kAddLo), s01, z01);
-            const uint32_t v1 = hfma2(hfma2(r[1], VCode<BITS>::kMul, VCode<BITS>::kAddLo), s01, z01);
-            const uint32_t v2 = hfma2(hfma2(r[2], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
-            const uint32_t v3 = hfma2(hfma2(r[3], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
-            // rows 16 mb + gl (+8), tokens tb + tl (+8): v_off plus constants
-            uint8_t* const vp = vd + v_off + s * 256 + half * 32 * TN;
-            *reinterpret_cast<uint32_t*>(vp) = v0;
-            *reinterpret_cast<uint32_t*>(vp + 16 * TN) = v1;
-            *reinterpret_cast<uint32_t*>(vp + 128) = v2;
-            *reinterpret_cast<uint32_t*>(vp + 16 * TN + 128) = v3;
-          }
-        }
-      } else if (j < n16) {
-        const int t0 = nq + (j - n_pages) * kPage;
-#pragma unroll
-        for (int k = 0; k < RPT; ++k) {
-          const int u = tid + k * NT;
-          if (u >= RV) continue;
-          const int c16 = u >> 5, l = u & 31;
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const uint32_t kx = reg[s][8 * k + r], vx = reg[s][8 * k + 4 + r];
-            // K block: word r holds channels cc, cc+1 of token t
-            const int t = 8 * (r & 1) + (l >> 2), cc = 8 * (r >> 1) + 2 * (l & 3);
-            const int c = 16 * c16 + cc;
-            *reinterpret_cast<uint16_t*>(kd + umma::umma_off(tb + t, kpos<BITS>(c), D)) =
-                static_cast<uint16_t>(kx & 0xffffu);
-            *reinterpret_cast<uint16_t*>(kd + umma::umma_off(tb + t, kpos<BITS>(c + 1), D)) =
-                static_cast<uint16_t>(kx >> 16);
-            // V block: word r holds tokens tv, tv+1 of channel 16c16 + cv;
-            // tokens past the end (stale ring slots) become 0
-            const int tv = 8 * (r >> 1) + 2 * (l & 3), cv = 8 * (r & 1) + (l >> 2);
-            const uint32_t msk = (t0 + tv < L ? 0x0000ffffu : 0u) | (t0 + tv + 1 < L ? 0xffff0000u : 0u);
-            *reinterpret_cast<uint32_t*>(vd + umma::umma_off(16 * c16 + cv, tb + tv, TN)) = vx & msk;
-          }
-        }
-      } else {
-        // past the last token of the CTA's rows: zero K rows and V^T columns
-        for (int i = tid; i < kPage * D / 8; i += NT) {
-          const int t = i / (D / 8), c8 = (i % (D / 8)) * 8;
-          *reinterpret_cast<uint4*>(kd + umma::umma_off(tb + t, c8, D)) = make_uint4(0, 0, 0, 0);
-        }
-        for (int i = tid; i < D * 2; i += NT) {
-          const int c = i >> 1, t8 = (i & 1) * 8;
-          *reinterpret_cast<uint4*>(vd + umma::umma_off(c, tb + t8, TN)) = make_uint4(0, 0, 0, 0);
-        }
-      }
-    }
-  };
-
   constexpr uint32_t idS = umma::idesc_f16(kUmmaRows, TN, false);
   constexpr uint32_t idO = umma::idesc_f16(kUmmaRows, D, false);
-  const float alpha = a.alpha;
-  float m_run = -INFINITY, l_run = 0.f;
   bool ok = true;
-  // A parity wait on an mbarrier targets the oldest of its phases not yet
-  // known to be complete, at most one phase behind: tile j's S and O MMAs
-  // commit to barriers of parity class j & 1, phase j >> 1.
-  auto wait_o = [&](int j, int w) {  // warpgroup w's O += P_j V_j (and its MMAs before) done
-    ok = mbar_wait(&bars[2 + 2 * w + (j & 1)], (j >> 1) & 1, a.err) && ok;
-    umma::fence_after_sync();
-  };
-  auto issue_s = [&](int j) {  // S_j = Q K_j^T of both warpgroups into their S[j & 1]
-    if (tid == 0) {
-      umma::fence_after_sync();
-      const uint32_t kb = smem_u32(Ks + (j & 1) * SM::K_BYTES);
-#pragma unroll
-      for (int w = 0; w < kUmmaWG; ++w)
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma::mma_f16(tmem + w * SM::TWG + (j & 1) * TN,
-                        umma::smem_desc(smem_u32(Qs + w * SM::Q_BYTES) + 256 * kk, 128, 16 * D),
-                        umma::smem_desc(kb + 256 * kk, 128, 16 * D), idS, kk > 0);
-      umma::commit(&bars[j & 1]);
-    }
-  };
-  if (n_tiles > 0) {
-    load_tile(0);
-    store_tile(0, Ks, Vs);
-    if (n_tiles > 1) load_tile(1);
-    umma::fence_smem_to_async();
-    umma::fence_before_sync();
-    __syncthreads();
-    issue_s(0);
-  }
-  for (int jt = 0; jt < n_tiles; ++jt) {
-    const int b = jt & 1;
-    if (jt >= 2) {
-      // the P buffer b of this warpgroup, and when tile jt+1 is dequantised
-      // below, the V^T buffer (jt + 1) % 3 read by both warpgroups.  A wait on
-      // the other warpgroup's barrier is made only before the CTA-wide barrier
-      // of this iteration, which keeps that warpgroup from completing a second
-      // phase of it first (in the last tile there is no such barrier).
-      if (jt + 1 < n_tiles) {
-        wait_o(jt - 2, 0);
-        wait_o(jt - 2, 1);
-      } else {
-        wait_o(jt - 2, wg);
+
+  if (producer) {
+    // ======================= producer warpgroups =======================
+    const int tid = ctid - kUmmaSoftmax;  // 0 .. NT-1
+    const uint8_t* pool_h = a.pool + (int64_t)h * F::PB;
+    const int64_t page_stride = (int64_t)a.n_kv_heads * F::PB;
+    constexpr int CHUNK = 2 * F::RBLK;
+    const uint8_t* ring_base =
+        reinterpret_cast<const uint8_t*>(a.ring) +
+        (((int64_t)row * a.n_kv_heads + h) * (a.ring_cap / kPage)) * CHUNK;
+    // Key code words are taken token-fastest: thread tid holds word column
+    // tid / 16 (channels kc0.. in tile order) of token tid % 16 of a page, so
+    // the 16-byte stores of 8 consecutive lanes fill one 128-byte core matrix
+    // of the K operand (no bank conflicts).
+    static_assert(KW <= NT, "one key word per thread and page");
+    const int kc0 = (tid / kPage) * CPW;
+    // this thread's store offsets in the operand tiles (sub-tile, half and
+    // neighbour offsets are compile-time): its key word (token tid % 16,
+    // channels kc0..), its value word's first (channel, token) pair
+    const uint32_t k_off = umma::umma_off(tid % kPage, tid < KW ? kc0 : 0, D);
+    const uint32_t v_off = umma::umma_off(16 * (BITS == 4 ? (tid >> 5) : 2 * (tid >> 5)) + ((tid & 31) >> 2),
+                                          2 * (tid & 3), TN);
+    // ---- registers of the next tile: NSUB sub-tiles of code words or ring vectors ----
+    uint32_t reg[NSUB][SLOT];
+    uint4 km[NKM][MVEC];
+    uint4 kml[MVEC];  // key meta of the group the previous tile ended in
+  #pragma unroll
+    for (int v = 0; v < MVEC; ++v) kml[v] = make_uint4(0, 0, 0, 0);
+    // page ids of the next tile load_tile reads, and of the pages holding this
+    // thread's key meta for the key groups starting in it: loaded one call
+    // ahead, so the code-word loads never wait on a block-table load
+    int pid_n[NSUB], mid_n[NKM][MVEC];
+    auto fetch_ids = [&](int jt) {
+  #pragma unroll
+      for (int s = 0; s < NSUB; ++s) {
+        const int j = jt * NSUB + s;
+        pid_n[s] = j < n_pages ? bt[j] : 0;
       }
-    }
-    if (jt + 1 < n_tiles) {
-      store_tile(jt + 1, Ks + ((jt + 1) & 1) * SM::K_BYTES, Vs + ((jt + 1) % 3) * SM::V_BYTES);
-      if (jt + 2 < n_tiles) load_tile(jt + 2);  // in flight during this tile's softmax
+  #pragma unroll
+      for (int g = 0; g < NKM; ++g) {
+        const int j = jt * NSUB + (F::PPG >= NSUB ? 0 : g * F::PPG);
+        // threads without a key word (tid >= KW) have kc0 >= D: they fetch no meta
+        const bool starts = tid < KW && j < n_pages && j % F::PPG == 0;
+  #pragma unroll
+        for (int v = 0; v < MVEC; ++v)
+          mid_n[g][v] = starts ? bt[j + (4 * (kc0 + 4 * v)) / F::KMS] : 0;
+      }
+    };
+    fetch_ids(0);
+    auto load_tile = [&](int jt) {
+      int pid[NSUB], mid[NKM][MVEC];
+  #pragma unroll
+      for (int s = 0; s < NSUB; ++s) pid[s] = pid_n[s];
+  #pragma unroll
+      for (int g = 0; g < NKM; ++g)
+  #pragma unroll
+        for (int v = 0; v < MVEC; ++v) mid[g][v] = mid_n[g][v];
+      fetch_ids(jt + 1);
+  #pragma unroll
+      for (int s = 0; s < NSUB; ++s) {
+        const int j = jt * NSUB + s;
+        if (j < n_pages) {
+          const uint8_t* pg = pool_h + (int64_t)pid[s] * page_stride;
+  #pragma unroll
+          for (int k = 0; k < KPT; ++k) {
+            const int u = tid + k * NT;
+            if (u >= KW) continue;
+            reg[s][k * (2 + VMW)] =
+                __ldg(reinterpret_cast<const uint32_t*>(pg) + (u % kPage) * WPR + u / kPage);
+            const int l = u & 31, w = u >> 5;
+            reg[s][k * (2 + VMW) + 1] = __ldg(reinterpret_cast<const uint32_t*>(
+                pg + F::V_CODES_OFF + ((w / F::VW) * 32 + l) * 4 * F::VW + (w % F::VW) * 4));
+            const uint32_t* vmp = reinterpret_cast<const uint32_t*>(pg + F::V_META_OFF);
+            const int t0 = 2 * (l & 3);
+            if constexpr (F::NVG == 1) {
+              // one value group per token: (step, zero) of tokens t0, t0+1 and
+              // t0+8, t0+9 as two 8-byte loads (the same for both 2-bit halves)
+              const uint2 m0 = __ldg(reinterpret_cast<const uint2*>(vmp + t0));
+              const uint2 m1 = __ldg(reinterpret_cast<const uint2*>(vmp + t0 + 8));
+  #pragma unroll
+              for (int x = 0; x < VMW; x += 4) {
+                reg[s][k * (2 + VMW) + 2 + x] = m0.x;
+                reg[s][k * (2 + VMW) + 3 + x] = m0.y;
+                reg[s][k * (2 + VMW) + 4 + x] = m1.x;
+                reg[s][k * (2 + VMW) + 5 + x] = m1.y;
+              }
+            } else {
+  #pragma unroll
+              for (int x = 0; x < VMW; ++x) {
+                const int mb = BITS == 4 ? w : 2 * w + (x >> 2);
+                const int t = t0 + (x & 1) + 8 * ((x >> 1) & 1);
+                reg[s][k * (2 + VMW) + 2 + x] = __ldg(vmp + t * F::NVG + (16 * mb) / G);
+              }
+            }
+          }
+          const int ki = F::PPG >= NSUB ? 0 : s / (F::PPG >= NSUB ? 1 : F::PPG);
+          if (j % F::PPG == 0 && tid < KW) {  // a new key group: this thread's channels
+  #pragma unroll
+            for (int v = 0; v < MVEC; ++v) {
+              const int off = 4 * (kc0 + 4 * v);
+              km[ki][v] = __ldg(reinterpret_cast<const uint4*>(
+                  pool_h + (int64_t)mid[ki][v] * page_stride + F::BODY + off % F::KMS));
+            }
+          } else if (s == 0) {  // the group the previous tile ended in
+  #pragma unroll
+            for (int v = 0; v < MVEC; ++v) km[0][v] = kml[v];
+          }
+        } else if (j < n16) {
+          const int t0 = nq + (j - n_pages) * kPage;
+          const uint8_t* ck = ring_base + (int64_t)((t0 % a.ring_cap) / kPage) * CHUNK;
+  #pragma unroll
+          for (int k = 0; k < RPT; ++k) {
+            const int u = tid + k * NT;
+            if (u >= RV) continue;
+            const uint4 x = __ldg(reinterpret_cast<const uint4*>(ck) + u);
+            const uint4 y = __ldg(reinterpret_cast<const uint4*>(ck + F::RBLK) + u);
+            reg[s][8 * k + 0] = x.x; reg[s][8 * k + 1] = x.y; reg[s][8 * k + 2] = x.z; reg[s][8 * k + 3] = x.w;
+            reg[s][8 * k + 4] = y.x; reg[s][8 * k + 5] = y.y; reg[s][8 * k + 6] = y.z; reg[s][8 * k + 7] = y.w;
+          }
+        }
+      }
+  #pragma unroll
+      for (int v = 0; v < MVEC; ++v) kml[v] = km[NKM - 1][v];
+    };
+
+    // dequantise the registers of tile jt into the K and V^T operand tiles
+    auto store_tile = [&](int jt, uint8_t* kd, uint8_t* vd) {
+      // the (step, zero) f16 pairs of this thread's key channels, once per key
+      // group of the tile (not per 16-token page)
+      uint32_t spk[NKM][HP], zpk[NKM][HP];
+  #pragma unroll
+      for (int ki = 0; ki < NKM; ++ki) {
+        uint32_t mw[CPW];
+  #pragma unroll
+        for (int v = 0; v < MVEC; ++v) {
+          mw[4 * v + 0] = km[ki][v].x; mw[4 * v + 1] = km[ki][v].y;
+          mw[4 * v + 2] = km[ki][v].z; mw[4 * v + 3] = km[ki][v].w;
+        }
+  #pragma unroll
+        for (int i = 0; i < HP; ++i) {
+          spk[ki][i] = __byte_perm(mw[i], mw[i + HP], 0x5410);
+          zpk[ki][i] = __byte_perm(mw[i], mw[i + HP], 0x7632);
+        }
+      }
+  #pragma unroll
+      for (int s = 0; s < NSUB; ++s) {
+        const int j = jt * NSUB + s;
+        const int tb = s * kPage;  // the sub-tile's first token in the tile
+        if (j < n_pages) {
+          const int ki = F::PPG >= NSUB ? 0 : s / (F::PPG >= NSUB ? 1 : F::PPG);
+          const uint32_t(&sp)[HP] = spk[ki];
+          const uint32_t(&zp)[HP] = zpk[ki];
+  #pragma unroll
+          for (int k = 0; k < KPT; ++k) {
+            const int u = tid + k * NT;
+            if (u >= KW) continue;
+            const uint32_t x = reg[s][k * (2 + VMW)], x8 = x >> 8;
+            uint32_t hv[HP];
+  #pragma unroll
+            for (int i = 0; i < HP; ++i) {
+              uint32_t c;
+              if (BITS == 4) {
+                c = (i & 1) ? code_pair<0x00F000F0u>(i < 2 ? x : x8)
+                            : code_pair<0x000F000Fu>(i < 2 ? x : x8);
+              } else {
+                const uint32_t y = i < 4 ? x : x8;
+                c = (i & 3) == 0 ? code_pair<0x00030003u>(y)
+                  : (i & 3) == 1 ? code_pair<0x000C000Cu>(y)
+                  : (i & 3) == 2 ? code_pair<0x00300030u>(y)
+                                 : code_pair<0x00C000C0u>(y);
+              }
+              hv[i] = hfma2(c, sp[i], zp[i]);
+            }
+  #pragma unroll
+            for (int q = 0; q < HP / 4; ++q)
+              *reinterpret_cast<uint4*>(kd + k_off + s * 32 * D + q * 128) =
+                  make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
+            // value word (lane l, word w): channels 16mb + l/4 and 16mb + 8 + l/4
+            // (mb = w, or 2w + half for 2-bit codes), tokens 2(l%4), +1, +8, +9;
+            // v_off carries the lane's part of those offsets
+  #pragma unroll
+            for (int half = 0; half < (BITS == 4 ? 1 : 2); ++half) {
+              const uint32_t* m4 = &reg[s][k * (2 + VMW) + 2 + 4 * half];
+              const uint32_t s01 = __byte_perm(m4[0], m4[1], 0x5410), z01 = __byte_perm(m4[0], m4[1], 0x7632);
+              const uint32_t s89 = __byte_perm(m4[2], m4[3], 0x5410), z89 = __byte_perm(m4[2], m4[3], 0x7632);
+              uint32_t r[4];
+              if (BITS == 4 || half == 0)
+                value_frag<BITS, 0>(&reg[s][k * (2 + VMW) + 1], r);
+              else
+                value_frag<BITS, (BITS == 2 ? 1 : 0)>(&reg[s][k * (2 + VMW) + 1], r);
+              const uint32_t v0 = hfma2(hfma2(r[0], VCode<BITS>::kMul, VCode<BITS>::kAddLo), s01, z01);
+              const uint32_t v1 = hfma2(hfma2(r[1], VCode<BITS>::kMul, VCode<BITS>::kAddLo), s01, z01);
+              const uint32_t v2 = hfma2(hfma2(r[2], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
+              const uint32_t v3 = hfma2(hfma2(r[3], VCode<BITS>::kMul, VCode<BITS>::kAddHi), s89, z89);
+              // rows 16 mb + gl (+8), tokens tb + tl (+8): v_off plus constants
+              uint8_t* const vp = vd + v_off + s * 256 + half * 32 * TN;
+              *reinterpret_cast<uint32_t*>(vp) = v0;
+              *reinterpret_cast<uint32_t*>(vp + 16 * TN) = v1;
+              *reinterpret_cast<uint32_t*>(vp + 128) = v2;
+              *reinterpret_cast<uint32_t*>(vp + 16 * TN + 128) = v3;
+            }
+          }
+        } else if (j < n16) {
+          const int t0 = nq + (j - n_pages) * kPage;
+  #pragma unroll
+          for (int k = 0; k < RPT; ++k) {
+            const int u = tid + k * NT;
+            if (u >= RV) continue;
+            const int c16 = u >> 5, l = u & 31;
+  #pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const uint32_t kx = reg[s][8 * k + r], vx = reg[s][8 * k + 4 + r];
+              // K block: word r holds channels cc, cc+1 of token t
+              const int t = 8 * (r & 1) + (l >> 2), cc = 8 * (r >> 1) + 2 * (l & 3);
+              const int c = 16 * c16 + cc;
+              *reinterpret_cast<uint16_t*>(kd + umma::umma_off(tb + t, kpos<BITS>(c), D)) =
+                  static_cast<uint16_t>(kx & 0xffffu);
+              *reinterpret_cast<uint16_t*>(kd + umma::umma_off(tb + t, kpos<BITS>(c + 1), D)) =
+                  static_cast<uint16_t>(kx >> 16);
+              // V block: word r holds tokens tv, tv+1 of channel 16c16 + cv;
+              // tokens past the end (stale ring slots) become 0
+              const int tv = 8 * (r >> 1) + 2 * (l & 3), cv = 8 * (r & 1) + (l >> 2);
+              const uint32_t msk = (t0 + tv < L ? 0x0000ffffu : 0u) | (t0 + tv + 1 < L ? 0xffff0000u : 0u);
+              *reinterpret_cast<uint32_t*>(vd + umma::umma_off(16 * c16 + cv, tb + tv, TN)) = vx & msk;
+            }
+          }
+        } else {
+          // past the last token of the CTA's rows: zero K rows and V^T columns
+          for (int i = tid; i < kPage * D / 8; i += NT) {
+            const int t = i / (D / 8), c8 = (i % (D / 8)) * 8;
+            *reinterpret_cast<uint4*>(kd + umma::umma_off(tb + t, c8, D)) = make_uint4(0, 0, 0, 0);
+          }
+          for (int i = tid; i < D * 2; i += NT) {
+            const int c = i >> 1, t8 = (i & 1) * 8;
+            *reinterpret_cast<uint4*>(vd + umma::umma_off(c, tb + t8, TN)) = make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
+    };
+
+
+    int last_s = -1;  // the leader's last S issued
+    if (n_tiles > 0) load_tile(0);
+    for (int jt = 0; jt < n_tiles; ++jt) {
+      // K buffer jt % 2 once S_{jt-2} has read it; V buffer jt % 3 once both
+      // warpgroups' O += P_{jt-3} V_{jt-3} have
+      if (jt >= 2) ok = mbar_wait(&sdone[jt & 1], ((jt - 2) >> 1) & 1, a.err) && ok;
+      if (jt >= 3) ok = mbar_wait(&vfree[jt % 3], ((jt - 3) / 3) & 1, a.err) && ok;
+      umma::fence_after_sync();
+      store_tile(jt, Ks + (jt & 1) * SM::K_BYTES, Vs + (jt % 3) * SM::V_BYTES);
+      if (jt + 1 < n_tiles) load_tile(jt + 1);  // in flight while the tensor cores run
       umma::fence_smem_to_async();
       umma::fence_before_sync();
-      if (!__syncthreads_and(ok)) {
+      if (!bar_and(kBarProducers, kUmmaProducers, ok)) {
         ok = false;
         break;
       }
-      issue_s(jt + 1);
+      if (tid == 0) {
+        // S_jt into the S buffers jt % 2 once both warpgroups have read S_{jt-2}
+        umma::fence_after_sync();
+        if (jt < 2 || mbar_wait(&sfree[jt & 1], ((jt - 2) >> 1) & 1, a.err)) {
+          const uint32_t kb = smem_u32(Ks + (jt & 1) * SM::K_BYTES);
+#pragma unroll
+          for (int w = 0; w < kUmmaWG; ++w)
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+              umma::mma_f16(tmem + w * SM::TWG + (jt & 1) * TN,
+                            umma::smem_desc(smem_u32(Qs + w * SM::Q_BYTES) + 256 * kk, 128, 16 * D),
+                            umma::smem_desc(kb + 256 * kk, 128, 16 * D), idS, kk > 0);
+          umma::commit(&sdone[jt & 1]);
+          last_s = jt;
+          mbar_arrive(&vready[jt % 3]);
+        } else {
+          ok = false;  // the others stop at the next barrier
+        }
+      }
     }
-    ok = mbar_wait(&bars[b], (jt >> 1) & 1, a.err) && ok;
-    umma::fence_after_sync();
-    // the row's 64 scores, read once from tensor memory as two 32-column halves
-    const uint32_t tSj = tS + b * TN;
-    const int tile0 = jt * TN;
-    const bool masked = tile0 + TN - 1 > plim;
-    static_assert(TN == 64, "the row's scores are read as two 32-column halves");
-    auto load_row = [&](float (&x0)[32], float (&x1)[32]) {  // both halves, one wait
-      umma::ld32(tSj + lane_base, x0);
-      umma::ld32(tSj + lane_base + 32, x1);
+    // a wait that gave up: no MMA of this thread may still run when tensor
+    // memory is released
+    if (tid == 0 && last_s >= 0 && !ok) mbar_wait(&sdone[last_s & 1], (last_s >> 1) & 1, nullptr);
+  } else {
+    // ======================= softmax warpgroups =======================
+    const uint32_t tS = tmem + wg * SM::TWG, tO = tS + 2 * TN;  // this warpgroup's columns
+    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    const uint32_t p_off = umma::umma_off(wt, 0, TN);
+    const float alpha = a.alpha;
+    float m_run = -INFINITY, l_run = 0.f;
+    int last_pv = -1;  // this warpgroup's last O += P V (thread wt == 0)
+    // warpgroup wg's O += P_j V_j (and its MMAs before) done
+    auto wait_o = [&](int j) {
+      ok = mbar_wait(&odone[2 * wg + (j & 1)], (j >> 1) & 1, a.err) && ok;
+      umma::fence_after_sync();
+    };
+    for (int jt = 0; jt < n_tiles; ++jt) {
+      const int b = jt & 1;
+      ok = mbar_wait(&sdone[b], (jt >> 1) & 1, a.err) && ok;
+      umma::fence_after_sync();
+      // the row's 64 scores, read once from tensor memory as two 32-column halves
+      const uint32_t tSj = tS + b * TN;
+      const int tile0 = jt * TN;
+      const bool masked = tile0 + TN - 1 > plim;
+      static_assert(TN == 64, "the row's scores are read as two 32-column halves");
+      float xr[2][32];
+      umma::ld32(tSj + lane_base, xr[0]);
+      umma::ld32(tSj + lane_base + 32, xr[1]);
       umma::wait_ld();
       if (masked) {
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          x0[c] = tile0 + c <= plim ? x0[c] : -INFINITY;
-          x1[c] = tile0 + 32 + c <= plim ? x1[c] : -INFINITY;
+          xr[0][c] = tile0 + c <= plim ? xr[0][c] : -INFINITY;
+          xr[1][c] = tile0 + 32 + c <= plim ? xr[1][c] : -INFINITY;
         }
       }
-    };
-    float xr[2][32];
-    load_row(xr[0], xr[1]);
-    float mx = -INFINITY;
+      float mx = -INFINITY;
 #pragma unroll
-    for (int c = 0; c < 32; ++c) mx = fmaxf(mx, fmaxf(xr[0][c], xr[1][c]));
-    mx *= alpha;  // alpha > 0 keeps the order
-    const bool need = mx > m_run + kPrefillLazyLog2;
-    if (__any_sync(0xffffffffu, need)) {
-      const float mnew = need ? fmaxf(m_run, mx) : m_run;
-      const float f = m_run == -INFINITY ? 0.f : fast_exp2(m_run - mnew);
-      l_run *= f;
-      m_run = mnew;
-      if (jt > 0) {  // this warp's rows of O in tensor memory, once O += P V of tile jt-1 is in
-        wait_o(jt - 1, wg);
-        // 16 columns at a time: the row's scores stay in registers meanwhile
+      for (int c = 0; c < 32; ++c) mx = fmaxf(mx, fmaxf(xr[0][c], xr[1][c]));
+      mx *= alpha;  // alpha > 0 keeps the order
+      const bool need = mx > m_run + kPrefillLazyLog2;
+      if (__any_sync(0xffffffffu, need)) {
+        const float mnew = need ? fmaxf(m_run, mx) : m_run;
+        const float f = m_run == -INFINITY ? 0.f : fast_exp2(m_run - mnew);
+        l_run *= f;
+        m_run = mnew;
+        if (jt > 0) {  // this warp's rows of O in tensor memory, once O += P V of tile jt-1 is in
+          wait_o(jt - 1);
+          // 16 columns at a time: the row's scores stay in registers meanwhile
 #pragma unroll
-        for (int c0 = 0; c0 < D; c0 += 16) {
-          float o[16];
-          umma::ld16(tO + lane_base + c0, o);
-          umma::wait_ld();
+          for (int c0 = 0; c0 < D; c0 += 16) {
+            float o[16];
+            umma::ld16(tO + lane_base + c0, o);
+            umma::wait_ld();
 #pragma unroll
-          for (int c = 0; c < 16; ++c) o[c] *= f;
-          umma::st16(tO + lane_base + c0, o);
+            for (int c = 0; c < 16; ++c) o[c] *= f;
+            umma::st16(tO + lane_base + c0, o);
+          }
+          umma::wait_st();
         }
-        umma::wait_st();
+      }
+      if (jt >= 2) wait_o(jt - 2);  // the P buffer b, read by O += P_{jt-2} V_{jt-2}
+      const float nb = m_run == -INFINITY ? 0.f : -m_run;
+      uint8_t* const pd = Ps + (2 * wg + b) * SM::P_BYTES;
+      float2 sum2 = make_float2(0.f, 0.f);
+      const float2 al2 = make_float2(alpha, alpha), nb2 = make_float2(nb, nb);
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const float (&x)[32] = xr[hf];
+#pragma unroll
+        for (int c8 = 0; c8 < 32; c8 += 8) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 y = ffma2(make_float2(x[c8 + 2 * e], x[c8 + 2 * e + 1]), al2, nb2);
+            const float2 pp = make_float2(fast_exp2(y.x), fast_exp2(y.y));
+            sum2 = fadd2(sum2, pp);
+            w[e] = pack_h2(pp.x, pp.y);
+          }
+          *reinterpret_cast<uint4*>(pd + p_off + (32 * hf + c8) * 16) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      l_run += sum2.x + sum2.y;
+      umma::fence_smem_to_async();
+      umma::fence_before_sync();
+      // this warpgroup's 128 threads only
+      if (!bar_and(kBarSoftmax + wg, 128, ok)) {
+        ok = false;
+        break;
+      }
+      if (wt == 0) {  // S_jt read; O += P_jt V_jt once V_jt is stored
+        umma::fence_after_sync();
+        mbar_arrive(&sfree[b]);
+        if (mbar_wait(&vready[jt % 3], (jt / 3) & 1, a.err)) {
+          const uint32_t vb = smem_u32(Vs + (jt % 3) * SM::V_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < TN / 16; ++kk)
+            umma::mma_f16(tO, umma::smem_desc(smem_u32(pd) + 256 * kk, 128, 16 * TN),
+                          umma::smem_desc(vb + 256 * kk, 128, 16 * TN), idO, jt > 0 || kk > 0);
+          umma::commit(&odone[2 * wg + b]);
+          umma::commit(&vfree[jt % 3]);
+          last_pv = jt;
+        } else {
+          ok = false;  // the warpgroup stops at the next barrier
+        }
       }
     }
-    const float nb = m_run == -INFINITY ? 0.f : -m_run;
-    uint8_t* const pd = Ps + (2 * wg + b) * SM::P_BYTES;
-    float2 sum2 = make_float2(0.f, 0.f);
-    const float2 al2 = make_float2(alpha, alpha), nb2 = make_float2(nb, nb);
+    if (ok && n_tiles > 0) wait_o(n_tiles - 1);
+    if (wt == 0 && last_pv >= 0 && !ok)
+      mbar_wait(&odone[2 * wg + (last_pv & 1)], (last_pv >> 1) & 1, nullptr);
+    if (bar_and(kBarSoftmax + wg, 128, ok) && n_tiles > 0) {
+      // ---- normalise and write this thread's row ----
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      const float (&x)[32] = xr[hf];
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        float o[32];
+        umma::ld32(tO + lane_base + c0, o);
+        umma::wait_ld();
+        if (valid) {
 #pragma unroll
-      for (int c8 = 0; c8 < 32; c8 += 8) {
-        uint32_t w[4];
+          for (int c = 0; c < 32; c += 8) {
+            const int64_t oi = qrow + c0 + c;
+            if (a.out_dtype == TKV_F32) {
+              float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + oi);
+              dst[0] = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+              dst[1] = make_float4(o[c + 4] * inv, o[c + 5] * inv, o[c + 6] * inv, o[c + 7] * inv);
+            } else if (a.out_dtype == TKV_BF16) {
+              uint32_t w[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 y = ffma2(make_float2(x[c8 + 2 * e], x[c8 + 2 * e + 1]), al2, nb2);
-          const float2 pp = make_float2(fast_exp2(y.x), fast_exp2(y.y));
-          sum2 = fadd2(sum2, pp);
-          w[e] = pack_h2(pp.x, pp.y);
-        }
-        *reinterpret_cast<uint4*>(pd + p_off + (32 * hf + c8) * 16) =
-            make_uint4(w[0], w[1], w[2], w[3]);
-      }
-    }
-    l_run += sum2.x + sum2.y;
-    umma::fence_smem_to_async();
-    umma::fence_before_sync();
-    // this warpgroup's 128 threads only (named barrier 1 + wg)
-    asm volatile("bar.sync %0, %1;\n" ::"r"(1 + wg), "r"(128) : "memory");
-    if (wt == 0) {  // O += P_jt V_jt of this warpgroup
-      umma::fence_after_sync();
-      const uint32_t vb = smem_u32(Vs + (jt % 3) * SM::V_BYTES);
+              for (int e = 0; e < 4; ++e) {
+                const __nv_bfloat162 hh = __floats2bfloat162_rn(o[c + 2 * e] * inv, o[c + 2 * e + 1] * inv);
+                w[e] = *reinterpret_cast<const uint32_t*>(&hh);
+              }
+              *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + oi) =
+                  make_uint4(w[0], w[1], w[2], w[3]);
+            } else {
+              uint32_t w[4];
 #pragma unroll
-      for (int kk = 0; kk < TN / 16; ++kk)
-        umma::mma_f16(tO, umma::smem_desc(smem_u32(pd) + 256 * kk, 128, 16 * TN),
-                      umma::smem_desc(vb + 256 * kk, 128, 16 * TN), idO, jt > 0 || kk > 0);
-      umma::commit(&bars[2 + 2 * wg + b]);
-    }
-  }
-  if (ok && n_tiles > 0) wait_o(n_tiles - 1, wg);
-  if (__syncthreads_and(ok) && n_tiles > 0) {
-    // ---- normalise and write this thread's row ----
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-#pragma unroll
-    for (int c0 = 0; c0 < D; c0 += 32) {
-      float o[32];
-      umma::ld32(tO + lane_base + c0, o);
-      umma::wait_ld();
-      if (valid) {
-#pragma unroll
-        for (int c = 0; c < 32; c += 8) {
-          const int64_t oi = qrow + c0 + c;
-          if (a.out_dtype == TKV_F32) {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + oi);
-            dst[0] = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
-            dst[1] = make_float4(o[c + 4] * inv, o[c + 5] * inv, o[c + 6] * inv, o[c + 7] * inv);
-          } else if (a.out_dtype == TKV_BF16) {
-            uint32_t w[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const __nv_bfloat162 hh = __floats2bfloat162_rn(o[c + 2 * e] * inv, o[c + 2 * e + 1] * inv);
-              w[e] = *reinterpret_cast<const uint32_t*>(&hh);
+              for (int e = 0; e < 4; ++e) w[e] = pack_h2(o[c + 2 * e] * inv, o[c + 2 * e + 1] * inv);
+              *reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + oi) = make_uint4(w[0], w[1], w[2], w[3]);
             }
-            *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + oi) =
-                make_uint4(w[0], w[1], w[2], w[3]);
-          } else {
-            uint32_t w[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) w[e] = pack_h2(o[c + 2 * e] * inv, o[c + 2 * e + 1] * inv);
-            *reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + oi) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
       }
@@ -647,7 +685,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) prefill_umma_kernel(PrefillAr
 template <int D, int BITS, int G>
 static int launch_prefill_umma_t(PrefillArgs a, cudaStream_t stream) {
   using SM = UmmaSmem<D>;
-  const int64_t tiles = ((int64_t)a.max_q * a.grp + kUmmaThreads - 1) / kUmmaThreads;
+  const int64_t tiles = ((int64_t)a.max_q * a.grp + kUmmaSoftmax - 1) / kUmmaSoftmax;
   const int64_t blocks = (int64_t)a.num_seqs * a.n_kv_heads * tiles;
   if (blocks <= 0) return TKV_OK;
   if (blocks > 0x7fffffffLL) return TKV_INVALID_ARGUMENT;
@@ -661,7 +699,7 @@ static int launch_prefill_umma_t(PrefillArgs a, cudaStream_t stream) {
     if (dev >= 0 && dev < kMaxPrefillDevices) attr_set[dev].store(1, std::memory_order_relaxed);
   }
   a.n_rt = (int)tiles;
-  prefill_umma_kernel<D, BITS, G><<<(unsigned)blocks, kUmmaThreads, SM::BYTES, stream>>>(a);
+  prefill_umma_kernel<D, BITS, G><<<(unsigned)blocks, kUmmaCtaThreads, SM::BYTES, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? TKV_OK : TKV_BACKEND_ERROR;
 }
 
