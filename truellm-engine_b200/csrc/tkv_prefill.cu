@@ -100,9 +100,9 @@ constexpr int kUmmaWG = 2;      // softmax warpgroups per CTA
 constexpr int kUmmaTN = 64;     // tokens per KV tile
 constexpr int kUmmaSoftmax = 128 * kUmmaWG;  // softmax threads: one query row each
 constexpr int kUmmaProducers = 256;          // dequantising (producer) threads
-constexpr int kUmmaCtaThreads = kUmmaSoftmax + kUmmaProducers;
-// named barriers: 1, 2 the softmax warpgroups, 3 the producers (0 is __syncthreads)
-constexpr int kBarSoftmax = 1, kBarProducers = 3;
+constexpr int kUmmaCtaThreads = kUmmaSoftmax + kUmmaProducers + 32;  // + the MMA warp
+// named barriers: 1, 2 the softmax warpgroups (0 is __syncthreads)
+constexpr int kBarSoftmax = 1;
 
 // Named-barrier AND over `nthreads` threads (whole warps) of barrier `id`.
 __device__ __forceinline__ bool bar_and(int id, int nthreads, bool v) {
@@ -128,7 +128,7 @@ struct UmmaSmem {
   static constexpr int V_OFF = K_OFF + 2 * K_BYTES;
   static constexpr int P_OFF = V_OFF + 3 * V_BYTES;  // [warpgroup][2]
   static constexpr int BAR_OFF = P_OFF + 2 * kUmmaWG * P_BYTES;
-  static constexpr int BYTES = BAR_OFF + 128;
+  static constexpr int BYTES = BAR_OFF + 256;
   // tensor memory: per warpgroup 256 columns, S of even and odd tiles, then O
   static constexpr uint32_t TWG = 256, TCOLS = 512;
   static_assert(2 * kUmmaTN + D <= TWG, "a warpgroup's S and O fit its columns");
@@ -163,19 +163,22 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
   // Pipeline barriers (tile j uses parity class j % 2 or j % 3, phase j / 2 or j / 3):
   //   sdone[b]     S_j = Q K_j^T of both softmax warpgroups done (commit)
   //   odone[w][b]  warpgroup w's O += P_j V_j done (commit)
-  //   sfree[b]     both softmax warpgroups have read S_j (2 arrivals)
-  //   vready[v]    V_j stored (the producers' leader)
   //   vfree[v]     both warpgroups' O += P_j V_j done (2 commits)
+  //   sfree[b]     every softmax thread has read its row of S_j (256 arrivals)
+  //   pready[w][b] warpgroup w's P_j stored (128 arrivals)
+  //   tready[v]    K_j and V_j stored (256 producer arrivals)
   uint64_t* const bars = reinterpret_cast<uint64_t*>(smem + SM::BAR_OFF);
   uint64_t* const sdone = bars;
-  uint64_t* const odone = bars + 2;  // [w * 2 + b]
-  uint64_t* const sfree = bars + 6;
-  uint64_t* const vready = bars + 8;
-  uint64_t* const vfree = bars + 11;
-  uint32_t* const tslot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* const odone = bars + 2;   // [w * 2 + b]
+  uint64_t* const vfree = bars + 6;
+  uint64_t* const sfree = bars + 9;
+  uint64_t* const pready = bars + 11;  // [w * 2 + b]
+  uint64_t* const tready = bars + 15;
+  uint32_t* const tslot = reinterpret_cast<uint32_t*>(bars + 18);
   const int ctid = threadIdx.x, warp = ctid >> 5;
   const int wg = ctid >> 7, wt = ctid & 127;  // warpgroup, row in the warpgroup (softmax)
-  const bool producer = ctid >= kUmmaSoftmax;
+  const bool producer = ctid >= kUmmaSoftmax && ctid < kUmmaSoftmax + kUmmaProducers;
+  const bool mma_warp = ctid >= kUmmaSoftmax + kUmmaProducers;
 
   const int64_t bid = blockIdx.x;
   const int rt = a.n_rt - 1 - (int)(bid % a.n_rt);
@@ -191,7 +194,7 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
   const int rows = n * a.grp, r0 = rt * kUmmaSoftmax;
   if (r0 >= rows) return;
   const int rho = r0 + ctid;
-  const bool valid = !producer && rho < rows;
+  const bool valid = ctid < kUmmaSoftmax && rho < rows;
   const int qi = valid ? rho / a.grp : 0;
   const int plim = valid ? L - n + qi : -1;  // causal limit of this thread's row
   const int kv_end = L - n + min(rows - 1, r0 + kUmmaSoftmax - 1) / a.grp + 1;
@@ -225,13 +228,14 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
   // ---- tensor memory, barriers, the Q operand (softmax threads: one row each) ----
   if (warp == 0) umma::alloc(tslot, SM::TCOLS);
   if (ctid == 0) {
-    for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);   // sdone, odone
-    for (int i = 6; i < 8; ++i) mbar_init(&bars[i], 2);   // sfree
-    for (int i = 8; i < 11; ++i) mbar_init(&bars[i], 1);  // vready
-    for (int i = 11; i < 14; ++i) mbar_init(&bars[i], 2); // vfree
+    for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);                 // sdone, odone
+    for (int i = 6; i < 9; ++i) mbar_init(&bars[i], 2);                 // vfree
+    for (int i = 9; i < 11; ++i) mbar_init(&bars[i], kUmmaSoftmax);     // sfree
+    for (int i = 11; i < 15; ++i) mbar_init(&bars[i], kUmmaRows);       // pready
+    for (int i = 15; i < 18; ++i) mbar_init(&bars[i], kUmmaProducers);  // tready
     fence_mbar_init();
   }
-  if (!producer) {
+  if (ctid < kUmmaSoftmax) {
 #pragma unroll
     for (int k8 = 0; k8 < D; k8 += 8) {
       uint32_t w[4];
@@ -493,45 +497,72 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
     };
 
 
-    int last_s = -1;  // the leader's last S issued
     if (n_tiles > 0) load_tile(0);
     for (int jt = 0; jt < n_tiles; ++jt) {
       // K buffer jt % 2 once S_{jt-2} has read it; V buffer jt % 3 once both
       // warpgroups' O += P_{jt-3} V_{jt-3} have
-      if (jt >= 2) ok = mbar_wait(&sdone[jt & 1], ((jt - 2) >> 1) & 1, a.err) && ok;
-      if (jt >= 3) ok = mbar_wait(&vfree[jt % 3], ((jt - 3) / 3) & 1, a.err) && ok;
+      if (jt >= 2 && !mbar_wait(&sdone[jt & 1], ((jt - 2) >> 1) & 1, a.err)) break;
+      if (jt >= 3 && !mbar_wait(&vfree[jt % 3], ((jt - 3) / 3) & 1, a.err)) break;
       umma::fence_after_sync();
       store_tile(jt, Ks + (jt & 1) * SM::K_BYTES, Vs + (jt % 3) * SM::V_BYTES);
       if (jt + 1 < n_tiles) load_tile(jt + 1);  // in flight while the tensor cores run
       umma::fence_smem_to_async();
-      umma::fence_before_sync();
-      if (!bar_and(kBarProducers, kUmmaProducers, ok)) {
-        ok = false;
-        break;
-      }
-      if (tid == 0) {
-        // S_jt into the S buffers jt % 2 once both warpgroups have read S_{jt-2}
+      mbar_arrive(&tready[jt % 3]);
+    }
+  } else if (mma_warp) {
+    // ======================= the MMA warp (lane 0 issues) =======================
+    // per tile j: S_{j+1} (as soon as K_{j+1} is stored and both warpgroups
+    // have read S_{j-1}), then O += P_j V_j of each warpgroup as its P_j lands
+    if ((ctid & 31) == 0 && n_tiles > 0) {
+      bool mok = true;
+      int last_s = -1, last_pv = -1;
+      auto issue_s = [&](int j) {
         umma::fence_after_sync();
-        if (jt < 2 || mbar_wait(&sfree[jt & 1], ((jt - 2) >> 1) & 1, a.err)) {
-          const uint32_t kb = smem_u32(Ks + (jt & 1) * SM::K_BYTES);
+        const uint32_t kb = smem_u32(Ks + (j & 1) * SM::K_BYTES);
 #pragma unroll
-          for (int w = 0; w < kUmmaWG; ++w)
+        for (int w = 0; w < kUmmaWG; ++w)
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk)
-              umma::mma_f16(tmem + w * SM::TWG + (jt & 1) * TN,
-                            umma::smem_desc(smem_u32(Qs + w * SM::Q_BYTES) + 256 * kk, 128, 16 * D),
-                            umma::smem_desc(kb + 256 * kk, 128, 16 * D), idS, kk > 0);
-          umma::commit(&sdone[jt & 1]);
-          last_s = jt;
-          mbar_arrive(&vready[jt % 3]);
-        } else {
-          ok = false;  // the others stop at the next barrier
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma::mma_f16(tmem + w * SM::TWG + (j & 1) * TN,
+                          umma::smem_desc(smem_u32(Qs + w * SM::Q_BYTES) + 256 * kk, 128, 16 * D),
+                          umma::smem_desc(kb + 256 * kk, 128, 16 * D), idS, kk > 0);
+        umma::commit(&sdone[j & 1]);
+        last_s = j;
+      };
+      mok = mbar_wait(&tready[0], 0, a.err);
+      if (mok) issue_s(0);
+      for (int j = 0; mok && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles) {
+          mok = mbar_wait(&tready[(j + 1) % 3], ((j + 1) / 3) & 1, a.err) &&
+                (j < 1 || mbar_wait(&sfree[(j + 1) & 1], ((j - 1) >> 1) & 1, a.err));
+          if (!mok) break;
+          issue_s(j + 1);
+        }
+        const uint32_t vb = smem_u32(Vs + (j % 3) * SM::V_BYTES);
+#pragma unroll
+        for (int w = 0; w < kUmmaWG; ++w) {
+          if (!mbar_wait(&pready[2 * w + (j & 1)], (j >> 1) & 1, a.err)) {
+            mok = false;
+            break;
+          }
+          umma::fence_after_sync();
+          const uint32_t pd = smem_u32(Ps + (2 * w + (j & 1)) * SM::P_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < TN / 16; ++kk)
+            umma::mma_f16(tmem + w * SM::TWG + 2 * TN, umma::smem_desc(pd + 256 * kk, 128, 16 * TN),
+                          umma::smem_desc(vb + 256 * kk, 128, 16 * TN), idO, j > 0 || kk > 0);
+          umma::commit(&odone[2 * w + (j & 1)]);
+          umma::commit(&vfree[j % 3]);
+          last_pv = j;
         }
       }
+      // no MMA may still run when tensor memory is released
+      if (last_s >= 0) mbar_wait(&sdone[last_s & 1], (last_s >> 1) & 1, nullptr);
+      if (last_pv >= 0) {
+        mbar_wait(&odone[last_pv & 1], (last_pv >> 1) & 1, nullptr);
+        mbar_wait(&odone[2 + (last_pv & 1)], (last_pv >> 1) & 1, nullptr);
+      }
     }
-    // a wait that gave up: no MMA of this thread may still run when tensor
-    // memory is released
-    if (tid == 0 && last_s >= 0 && !ok) mbar_wait(&sdone[last_s & 1], (last_s >> 1) & 1, nullptr);
   } else {
     // ======================= softmax warpgroups =======================
     const uint32_t tS = tmem + wg * SM::TWG, tO = tS + 2 * TN;  // this warpgroup's columns
@@ -539,35 +570,40 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
     const uint32_t p_off = umma::umma_off(wt, 0, TN);
     const float alpha = a.alpha;
     float m_run = -INFINITY, l_run = 0.f;
-    int last_pv = -1;  // this warpgroup's last O += P V (thread wt == 0)
     // warpgroup wg's O += P_j V_j (and its MMAs before) done
+    // (warp-uniform results: the tensor-memory loads after a wait are
+    // whole-warp instructions)
     auto wait_o = [&](int j) {
-      ok = mbar_wait(&odone[2 * wg + (j & 1)], (j >> 1) & 1, a.err) && ok;
+      ok = __all_sync(0xffffffffu, mbar_wait(&odone[2 * wg + (j & 1)], (j >> 1) & 1, a.err)) && ok;
       umma::fence_after_sync();
     };
     for (int jt = 0; jt < n_tiles; ++jt) {
       const int b = jt & 1;
-      ok = mbar_wait(&sdone[b], (jt >> 1) & 1, a.err) && ok;
+      ok = __all_sync(0xffffffffu, mbar_wait(&sdone[b], (jt >> 1) & 1, a.err)) && ok;
+      if (!ok) break;
       umma::fence_after_sync();
-      // the row's 64 scores, read once from tensor memory as two 32-column halves
+      // the row's 64 scores as two 32-column halves of tensor memory: a pass
+      // for the maximum, then one for the weights (32 score registers live)
       const uint32_t tSj = tS + b * TN;
       const int tile0 = jt * TN;
       const bool masked = tile0 + TN - 1 > plim;
       static_assert(TN == 64, "the row's scores are read as two 32-column halves");
-      float xr[2][32];
-      umma::ld32(tSj + lane_base, xr[0]);
-      umma::ld32(tSj + lane_base + 32, xr[1]);
-      umma::wait_ld();
-      if (masked) {
+      auto load_half = [&](int hf, float (&x)[32]) {
+        umma::ld32(tSj + lane_base + 32 * hf, x);
+        umma::wait_ld();
+        if (masked) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          xr[0][c] = tile0 + c <= plim ? xr[0][c] : -INFINITY;
-          xr[1][c] = tile0 + 32 + c <= plim ? xr[1][c] : -INFINITY;
+          for (int c = 0; c < 32; ++c) x[c] = tile0 + 32 * hf + c <= plim ? x[c] : -INFINITY;
         }
-      }
+      };
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 32; ++c) mx = fmaxf(mx, fmaxf(xr[0][c], xr[1][c]));
+      for (int hf = 0; hf < 2; ++hf) {
+        float x[32];
+        load_half(hf, x);
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) mx = fmaxf(mx, fmaxf(x[c], x[c + 1]));
+      }
       mx *= alpha;  // alpha > 0 keeps the order
       const bool need = mx > m_run + kPrefillLazyLog2;
       if (__any_sync(0xffffffffu, need)) {
@@ -577,7 +613,6 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
         m_run = mnew;
         if (jt > 0) {  // this warp's rows of O in tensor memory, once O += P V of tile jt-1 is in
           wait_o(jt - 1);
-          // 16 columns at a time: the row's scores stay in registers meanwhile
 #pragma unroll
           for (int c0 = 0; c0 < D; c0 += 16) {
             float o[16];
@@ -597,7 +632,12 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
       const float2 al2 = make_float2(alpha, alpha), nb2 = make_float2(nb, nb);
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        const float (&x)[32] = xr[hf];
+        float x[32];
+        load_half(hf, x);
+        if (hf == 1) {
+          umma::fence_before_sync();
+          mbar_arrive(&sfree[b]);  // this row of S_jt is no longer read
+        }
 #pragma unroll
         for (int c8 = 0; c8 < 32; c8 += 8) {
           uint32_t w[4];
@@ -615,31 +655,10 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
       l_run += sum2.x + sum2.y;
       umma::fence_smem_to_async();
       umma::fence_before_sync();
-      // this warpgroup's 128 threads only
-      if (!bar_and(kBarSoftmax + wg, 128, ok)) {
-        ok = false;
-        break;
-      }
-      if (wt == 0) {  // S_jt read; O += P_jt V_jt once V_jt is stored
-        umma::fence_after_sync();
-        mbar_arrive(&sfree[b]);
-        if (mbar_wait(&vready[jt % 3], (jt / 3) & 1, a.err)) {
-          const uint32_t vb = smem_u32(Vs + (jt % 3) * SM::V_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < TN / 16; ++kk)
-            umma::mma_f16(tO, umma::smem_desc(smem_u32(pd) + 256 * kk, 128, 16 * TN),
-                          umma::smem_desc(vb + 256 * kk, 128, 16 * TN), idO, jt > 0 || kk > 0);
-          umma::commit(&odone[2 * wg + b]);
-          umma::commit(&vfree[jt % 3]);
-          last_pv = jt;
-        } else {
-          ok = false;  // the warpgroup stops at the next barrier
-        }
-      }
+      mbar_arrive(&pready[2 * wg + b]);  // P_jt (and any O rescale) in place
+      if (!ok) break;
     }
     if (ok && n_tiles > 0) wait_o(n_tiles - 1);
-    if (wt == 0 && last_pv >= 0 && !ok)
-      mbar_wait(&odone[2 * wg + (last_pv & 1)], (last_pv >> 1) & 1, nullptr);
     if (bar_and(kBarSoftmax + wg, 128, ok) && n_tiles > 0) {
       // ---- normalise and write this thread's row ----
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
