@@ -132,6 +132,7 @@ struct UmmaSmem {
   // tensor memory: per warpgroup 256 columns, S of even and odd tiles, then O
   static constexpr uint32_t TWG = 256, TCOLS = 512;
   static_assert(2 * kUmmaTN + D <= TWG, "a warpgroup's S and O fit its columns");
+  static_assert(BYTES <= (1 << 18), "descriptor address fields (addr >> 4, 14 bits) never carry");
 };
 
 template <int D, int BITS, int G>
@@ -516,16 +517,27 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
     if ((ctid & 31) == 0 && n_tiles > 0) {
       bool mok = true;
       int last_s = -1, last_pv = -1;
+      // Operand descriptors are built once; the k-slice kk of an operand
+      // starts 256 kk bytes further, i.e. 16 kk in the descriptor's address
+      // field (shared-memory addresses stay below 2^18, so the field does not
+      // carry).
+      const uint64_t dq0 = umma::smem_desc(smem_u32(Qs), 128, 16 * D);
+      const uint64_t dq1 = umma::smem_desc(smem_u32(Qs + SM::Q_BYTES), 128, 16 * D);
+      const uint64_t dk0 = umma::smem_desc(smem_u32(Ks), 128, 16 * D);
+      const uint64_t dk1 = umma::smem_desc(smem_u32(Ks + SM::K_BYTES), 128, 16 * D);
+      const uint64_t dv0 = umma::smem_desc(smem_u32(Vs), 128, 16 * TN);
+      const uint64_t dp0 = umma::smem_desc(smem_u32(Ps), 128, 16 * TN);
+      constexpr uint64_t kVStep = SM::V_BYTES >> 4, kPStep = SM::P_BYTES >> 4;
       auto issue_s = [&](int j) {
         umma::fence_after_sync();
-        const uint32_t kb = smem_u32(Ks + (j & 1) * SM::K_BYTES);
+        const uint64_t dk = (j & 1) ? dk1 : dk0;
+        const uint32_t t0 = tmem + (j & 1) * TN;
 #pragma unroll
-        for (int w = 0; w < kUmmaWG; ++w)
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma::mma_f16(t0, dq0 + 16 * kk, dk + 16 * kk, idS, kk > 0);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma::mma_f16(tmem + w * SM::TWG + (j & 1) * TN,
-                          umma::smem_desc(smem_u32(Qs + w * SM::Q_BYTES) + 256 * kk, 128, 16 * D),
-                          umma::smem_desc(kb + 256 * kk, 128, 16 * D), idS, kk > 0);
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma::mma_f16(t0 + SM::TWG, dq1 + 16 * kk, dk + 16 * kk, idS, kk > 0);
         umma::commit(&sdone[j & 1]);
         last_s = j;
       };
@@ -538,7 +550,7 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
           if (!mok) break;
           issue_s(j + 1);
         }
-        const uint32_t vb = smem_u32(Vs + (j % 3) * SM::V_BYTES);
+        const uint64_t dv = dv0 + (j % 3) * kVStep;
 #pragma unroll
         for (int w = 0; w < kUmmaWG; ++w) {
           if (!mbar_wait(&pready[2 * w + (j & 1)], (j >> 1) & 1, a.err)) {
@@ -546,11 +558,11 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
             break;
           }
           umma::fence_after_sync();
-          const uint32_t pd = smem_u32(Ps + (2 * w + (j & 1)) * SM::P_BYTES);
+          const uint64_t dp = dp0 + (2 * w + (j & 1)) * kPStep;
 #pragma unroll
           for (int kk = 0; kk < TN / 16; ++kk)
-            umma::mma_f16(tmem + w * SM::TWG + 2 * TN, umma::smem_desc(pd + 256 * kk, 128, 16 * TN),
-                          umma::smem_desc(vb + 256 * kk, 128, 16 * TN), idO, j > 0 || kk > 0);
+            umma::mma_f16(tmem + w * SM::TWG + 2 * TN, dp + 16 * kk, dv + 16 * kk, idO,
+                          j > 0 || kk > 0);
           umma::commit(&odone[2 * w + (j & 1)]);
           umma::commit(&vfree[j % 3]);
           last_pv = j;
