@@ -56,6 +56,15 @@ __device__ __forceinline__ bool append_lengths_ok(const AppendArgs& a, int L, in
 constexpr int kFlushThreads = TKV_FLUSH_THREADS;
 
 
+// Four 8x8 16-bit matrices transposed from shared memory: lane L gives the
+// address of row L % 8 of matrix L / 8; register m of lane 4 g + t then holds
+// the elements of rows 2t and 2t + 1 (low, high half) at column g of matrix m.
+__device__ __forceinline__ void ldsm_x4_t(const void* p, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
 __device__ __forceinline__ float h2f(uint16_t h) {
   return __half2float(*reinterpret_cast<const __half*>(&h));
 }
@@ -198,11 +207,21 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
   auto code = [&](float x, float2 p) {
     return __float2uint_rn(__fmul_rn(__fadd_rn(x, p.x), p.y));
   };
-  auto page_base = [&](int pi) -> uint8_t* {
+  // the group's page blocks for this kv head, once (nullptr for a page id
+  // outside the pool, which is flagged above and skipped)
+  uint8_t* pbase[G / kPage];
+#pragma unroll
+  for (int pi = 0; pi < G / kPage; ++pi) {
     const int ph = S.phys[pi];
-    return (ph < 0 || ph >= a.num_pages)
-               ? nullptr
-               : a.pool + ((int64_t)ph * a.n_kv_heads + h) * a.page_bytes;
+    pbase[pi] = (ph < 0 || ph >= a.num_pages)
+                    ? nullptr
+                    : a.pool + ((int64_t)ph * a.n_kv_heads + h) * a.page_bytes;
+  }
+  auto page_base = [&](int pi) -> uint8_t* {
+    uint8_t* r = pbase[0];
+#pragma unroll
+    for (int i = 1; i < G / kPage; ++i) r = i == pi ? pbase[i] : r;
+    return r;
   };
   const __half2 pinf = __half2half2(__ushort_as_half(0x7c00u));
   const __half2 ninf = __half2half2(__ushort_as_half(0xfc00u));
@@ -269,9 +288,12 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
         const uint4 x = *reinterpret_cast<const uint4*>(&tile[t * TS + w * CPW + n8]);
         const uint16_t* hx = reinterpret_cast<const uint16_t*>(&x);
 #pragma unroll
-        for (int n = 0; n < 8; ++n) word |= code(h2f(hx[n]), p[n8 + n]) << (BITS * (n8 + n));
+        for (int n = 0; n < 8; ++n)  // disjoint bit fields: + packs like |, as one LEA
+          word += code(h2f(hx[n]), p[n8 + n]) << (BITS * (n8 + n));
       }
-      uint8_t* blk = page_base(t / kPage);
+      // t / 16 is k * TSTEP / 16 (t_first < TSTEP) when TSTEP divides 16
+      constexpr bool kStatic = TSTEP <= kPage && kPage % TSTEP == 0;
+      uint8_t* blk = page_base(kStatic ? k * TSTEP / kPage : t / kPage);
       if (blk) reinterpret_cast<uint32_t*>(blk + a.k_codes_off)[(t % kPage) * NWR + w] = word;
     }
     // key meta slices: page pi holds channels [pi * KMW, (pi + 1) * KMW)
@@ -324,9 +346,11 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
     for (int k = 0; k < ((G / kPage) * 32 + kFlushThreads - 1) / kFlushThreads; ++k) {
       const int pl = tid + k * kFlushThreads;
       if (pl >= (G / kPage) * 32) break;
-      const int pi = pl >> 5, l = pl & 31, g = l >> 2, tig = l & 3;
+      const int pi = pl >> 5, l = pl & 31, tig = l & 3;
       const int tb = pi * kPage + 2 * tig;  // token of (th, e) = (0, 0)
-      const uint16_t* base = &tile[tb * TS + g];
+      // ldmatrix.trans source row of this lane: matrix m = l / 8 covers
+      // channels + 8 (m & 1) and tokens + 8 (m >> 1) of an m-block
+      const uint16_t* lrow = &tile[(pi * kPage + 8 * (l >> 4) + (l & 7)) * TS + 8 * ((l >> 3) & 1)];
       // parameters of the lane's tokens (th, e), per value group
       float2 pv[2][2][NVG];
 #pragma unroll
@@ -343,20 +367,25 @@ __global__ void __launch_bounds__(kFlushThreads) flush_groups_kernel(AppendArgs 
         for (int u = 0; u < VW; ++u) {
           const int wv = q * VW + u;
           uint32_t wd = 0;
+          // register m of m-block mb: channel 16 mb + 8 rh + g, tokens
+          // 2 tig + 8 th (+1 in the high half), rh = m & 1, th = m >> 1
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int rh = k >> 1, th = k & 1;
-            const int r0 = 8 * th * TS, r1 = (8 * th + 1) * TS;  // rows of tokens (th, e = 0, 1)
-            if (BITS == 4) {
-              const int c = 16 * wv + 8 * rh;  // channel minus g (g < 8 stays in the group)
-              wd |= code(h2f(base[r0 + c]), pv[th][0][c / VG_CH]) << (4 * k);
-              wd |= code(h2f(base[r1 + c]), pv[th][1][c / VG_CH]) << (4 * (k + 4));
-            } else {
+          for (int mbi = 0; mbi < (BITS == 4 ? 1 : 2); ++mbi) {
+            const int mb = BITS == 4 ? wv : 2 * wv + mbi;
+            uint32_t r[4];
+            ldsm_x4_t(lrow + 16 * mb, r);
 #pragma unroll
-              for (int mbi = 0; mbi < 2; ++mbi) {
-                const int c = 16 * (2 * wv + mbi) + 8 * rh;
-                wd |= code(h2f(base[r0 + c]), pv[th][0][c / VG_CH]) << (2 * (4 * mbi + k));
-                wd |= code(h2f(base[r1 + c]), pv[th][1][c / VG_CH]) << (2 * (4 * mbi + k + 8));
+            for (int m = 0; m < 4; ++m) {
+              const int rh = m & 1, th = m >> 1, k = 2 * rh + th;
+              const int vg = (16 * mb + 8 * rh) / VG_CH;
+              const uint32_t c0 = code(h2f(static_cast<uint16_t>(r[m] & 0xffffu)), pv[th][0][vg]);
+              const uint32_t c1 = code(h2f(static_cast<uint16_t>(r[m] >> 16)), pv[th][1][vg]);
+              if (BITS == 4) {  // nibbles k (token e = 0) and k + 4 (e = 1)
+                wd += c0 << (4 * k);
+                wd += c1 << (4 * (k + 4));
+              } else {          // 2-bit fields 4 mbi + k and 4 mbi + k + 8
+                wd += c0 << (2 * (4 * mbi + k));
+                wd += c1 << (2 * (4 * mbi + k + 8));
               }
             }
           }
