@@ -64,6 +64,13 @@ __device__ __forceinline__ void ldsm_x4_t(const void* p, uint32_t (&r)[4]) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(smem_u32(p)));
 }
+// The same without the transpose: register m of lane 4 g + t holds row g,
+// columns 2t and 2t + 1 (low, high half) of matrix m.
+__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
 
 __device__ __forceinline__ float h2f(uint16_t h) {
   return __half2float(*reinterpret_cast<const __half*>(&h));
@@ -456,7 +463,10 @@ __global__ void __launch_bounds__(kResThreads) residual_write_kernel(AppendArgs 
     }
     return;
   }
-  // full chunk: stage the 16 input rows (16-byte aligned by the entry point)
+  // full chunk: stage the 16 input rows (16-byte aligned by the entry point);
+  // unrolled, so every thread's loads are in flight together
+  static_assert((2 * kPage * VPR) % kResThreads == 0, "whole staging rounds");
+#pragma unroll
   for (int i = tid; i < 2 * kPage * VPR; i += kResThreads) {
     const int kv = i / (kPage * VPR), r = i % (kPage * VPR), t = r / VPR, v = r % VPR;
     uint4 x = *reinterpret_cast<const uint4*>(in_elem(kv ? a.v_new : a.k_new, lo + t, v * 8));
@@ -475,19 +485,21 @@ __global__ void __launch_bounds__(kResThreads) residual_write_kernel(AppendArgs 
   // vector v of a block = (bi = v / 32, lane l = 4 g + tig), halves 2 r + e:
   //   K: (t = g + 8 (r & 1), c = 16 bi + 2 tig + 8 (r >> 1) + e)
   //   V: (t = 8 (r >> 1) + 2 tig + e, c = 16 bi + g + 8 (r & 1))
+  // i.e. the mma A fragment of the 16 x 16 block bi of K [token][channel]
+  // (ldmatrix, matrix m: tokens + 8 (m & 1), channels + 8 (m >> 1)) and of
+  // V^T (ldmatrix.trans, matrix m: channels + 8 (m & 1), tokens + 8 (m >> 1)).
+  // A warp's 32 consecutive vectors share kv and bi.
+#pragma unroll
   for (int i = tid; i < 2 * kPage * VPR; i += kResThreads) {
     const int kv = i / (kPage * VPR), v = i % (kPage * VPR);
-    const int bi = v >> 5, l = v & 31, g = l >> 2, tig = l & 3;
-    uint16_t x[8];
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int t = kv ? 8 * (r >> 1) + 2 * tig + e : g + 8 * (r & 1);
-        const int c = 16 * bi + (kv ? g + 8 * (r & 1) : 2 * tig + 8 * (r >> 1) + e);
-        x[2 * r + e] = st[kv][t * TS + c];
-      }
-    reinterpret_cast<uint4*>(kv ? vc : kc)[v] = *reinterpret_cast<const uint4*>(x);
+    const int bi = v >> 5, l = v & 31, m = l >> 3;
+    uint32_t x[4];
+    if (kv == 0) {
+      ldsm_x4(&st[0][(8 * (m & 1) + (l & 7)) * TS + 16 * bi + 8 * (m >> 1)], x);
+    } else {
+      ldsm_x4_t(&st[1][(8 * (m >> 1) + (l & 7)) * TS + 16 * bi + 8 * (m & 1)], x);
+    }
+    reinterpret_cast<uint4*>(kv ? vc : kc)[v] = make_uint4(x[0], x[1], x[2], x[3]);
   }
 }
 
