@@ -97,8 +97,11 @@ typedef enum tkv_status {
   TKV_BACKEND_ERROR = 5,
 } tkv_status_t;
 
-/* Element types: the values of truellm::DataType (include/truellm/types.h:47-53). */
-typedef enum tkv_dtype { TKV_F32 = 0, TKV_F16 = 1, TKV_BF16 = 2 } tkv_dtype_t;
+/* Element types: the values of truellm::DataType (include/truellm/types.h:47-53).
+ * TKV_I32 only describes index views (block tables, lengths) in the C++
+ * adapter's tensor-view overloads; no entry point takes it as a q, K/V or
+ * output type. */
+typedef enum tkv_dtype { TKV_F32 = 0, TKV_F16 = 1, TKV_BF16 = 2, TKV_I32 = 3 } tkv_dtype_t;
 
 /* Bits set in the device error word (err_flag arguments) by bounds checks. */
 #define TKV_ERR_BAD_PAGE 0x1    /* block-table entry outside [0, num_pages)    */

@@ -181,7 +181,58 @@ class PagedKiviCache {
              "PagedKiviCache::decode");
   }
 
+  // The same two slots with the engine's tensor views, for an engine that
+  // keeps its call sites shaped like cuda_engine.cpp:48-62, where
+  // paged_attention_v1/v2 and reshape_and_cache take truellm::TrueBuffer
+  // (include/truellm/types.h:69-77).  Buf is any view with TrueBuffer's
+  // fields (data, dtype, ndim, shape[4]); dtype holds truellm::DataType,
+  // whose F32 / F16 / BF16 / I32 values equal TKV_F32 / TKV_F16 / TKV_BF16 /
+  // TKV_I32.  Shapes are read from the views:
+  //   decode: out, q [num_seqs, num_q_heads, head_dim]; block_tables
+  //           [num_seqs, max_blocks_per_seq] int32; seq_lens [num_seqs] int32.
+  //   append: key, value [total_new_tokens, n_kv_heads, head_dim]; cu_new
+  //           [num_seqs + 1] int32; seq_lens_old [num_seqs] int32;
+  //           block_tables [num_seqs, max_blocks_per_seq] int32.
+  // A view of the wrong element type or rank throws, as a wrong argument to
+  // the pointer forms does.
+  template <class Buf>
+  void decode(Buf& out, const Buf& q, const Buf& block_tables, const Buf& seq_lens, float scale,
+              int max_context_len, void* workspace, size_t workspace_bytes, int* err_flag,
+              cudaStream_t stream, const int32_t* seq_slots = nullptr) const {
+    check_view(q, 3, -1, "decode: q");
+    check_view(out, 3, -1, "decode: out");
+    check_view(block_tables, 2, TKV_I32, "decode: block_tables");
+    check_view(seq_lens, 1, TKV_I32, "decode: seq_lens");
+    decode(q.data, static_cast<int>(q.dtype), out.data, static_cast<int>(out.dtype),
+           static_cast<const int32_t*>(block_tables.data), static_cast<int>(block_tables.shape[1]),
+           static_cast<const int32_t*>(seq_lens.data), seq_slots,
+           static_cast<int>(q.shape[0]), static_cast<int>(q.shape[1]), scale, max_context_len,
+           workspace, workspace_bytes, err_flag, stream);
+  }
+  template <class Buf>
+  void append(const Buf& key, const Buf& value, const Buf& cu_new, const Buf& seq_lens_old,
+              const Buf& block_tables, int max_new_tokens, int* err_flag, cudaStream_t stream,
+              const int32_t* seq_slots = nullptr) const {
+    check_view(key, 3, -1, "append: key");
+    check_view(value, 3, static_cast<int>(key.dtype), "append: value");
+    check_view(cu_new, 1, TKV_I32, "append: cu_new");
+    check_view(seq_lens_old, 1, TKV_I32, "append: seq_lens_old");
+    check_view(block_tables, 2, TKV_I32, "append: block_tables");
+    append(key.data, value.data, static_cast<int>(key.dtype),
+           static_cast<const int32_t*>(cu_new.data),
+           static_cast<const int32_t*>(seq_lens_old.data),
+           static_cast<const int32_t*>(block_tables.data), static_cast<int>(block_tables.shape[1]),
+           seq_slots, static_cast<int>(seq_lens_old.shape[0]), static_cast<int>(key.shape[0]),
+           max_new_tokens, err_flag, stream);
+  }
+
  private:
+  template <class Buf>
+  static void check_view(const Buf& b, int ndim, int dtype, const char* what) {
+    if (b.data == nullptr || b.ndim != ndim ||
+        (dtype >= 0 && static_cast<int>(b.dtype) != dtype))
+      throw_on(TKV_INVALID_ARGUMENT, what);
+  }
   tkv_cache_t c_{};
 };
 

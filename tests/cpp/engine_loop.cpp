@@ -22,6 +22,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -64,6 +65,36 @@ T* device_copy(const std::vector<T>& h) {
   cuda_ok(cudaMalloc(&d, h.size() * sizeof(T)), "cudaMalloc");
   cuda_ok(cudaMemcpy(d, h.data(), h.size() * sizeof(T), cudaMemcpyHostToDevice), "upload");
   return d;
+}
+
+// a view with the fields of truellm::TrueBuffer (include/truellm/types.h:69-77)
+// and truellm::DataType's values, for the adapter's tensor-view overloads
+enum class DataType : uint8_t { F32 = 0, F16 = 1, BF16 = 2, I32 = 3 };
+struct TrueBuffer {
+  void* data;
+  std::size_t size_bytes;
+  DataType dtype;
+  int32_t device_id;
+  int32_t ndim;
+  int64_t shape[4];
+  int64_t stride[4];
+};
+TrueBuffer view(const void* p, DataType t, std::size_t elem, std::initializer_list<int64_t> shape) {
+  TrueBuffer b{const_cast<void*>(p), 0, t, 0, static_cast<int32_t>(shape.size()), {1, 1, 1, 1},
+               {0, 0, 0, 0}};
+  std::size_t n = 1;
+  int i = 0;
+  for (int64_t d : shape) {
+    b.shape[i++] = d;
+    n *= static_cast<std::size_t>(d);
+  }
+  int64_t st = 1;
+  for (int k = b.ndim - 1; k >= 0; --k) {
+    b.stride[k] = st;
+    st *= b.shape[k];
+  }
+  b.size_bytes = n * elem;
+  return b;
 }
 
 // stand-ins with the field names of truellm::CompressionConfig (config_schema.h:121-159)
@@ -193,11 +224,24 @@ int main(int argc, char** argv) {
           throw std::runtime_error("extend_sequence");
       upload_tables(t + 1);
       for (int l = 0; l < n_layers; ++l) {
-        caches[l].append(d_kd + (l * T + t) * B * tok, d_vd + (l * T + t) * B * tok, TKV_F16,
-                         d_cu_one, d_lens_old, d_bt, max_blocks, d_rows, B, B, 1, d_err, s);
-        caches[l].decode(d_qd + (l * T + t) * B * row, TKV_F16, d_out_decode + l * B * row,
-                         TKV_F32, d_bt, max_blocks, d_lens, d_rows, B, Hq, scale, max_len + T,
-                         d_ws, ws_bytes, d_err, s);
+        if (l == 0) {  // pointer forms
+          caches[l].append(d_kd + (l * T + t) * B * tok, d_vd + (l * T + t) * B * tok, TKV_F16,
+                           d_cu_one, d_lens_old, d_bt, max_blocks, d_rows, B, B, 1, d_err, s);
+          caches[l].decode(d_qd + (l * T + t) * B * row, TKV_F16, d_out_decode + l * B * row,
+                           TKV_F32, d_bt, max_blocks, d_lens, d_rows, B, Hq, scale, max_len + T,
+                           d_ws, ws_bytes, d_err, s);
+        } else {  // tensor views shaped like the reference's call sites
+          const TrueBuffer k = view(d_kd + (l * T + t) * B * tok, DataType::F16, 2, {B, Hkv, D});
+          const TrueBuffer v = view(d_vd + (l * T + t) * B * tok, DataType::F16, 2, {B, Hkv, D});
+          const TrueBuffer cu = view(d_cu_one, DataType::I32, 4, {B + 1});
+          const TrueBuffer lo = view(d_lens_old, DataType::I32, 4, {B});
+          const TrueBuffer bt = view(d_bt, DataType::I32, 4, {B, max_blocks});
+          const TrueBuffer ln = view(d_lens, DataType::I32, 4, {B});
+          const TrueBuffer qv = view(d_qd + (l * T + t) * B * row, DataType::F16, 2, {B, Hq, D});
+          TrueBuffer ov = view(d_out_decode + l * B * row, DataType::F32, 4, {B, Hq, D});
+          caches[l].append(k, v, cu, lo, bt, 1, d_err, s, d_rows);
+          caches[l].decode(ov, qv, bt, ln, scale, max_len + T, d_ws, ws_bytes, d_err, s, d_rows);
+        }
       }
     }
     // ---- KvCompressionPass on a separate K/V buffer ----

@@ -2,8 +2,9 @@
 the C ABI and keeps the reference's host-side behaviour, checked without a
 GPU: KvCompressionPass maps the config like kv_compression_pass.cpp:29-67 and
 disables itself on unsupported parameters, the reference-format calls are
-silent no-ops on unsupported parameters (kivi_cache.cu:219-220), and a bad
-paged call throws instead of returning an unchecked status.
+silent no-ops on unsupported parameters (kivi_cache.cu:219-220), a bad paged
+call throws instead of returning an unchecked status, and the tensor-view
+(TrueBuffer-shaped) overloads reject views of the wrong rank or type.
 """
 import os
 import shutil
@@ -27,6 +28,12 @@ namespace kb = truellm::kivi_b200;
 struct KiviConfig { bool enabled = false; int bits = 8; int residual_length = 128; };
 struct CompressionConfig { bool enabled = false; KiviConfig kv_kivi; };
 struct CudaAllocator {};
+// a view with the fields of truellm::TrueBuffer (include/truellm/types.h:69-77)
+enum class DataType : uint8_t { F32 = 0, F16 = 1, BF16 = 2, I32 = 3 };
+struct TrueBuffer {
+  void* data; std::size_t size_bytes; DataType dtype; int32_t device_id; int32_t ndim;
+  int64_t shape[4]; int64_t stride[4];
+};
 
 #define CHECK(x) do { if (!(x)) { std::printf("FAIL %s:%d %s\n", __FILE__, __LINE__, #x); return 1; } } while (0)
 
@@ -78,6 +85,52 @@ int main() {
     threw = true;
   }
   CHECK(threw);
+  // tensor-view overloads (the reference's TrueBuffer call sites): a view of
+  // the wrong rank or element type is rejected before any launch
+  {
+    int32_t idx[8] = {0};
+    uint16_t qh[8] = {0};
+    TrueBuffer q{qh, 16, DataType::F16, 0, 3, {1, 32, 128, 1}, {0, 0, 0, 0}};
+    TrueBuffer out = q;
+    TrueBuffer bt2{idx, 32, DataType::I32, 0, 2, {1, 8, 1, 1}, {0, 0, 0, 0}};
+    TrueBuffer lens1{idx, 4, DataType::I32, 0, 1, {1, 1, 1, 1}, {0, 0, 0, 0}};
+    TrueBuffer bad_bt = bt2;
+    bad_bt.dtype = DataType::F16;
+    threw = false;
+    try {
+      cache.decode(out, q, bad_bt, lens1, 0.1f, 16, nullptr, 0, nullptr, nullptr);
+    } catch (const std::invalid_argument&) {
+      threw = true;
+    }
+    CHECK(threw);
+    TrueBuffer flat_q = q;
+    flat_q.ndim = 2;
+    threw = false;
+    try {
+      cache.decode(out, flat_q, bt2, lens1, 0.1f, 16, nullptr, 0, nullptr, nullptr);
+    } catch (const std::invalid_argument&) {
+      threw = true;
+    }
+    CHECK(threw);
+    threw = false;
+    try {  // well-formed views, null pool: rejected by the C ABI before any launch
+      cache.decode(out, q, bt2, lens1, 0.1f, 16, nullptr, 0, nullptr, nullptr);
+    } catch (const std::invalid_argument&) {
+      threw = true;
+    }
+    CHECK(threw);
+    TrueBuffer kv{qh, 16, DataType::F16, 0, 3, {1, 8, 128, 1}, {0, 0, 0, 0}};
+    TrueBuffer vv = kv;
+    vv.dtype = DataType::BF16;  // value of another type than key
+    TrueBuffer cu{idx, 8, DataType::I32, 0, 1, {2, 1, 1, 1}, {0, 0, 0, 0}};
+    threw = false;
+    try {
+      cache.append(kv, vv, cu, lens1, bt2, 1, nullptr, nullptr);
+    } catch (const std::invalid_argument&) {
+      threw = true;
+    }
+    CHECK(threw);
+  }
   threw = false;
   try {
     kb::PagedKiviCache::format(96, 128, 128, 4, 8);
