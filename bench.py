@@ -428,24 +428,30 @@ def run_kivi(args):
     side = [torch.cuda.Stream() for _ in parts[1:]]
 
     def run_parts(fn):
+        cur = torch.cuda.current_stream()  # the capture stream while a graph is captured
         if not side:
-            fn(parts[0], stream)
+            fn(parts[0], cur)
             return
         for s_ in side:
-            s_.wait_stream(stream)
-        fn(parts[0], stream)
+            s_.wait_stream(cur)
+        fn(parts[0], cur)
         for p, s_ in zip(parts[1:], side):
             with torch.cuda.stream(s_):
                 fn(p, s_)
         for s_ in side:
-            stream.wait_stream(s_)
+            cur.wait_stream(s_)
+
+    step_graph = None
 
     def step(ev=None):
         # one decode step: one decode launch per part (split + fused merge); the
         # token-split layout adds the all-gather of partials and the merge
         if ev is not None:
             ev[0].record(stream)
-        run_parts(lambda p, s_: decode(p, p.q, p.lens, s_))
+        if step_graph is not None:
+            step_graph.replay()
+        else:
+            run_parts(lambda p, s_: decode(p, p.q, p.lens, s_))
         if ev is not None:
             ev[1].record(stream)
 
@@ -456,6 +462,24 @@ def run_kivi(args):
 
     for _ in range(args.warmup):
         step()
+    # Above one GPU a rank's step is 20-90 us of GPU work, and a config-5 step
+    # (two calls on two streams) costs ~50 us of Python to enqueue while every
+    # rank's loop shares the host's cores: the step's launches are captured
+    # once in a CUDA graph and replayed, so the host's launch rate does not
+    # set the measured step.  The end-to-end leg below keeps the direct calls.
+    if dec is None and (world > 1 or len(parts) > 1):
+        torch.cuda.synchronize()
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                run_parts(lambda p, s_: decode(p, p.q, p.lens, s_))
+            step_graph = g
+            for _ in range(args.warmup):
+                step()
+        except Exception as e:  # capture not supported here: direct calls
+            print(f"rank {rank}: CUDA graph capture failed ({e!r}); direct calls",
+                  file=sys.stderr)
+            step_graph = None
     barrier()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
@@ -606,6 +630,8 @@ def run_kivi(args):
             "config": {"workload": workload_desc(args.workload, w),
                        "global_batch": total_seqs, "mean_context": float(w.lengths.mean()),
                        "parallelism": layout, "rank0_parts": [p.label for p in parts],
+                       "launch": ("one CUDA graph per step" if graph is not None or
+                                  step_graph is not None else "direct C calls"),
                        "l2": "inputs larger than L2 (cache %.0f MB per rank)" % (alg_bytes / 1e6)},
             "gpu_launches": n_launch * args.steps,
             "e2e": {"value": total_seqs / t_e2e, "unit": UNIT, "h2d_bytes_per_step": h2d,
@@ -625,6 +651,7 @@ def run_kivi(args):
             "clocks": clocks,
         }
         print(json.dumps(line))
+    step_graph = None
     if graph is not None:  # a graph holding collectives goes before the group
         torch.cuda.synchronize()
         del graph
