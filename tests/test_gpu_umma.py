@@ -2,7 +2,8 @@
 (tests/cuda/umma_selftest.cu, compiled here with nvcc for sm_100a) stages
 16-bit operands into the K-major no-swizzle layout, runs two accumulating
 rounds of eight K = 16 `tcgen05.mma` into tensor memory and reads D back with
-`tcgen05.ld`; D must equal A0 B0^T + A1 B1^T computed by torch in fp32.
+`tcgen05.ld`; D must equal A0 B0^T + A1 B1^T computed by torch in fp32, with A
+read from shared memory or (a_tmem) from tensor memory.
 """
 import ctypes as C
 import os
@@ -28,20 +29,23 @@ def selftest():
                    check=True)
     lib = C.CDLL(str(out))
     lib.umma_selftest.restype = C.c_int
-    lib.umma_selftest.argtypes = [C.c_void_p] * 5 + [C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+    lib.umma_selftest.argtypes = [C.c_void_p] * 5 + [C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                                      C.c_void_p]
     return lib
 
 
+@pytest.mark.parametrize("a_tmem", [0, 1])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("N", [64, 128, 256])
-def test_tcgen05_gemm_matches_torch(selftest, cuda, dtype, N):
+def test_tcgen05_gemm_matches_torch(selftest, cuda, dtype, N, a_tmem):
     g = torch.Generator(device=cuda).manual_seed(N)
     a0, a1 = (torch.randn((128, 128), generator=g, device=cuda).to(dtype) for _ in range(2))
     b0, b1 = (torch.randn((N, 128), generator=g, device=cuda).to(dtype) for _ in range(2))
     d = torch.full((128, N), float("nan"), device=cuda)
     err = torch.zeros(1, dtype=torch.int32, device=cuda)
     st = selftest.umma_selftest(a0.data_ptr(), b0.data_ptr(), a1.data_ptr(), b1.data_ptr(),
-                                d.data_ptr(), N, int(dtype == torch.bfloat16), err.data_ptr(),
+                                d.data_ptr(), N, int(dtype == torch.bfloat16), a_tmem,
+                                err.data_ptr(),
                                 torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert st == 0 and int(err.item()) == 0

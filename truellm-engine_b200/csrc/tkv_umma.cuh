@@ -61,6 +61,19 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T, issued by one thread: A (M = 128 rows x
+// K = 16 16-bit elements) sits in tensor memory, row i in lane i, elements
+// 2c and 2c + 1 of the row in column a_tmem + c (low and high half).
+__device__ __forceinline__ void mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
 // Arrive on the mbarrier once every MMA this thread issued before has
 // completed (their shared-memory reads included).
 __device__ __forceinline__ void commit(uint64_t* bar) {
