@@ -79,14 +79,15 @@ __device__ __forceinline__ constexpr int kchan_at(int p) {
 // into tensor memory; each thread then owns one query row: it loads the row's
 // 64 scores with tcgen05.ld, masks them causally, runs the online softmax
 // (exp2 domain, lazy rescale: when a warp's running maxima move, its rows of O
-// are rescaled in tensor memory) and stores the row's weights P as f16 into
-// its warpgroup's P tile; one thread of the warpgroup issues O += P V (4 MMAs,
-// N = D) into tensor memory.  Software pipeline: while tile j's softmax runs,
+// are rescaled in tensor memory) and writes the row's weights P as f16 pairs
+// into tensor memory over the scores it has read (tcgen05.st, 32 columns);
+// O += P V (4 MMAs, N = D) then takes its A operand from tensor memory.  Software pipeline: while tile j's softmax runs,
 // S of tile j+1 is on the tensor cores (its K already dequantised), and
 // O += P V of tile j runs while tile j+1's successor is dequantised; the next
 // tile's code words are loaded into registers one tile ahead.  Tensor memory
-// per warpgroup (256 columns): S of even and odd tiles in [0, 128), O in
-// [128, 128 + D).
+// per warpgroup (256 columns): S of even and odd tiles in [0, 128) (P_j over
+// the first 32 columns of S_j's buffer), O in [128, 128 + D).  S_{j+2} reuses
+// S_j's buffer only after O += P_j V_j of both warpgroups is done.
 // ---------------------------------------------------------------------------
 // Lazy rescale of the tcgen05 prefill: a row's running maximum (log2 units)
 // moves only when a tile's maximum exceeds it by more than this, so the O
@@ -118,16 +119,14 @@ __device__ __forceinline__ bool bar_and(int id, int nthreads, bool v) {
 
 template <int D>
 struct UmmaSmem {
-  // K double-, V triple- and P double-buffered: tile j+1 is dequantised and
-  // its S issued while tile j's softmax runs, and O += P_j V_j runs while
-  // tile j+2 is dequantised
+  // K and V triple-buffered: the producers dequantise up to two tiles ahead
+  // of the softmax (P lives in tensor memory)
   static constexpr int K_BYTES = kUmmaTN * D * 2, V_BYTES = D * kUmmaTN * 2;
-  static constexpr int P_BYTES = kUmmaRows * kUmmaTN * 2, Q_BYTES = kUmmaRows * D * 2;
+  static constexpr int Q_BYTES = kUmmaRows * D * 2;
   static constexpr int Q_OFF = 0;  // one Q operand per warpgroup
   static constexpr int K_OFF = Q_OFF + kUmmaWG * Q_BYTES;
-  static constexpr int V_OFF = K_OFF + 2 * K_BYTES;
-  static constexpr int P_OFF = V_OFF + 3 * V_BYTES;  // [warpgroup][2]
-  static constexpr int BAR_OFF = P_OFF + 2 * kUmmaWG * P_BYTES;
+  static constexpr int V_OFF = K_OFF + 3 * K_BYTES;
+  static constexpr int BAR_OFF = V_OFF + 3 * V_BYTES;
   static constexpr int BYTES = BAR_OFF + 256;
   // tensor memory: per warpgroup 256 columns, S of even and odd tiles, then O
   static constexpr uint32_t TWG = 256, TCOLS = 512;
@@ -160,22 +159,21 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
   uint8_t* const Qs = smem + SM::Q_OFF;
   uint8_t* const Ks = smem + SM::K_OFF;
   uint8_t* const Vs = smem + SM::V_OFF;
-  uint8_t* const Ps = smem + SM::P_OFF;
   // Pipeline barriers (tile j uses parity class j % 2 or j % 3, phase j / 2 or j / 3):
   //   sdone[b]     S_j = Q K_j^T of both softmax warpgroups done (commit)
   //   odone[w][b]  warpgroup w's O += P_j V_j done (commit)
   //   vfree[v]     both warpgroups' O += P_j V_j done (2 commits)
-  //   sfree[b]     every softmax thread has read its row of S_j (256 arrivals)
-  //   pready[w][b] warpgroup w's P_j stored (128 arrivals)
+  //   pready[w][b] warpgroup w's P_j written to tensor memory (128 arrivals)
   //   tready[v]    K_j and V_j stored (256 producer arrivals)
+  //   kfree[v]     S_j done: K buffer j % 3 may be overwritten (commit)
   uint64_t* const bars = reinterpret_cast<uint64_t*>(smem + SM::BAR_OFF);
   uint64_t* const sdone = bars;
   uint64_t* const odone = bars + 2;   // [w * 2 + b]
   uint64_t* const vfree = bars + 6;
-  uint64_t* const sfree = bars + 9;
-  uint64_t* const pready = bars + 11;  // [w * 2 + b]
-  uint64_t* const tready = bars + 15;
-  uint32_t* const tslot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* const pready = bars + 9;  // [w * 2 + b]
+  uint64_t* const tready = bars + 13;
+  uint64_t* const kfree = bars + 16;
+  uint32_t* const tslot = reinterpret_cast<uint32_t*>(bars + 19);
   const int ctid = threadIdx.x, warp = ctid >> 5;
   const int wg = ctid >> 7, wt = ctid & 127;  // warpgroup, row in the warpgroup (softmax)
   const bool producer = ctid >= kUmmaSoftmax && ctid < kUmmaSoftmax + kUmmaProducers;
@@ -231,9 +229,9 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
   if (ctid == 0) {
     for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);                 // sdone, odone
     for (int i = 6; i < 9; ++i) mbar_init(&bars[i], 2);                 // vfree
-    for (int i = 9; i < 11; ++i) mbar_init(&bars[i], kUmmaSoftmax);     // sfree
-    for (int i = 11; i < 15; ++i) mbar_init(&bars[i], kUmmaRows);       // pready
-    for (int i = 15; i < 18; ++i) mbar_init(&bars[i], kUmmaProducers);  // tready
+    for (int i = 9; i < 13; ++i) mbar_init(&bars[i], kUmmaRows);        // pready
+    for (int i = 13; i < 16; ++i) mbar_init(&bars[i], kUmmaProducers);  // tready
+    for (int i = 16; i < 19; ++i) mbar_init(&bars[i], 1);               // kfree
     fence_mbar_init();
   }
   if (ctid < kUmmaSoftmax) {
@@ -500,20 +498,21 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
 
     if (n_tiles > 0) load_tile(0);
     for (int jt = 0; jt < n_tiles; ++jt) {
-      // K buffer jt % 2 once S_{jt-2} has read it; V buffer jt % 3 once both
+      // K buffer jt % 3 once S_{jt-3} has read it; V buffer jt % 3 once both
       // warpgroups' O += P_{jt-3} V_{jt-3} have
-      if (jt >= 2 && !mbar_wait(&sdone[jt & 1], ((jt - 2) >> 1) & 1, a.err)) break;
+      if (jt >= 3 && !mbar_wait(&kfree[jt % 3], ((jt - 3) / 3) & 1, a.err)) break;
       if (jt >= 3 && !mbar_wait(&vfree[jt % 3], ((jt - 3) / 3) & 1, a.err)) break;
       umma::fence_after_sync();
-      store_tile(jt, Ks + (jt & 1) * SM::K_BYTES, Vs + (jt % 3) * SM::V_BYTES);
+      store_tile(jt, Ks + (jt % 3) * SM::K_BYTES, Vs + (jt % 3) * SM::V_BYTES);
       if (jt + 1 < n_tiles) load_tile(jt + 1);  // in flight while the tensor cores run
       umma::fence_smem_to_async();
       mbar_arrive(&tready[jt % 3]);
     }
   } else if (mma_warp) {
     // ======================= the MMA warp (lane 0 issues) =======================
-    // per tile j: S_{j+1} (as soon as K_{j+1} is stored and both warpgroups
-    // have read S_{j-1}), then O += P_j V_j of each warpgroup as its P_j lands
+    // per tile j: S_{j+1} (as soon as K_{j+1} is stored and O += P_{j-1}
+    // V_{j-1} of both warpgroups, which reads P_{j-1} from S_{j+1}'s buffer,
+    // is done), then O += P_j V_j of each warpgroup as its P_j lands
     if ((ctid & 31) == 0 && n_tiles > 0) {
       bool mok = true;
       int last_s = -1, last_pv = -1;
@@ -524,13 +523,11 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
       const uint64_t dq0 = umma::smem_desc(smem_u32(Qs), 128, 16 * D);
       const uint64_t dq1 = umma::smem_desc(smem_u32(Qs + SM::Q_BYTES), 128, 16 * D);
       const uint64_t dk0 = umma::smem_desc(smem_u32(Ks), 128, 16 * D);
-      const uint64_t dk1 = umma::smem_desc(smem_u32(Ks + SM::K_BYTES), 128, 16 * D);
       const uint64_t dv0 = umma::smem_desc(smem_u32(Vs), 128, 16 * TN);
-      const uint64_t dp0 = umma::smem_desc(smem_u32(Ps), 128, 16 * TN);
-      constexpr uint64_t kVStep = SM::V_BYTES >> 4, kPStep = SM::P_BYTES >> 4;
+      constexpr uint64_t kKStep = SM::K_BYTES >> 4, kVStep = SM::V_BYTES >> 4;
       auto issue_s = [&](int j) {
         umma::fence_after_sync();
-        const uint64_t dk = (j & 1) ? dk1 : dk0;
+        const uint64_t dk = dk0 + (j % 3) * kKStep;
         const uint32_t t0 = tmem + (j & 1) * TN;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
@@ -539,6 +536,7 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
         for (int kk = 0; kk < D / 16; ++kk)
           umma::mma_f16(t0 + SM::TWG, dq1 + 16 * kk, dk + 16 * kk, idS, kk > 0);
         umma::commit(&sdone[j & 1]);
+        umma::commit(&kfree[j % 3]);
         last_s = j;
       };
       mok = mbar_wait(&tready[0], 0, a.err);
@@ -546,7 +544,8 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
       for (int j = 0; mok && j < n_tiles; ++j) {
         if (j + 1 < n_tiles) {
           mok = mbar_wait(&tready[(j + 1) % 3], ((j + 1) / 3) & 1, a.err) &&
-                (j < 1 || mbar_wait(&sfree[(j + 1) & 1], ((j - 1) >> 1) & 1, a.err));
+                (j < 1 || (mbar_wait(&odone[(j - 1) & 1], ((j - 1) >> 1) & 1, a.err) &&
+                           mbar_wait(&odone[2 + ((j - 1) & 1)], ((j - 1) >> 1) & 1, a.err)));
           if (!mok) break;
           issue_s(j + 1);
         }
@@ -558,11 +557,12 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
             break;
           }
           umma::fence_after_sync();
-          const uint64_t dp = dp0 + (2 * w + (j & 1)) * kPStep;
+          // P_j: 8 columns of f16 pairs per 16 tokens, over S_j's buffer
+          const uint32_t tp = tmem + w * SM::TWG + (j & 1) * TN;
 #pragma unroll
           for (int kk = 0; kk < TN / 16; ++kk)
-            umma::mma_f16(tmem + w * SM::TWG + 2 * TN, dp + 16 * kk, dv + 16 * kk, idO,
-                          j > 0 || kk > 0);
+            umma::mma_f16_ta(tmem + w * SM::TWG + 2 * TN, tp + 8 * kk, dv + 16 * kk, idO,
+                             j > 0 || kk > 0);
           umma::commit(&odone[2 * w + (j & 1)]);
           umma::commit(&vfree[j % 3]);
           last_pv = j;
@@ -579,7 +579,6 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
     // ======================= softmax warpgroups =======================
     const uint32_t tS = tmem + wg * SM::TWG, tO = tS + 2 * TN;  // this warpgroup's columns
     const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-    const uint32_t p_off = umma::umma_off(wt, 0, TN);
     const float alpha = a.alpha;
     float m_run = -INFINITY, l_run = 0.f;
     // warpgroup wg's O += P_j V_j (and its MMAs before) done
@@ -637,35 +636,32 @@ __global__ void __launch_bounds__(kUmmaCtaThreads, 1) prefill_umma_kernel(Prefil
           umma::wait_st();
         }
       }
-      if (jt >= 2) wait_o(jt - 2);  // the P buffer b, read by O += P_{jt-2} V_{jt-2}
+      // P_jt over the scores already read: tokens 32 hf .. 32 hf + 31 as 16
+      // columns of f16 pairs at column 16 hf of S_jt's buffer (O += P_{jt-2}
+      // V_{jt-2}, the buffer's last reader, finished before S_jt was issued)
       const float nb = m_run == -INFINITY ? 0.f : -m_run;
-      uint8_t* const pd = Ps + (2 * wg + b) * SM::P_BYTES;
       float2 sum2 = make_float2(0.f, 0.f);
       const float2 al2 = make_float2(alpha, alpha), nb2 = make_float2(nb, nb);
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         float x[32];
         load_half(hf, x);
-        if (hf == 1) {
-          umma::fence_before_sync();
-          mbar_arrive(&sfree[b]);  // this row of S_jt is no longer read
-        }
 #pragma unroll
-        for (int c8 = 0; c8 < 32; c8 += 8) {
-          uint32_t w[4];
+        for (int q = 0; q < 2; ++q) {
+          uint32_t pw[8];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 y = ffma2(make_float2(x[c8 + 2 * e], x[c8 + 2 * e + 1]), al2, nb2);
+          for (int e = 0; e < 8; ++e) {
+            const int c = 16 * q + 2 * e;
+            const float2 y = ffma2(make_float2(x[c], x[c + 1]), al2, nb2);
             const float2 pp = make_float2(fast_exp2(y.x), fast_exp2(y.y));
             sum2 = fadd2(sum2, pp);
-            w[e] = pack_h2(pp.x, pp.y);
+            pw[e] = pack_h2(pp.x, pp.y);
           }
-          *reinterpret_cast<uint4*>(pd + p_off + (32 * hf + c8) * 16) =
-              make_uint4(w[0], w[1], w[2], w[3]);
+          umma::st8(tSj + lane_base + 16 * hf + 8 * q, pw);
         }
       }
       l_run += sum2.x + sum2.y;
-      umma::fence_smem_to_async();
+      umma::wait_st();
       umma::fence_before_sync();
       mbar_arrive(&pready[2 * wg + b]);  // P_jt (and any O rescale) in place
       if (!ok) break;

@@ -171,6 +171,13 @@ __device__ __forceinline__ void st16(uint32_t taddr, const float (&v)[16]) {
       "r"(__float_as_uint(v[15]))
       : "memory");
 }
+__device__ __forceinline__ void st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+      : "memory");
+}
 __device__ __forceinline__ void wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
