@@ -1,6 +1,7 @@
 """Config switches of the path (CPU): the reference's keys and defaults, the
-kv-cache type validation extended with kivi4/kivi2, and the KvCompressionPass
-mirror's enable rule (config_schema.h:46-50,121-129; config.cpp:78-86,215-224,
+kv-cache type validation extended with kivi4/kivi2, the [inference.cuda_engine]
+keys (use_megakernel included), and the KvCompressionPass mirror's enable rule
+(config_schema.h:46-50,66-84,121-129; config.cpp:78-86,110-134,215-224,
 562-568; kv_compression_pass.cpp:29-67)."""
 import importlib
 
@@ -38,6 +39,9 @@ def test_defaults_match_the_reference_schema():
     assert (cfg.kv_kivi.enabled, cfg.kv_kivi.bits, cfg.kv_kivi.residual_length) == (False, 8, 128)
     assert (cfg.kv_cache.type_k, cfg.kv_cache.type_v, cfg.kv_cache.size_mb) == ("f16", "f16", 0)
     assert cfg.backend == "cpu"
+    e = cfg.cuda_engine
+    assert (e.paged_kv_block_size, e.max_num_blocks, e.max_num_seqs, e.use_megakernel) == (
+        16, 0, 256, False)
     assert CF.validate(cfg) is None
     assert not cfg.paged_kivi and not cfg.compression_pass and cfg.kivi_path is None
 
@@ -49,6 +53,10 @@ def test_fp16_cache_with_the_compression_pass():
     assert CF.validate(cfg) is None
     assert cfg.kivi_path == "pass"
     assert CF.parse(FP16_PASS.replace('"cuda"', '"cpu"')).kivi_path is None
+    # built, but only the megakernel path calls it (cuda_engine.cpp:834, 1482)
+    assert not cfg.pass_runs
+    mk = CF.parse(FP16_PASS + "\n[inference.cuda_engine]\nuse_megakernel = true\n")
+    assert mk.pass_runs and CF.validate(mk) is None
 
 
 def test_paged_kivi_cache():
@@ -67,6 +75,10 @@ def test_paged_kivi_cache():
     (PAGED.replace("group_size = 128", "group_size = 96"), "group_size must be"),
     (PAGED.replace('backend = "cuda"', 'backend = "cpu"'), 'need inference.backend = "cuda"'),
     ('[inference]\nbackend = "vulkan"', "backend 'vulkan' is not recognised"),
+    (PAGED + "\n[inference.cuda_engine]\npaged_kv_block_size = 32\n",
+     "paged_kv_block_size must be 16"),
+    (PAGED + "\n[inference.cuda_engine]\nuse_megakernel = true\n",
+     "use_megakernel must be false"),
 ])
 def test_validation_messages(text, msg):
     assert msg in CF.validate(CF.parse(text))
@@ -75,6 +87,8 @@ def test_validation_messages(text, msg):
 def test_type_errors_are_reported():
     with pytest.raises(ValueError):
         CF.parse('[inference.compression.kv_kivi]\nbits = "four"')
+    with pytest.raises(ValueError):
+        CF.parse('[inference.cuda_engine]\nuse_megakernel = 1')
 
 
 def test_compression_pass_enable_rule():

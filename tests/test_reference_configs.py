@@ -5,7 +5,8 @@
   (:73-79): the per-vector KIVI pass (kv_compression_pass.cpp:29-67) with 8
   outlier channels and 16-channel groups, built whenever kv_kivi is enabled
   (cuda_engine.cpp:193-200; the file's q8_0 kv_cache types at :34-36 are not
-  read by the CUDA engine); not the paged cache.
+  read by the CUDA engine) and run because [inference.cuda_engine] sets
+  use_megakernel = true (:55); not the paged cache.
 * configs/scenario-quantized-kv.toml -- backend "cpu" (:27) with a q8_0
   [inference.kv_cache] (:36-39): the ggml CPU backend's q8_0 cache, so neither
   the pass nor the paged KIVI cache is selected.
@@ -40,6 +41,12 @@ def test_cuda_kivi_compression_selects_the_pass_with_8_outliers_g16():
         "per_channel", "per_token", True)
     assert cfg.backend == "cuda" and cfg.kivi_path == "pass"
     assert cfg.compression_pass and not cfg.paged_kivi
+    # [inference.cuda_engine] (:49-55) asks for the megakernel, the only path
+    # that calls the pass (cuda_engine.cpp:834, 1482); the reference's parser
+    # drops the key, so there the pass is built but never run
+    e = cfg.cuda_engine
+    assert (e.use_megakernel, e.paged_kv_block_size, e.max_num_seqs) == (True, 16, 4)
+    assert cfg.pass_runs
     # the KvCompressionPass mirror: outliers = residual_length, G = 16 for 4 bits
     p = CF.KvCompressionPass(cfg, n_layers=32, n_kv_heads=8, head_dim=128, block_size=16)
     assert p.enabled() and (p.n_outliers, p.group_size) == (8, 16)
@@ -53,7 +60,7 @@ def test_scenario_quantized_kv_selects_q8_0_not_this_path():
     assert CF.validate(cfg) is None
     assert (cfg.kv_cache.type_k, cfg.kv_cache.type_v, cfg.kv_cache.size_mb) == ("q8_0", "q8_0", 0)
     assert cfg.backend == "cpu" and cfg.kivi_path is None
-    assert not cfg.paged_kivi and not cfg.compression_pass
+    assert not cfg.paged_kivi and not cfg.compression_pass and not cfg.pass_runs
     assert not CF.KvCompressionPass(cfg, 32, 8, 128, 16).enabled()
 
 

@@ -1,12 +1,22 @@
 """The config switches that select this path, read the way the reference reads
-them (src/host/config/config.cpp: backend :143, parse_kv_cache :78-86, the
-kv_kivi block :215-224, validation :558-568; defaults from
-include/truellm/config_schema.h:46-50, 121-129, 204).
+them (src/host/config/config.cpp: backend :143, parse_kv_cache :78-86,
+parse_cuda_engine :110-134, the kv_kivi block :215-224, validation :558-568;
+defaults from include/truellm/config_schema.h:46-50, 66-84, 121-129, 204).
 
     [inference]                       backend: "cpu" | "ggml" | "cuda"
     [inference.compression.kv_kivi]   enabled, bits, residual_length, (group_size)
     [inference.kv_cache]              type_k / type_v: "f16" | "q8_0" | "q4_0" and,
                                       for this path, "kivi4" | "kivi2"
+    [inference.cuda_engine]           paged_kv_block_size, max_num_blocks,
+                                      max_num_seqs, use_megakernel
+
+use_megakernel is read here although the reference's parse_cuda_engine omits
+it (config.cpp:110-134; the field keeps its default, false,
+config_schema.h:80).  The KIVI pass only runs on the megakernel path (after
+the megakernel prefill, cuda_engine.cpp:834, and in inject_tokens, :1482), so
+in the reference a config that enables both (configs/cuda-kivi-compression.toml
+sets use_megakernel = true at :55) builds the pass and never runs it;
+`PathConfig.pass_runs` reports what the config asks for.
 
 Two consumers:
 * the per-vector fake-quant pass (KvCompressionPass, kv_compression_pass.cpp
@@ -52,9 +62,20 @@ class KvCacheConfig:
 
 
 @dataclass
+class CudaEngineConfig:
+    """[inference.cuda_engine] (config_schema.h:66-84): the keys this path
+    depends on."""
+    paged_kv_block_size: int = 16  # tokens per block: the KIVI pages hold 16
+    max_num_blocks: int = 0        # 0 = sized from free device memory
+    max_num_seqs: int = 256        # live sequences (ring rows of the paged cache)
+    use_megakernel: bool = False   # megakernel forward instead of the per-layer path
+
+
+@dataclass
 class PathConfig:
     kv_kivi: KiviConfig = field(default_factory=KiviConfig)
     kv_cache: KvCacheConfig = field(default_factory=KvCacheConfig)
+    cuda_engine: CudaEngineConfig = field(default_factory=CudaEngineConfig)
     backend: str = "cpu"         # inference.backend (config_schema.h:204)
 
     @property
@@ -81,8 +102,14 @@ class PathConfig:
 
     @property
     def compression_pass(self) -> bool:
-        """True when the per-vector KIVI pass runs over an fp16 cache."""
+        """True when the per-vector KIVI pass is built over an fp16 cache."""
         return self.kv_kivi.enabled and not self.paged_kivi
+
+    @property
+    def pass_runs(self) -> bool:
+        """True when the built pass is also called: only the megakernel path
+        calls it (cuda_engine.cpp:834, 1482)."""
+        return self.backend == "cuda" and self.compression_pass and self.cuda_engine.use_megakernel
 
 
 def _get(t: Mapping[str, Any], key: str, default, kind):
@@ -111,6 +138,13 @@ def parse(doc: Union[str, Path, Mapping[str, Any]]) -> PathConfig:
         cfg.kv_cache.type_k = _get(kc, "type_k", cfg.kv_cache.type_k, str)
         cfg.kv_cache.type_v = _get(kc, "type_v", cfg.kv_cache.type_v, str)
         cfg.kv_cache.size_mb = _get(kc, "size_mb", cfg.kv_cache.size_mb, int)
+    ce = inf.get("cuda_engine")
+    if ce is not None:
+        e = cfg.cuda_engine
+        e.paged_kv_block_size = _get(ce, "paged_kv_block_size", e.paged_kv_block_size, int)
+        e.max_num_blocks = _get(ce, "max_num_blocks", e.max_num_blocks, int)
+        e.max_num_seqs = _get(ce, "max_num_seqs", e.max_num_seqs, int)
+        e.use_megakernel = _get(ce, "use_megakernel", e.use_megakernel, bool)
     ki = inf.get("compression", {}).get("kv_kivi")
     if ki is not None:
         k = cfg.kv_kivi
@@ -143,6 +177,12 @@ def validate(cfg: PathConfig) -> Optional[str]:
             return "inference.compression.kv_kivi.residual_length must be >= 0"
         if cfg.backend != "cuda":
             return 'inference.kv_cache: kivi4/kivi2 need inference.backend = "cuda"'
+        if cfg.cuda_engine.paged_kv_block_size != 16:
+            return ("inference.cuda_engine.paged_kv_block_size must be 16 with "
+                    "kivi4/kivi2 (16-token pages)")
+        if cfg.cuda_engine.use_megakernel:
+            return ("inference.kv_cache: kivi4/kivi2 replace the per-layer cache and "
+                    "attention calls; inference.cuda_engine.use_megakernel must be false")
     return None
 
 
