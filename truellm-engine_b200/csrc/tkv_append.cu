@@ -13,9 +13,13 @@
 //                16-byte fragment vectors for fully written 16-token chunks.
 // Running the flush before the residual write keeps ring slots that are read
 // by (1) from being overwritten by (2) in the same call.
+#include <atomic>
+
 #include "tkv_common.cuh"
 
 namespace tkv {
+
+constexpr int kMaxAppendDevices = 64;
 
 
 __device__ __forceinline__ int nq_of(int len, int R, int G) {
@@ -506,12 +510,16 @@ __global__ void __launch_bounds__(kResThreads) residual_write_kernel(AppendArgs 
 template <int D, int BITS, int G>
 static int launch_flush_t(const AppendArgs& a, int num_seqs, cudaStream_t stream) {
   constexpr int smem = sizeof(FlushSmem<D, G>);
-  static bool attr_set = false;
-  if (!attr_set) {
+  // the attribute belongs to each device's context: set once per device
+  // (atomic flags, so concurrent host threads may call this)
+  static std::atomic<int> attr_set[kMaxAppendDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return TKV_BACKEND_ERROR;
+  if (dev < 0 || dev >= kMaxAppendDevices || !attr_set[dev].load(std::memory_order_relaxed)) {
     if (cudaFuncSetAttribute(flush_groups_kernel<D, BITS, G>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return TKV_BACKEND_ERROR;
-    attr_set = true;
+    if (dev >= 0 && dev < kMaxAppendDevices) attr_set[dev].store(1, std::memory_order_relaxed);
   }
   dim3 grid(2 * (a.max_new / G + 1), a.n_kv_heads, num_seqs);  // x: (group, K or V)
   flush_groups_kernel<D, BITS, G><<<grid, kFlushThreads, smem, stream>>>(a);
