@@ -598,7 +598,7 @@ def run_kivi(args):
     # its reduce + publish to the peers, wait + merge); otherwise one or two
     # per decode call (ops.decode_launches)
     n_launch = (3 if dec is not None and not dec.single else
-                sum(ops.decode_launches(p.w.B, p.w.Hq, p.max_ctx) for p in parts))
+                sum(ops.decode_launches(p.w.B, p.w.Hq, p.w.Hkv, p.max_ctx) for p in parts))
 
     line = None
     if rank == 0:

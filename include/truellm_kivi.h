@@ -197,10 +197,13 @@ TKV_API int tkv_decode_num_splits(int max_context_len);
  * size does not depend on max_context_len. */
 TKV_API size_t tkv_decode_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
                                   int max_context_len);
-/* Kernel launches tkv_paged_decode makes for these sizes: 1 (merge fused into
- * the decode launch) or 2 (num_seqs * num_q_heads < 1024: few, long pairs
- * whose merge runs in a separate slot-parallel launch). */
-TKV_API int tkv_decode_launches(int num_seqs, int num_q_heads, int max_context_len);
+/* Kernel launches tkv_paged_decode makes for these sizes on the current
+ * device: 1 (merge fused into the decode launch) or 2 (fewer than one
+ * (sequence, kv head) pair per 16 resident warps: pairs spread over many warps
+ * each, whose merge runs in a separate slot-parallel launch).  0 for invalid
+ * sizes (num_q_heads not a multiple of num_kv_heads included). */
+TKV_API int tkv_decode_launches(int num_seqs, int num_q_heads, int num_kv_heads,
+                                int max_context_len);
 /* Workspace bytes for tkv_paged_decode_range over splits [split_lo, split_hi)
  * (with the finer internal splits the range may use). */
 TKV_API size_t tkv_decode_range_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
@@ -215,8 +218,8 @@ TKV_API size_t tkv_decode_range_workspace_bytes(int num_seqs, int num_q_heads, i
  * equal-cost range of the call's (sequence, kv head) pages and residual
  * chunks; a pair spread over several warps is merged by log-sum-exp
  * (paged_attention_v2.cu:132-170) in the warp that finishes its last part
- * (one launch) or, when num_seqs * num_q_heads < 1024, in a second
- * slot-parallel launch (tkv_decode_launches).  Sequences longer than
+ * (one launch) or, when pairs are fewer than one per 16 resident warps, in a
+ * second slot-parallel launch (tkv_decode_launches).  Sequences longer than
  * max_context_len (or than max_blocks_per_seq pages) set TKV_ERR_BAD_LENGTH
  * in *err_flag and get a zero output row. */
 TKV_API int tkv_paged_decode(const tkv_cache_t* cache, const void* q, int q_dtype, void* out,

@@ -151,7 +151,7 @@ def test_config4_full_batch(ops, O, wl, cuda, bench):
     q = _q(wl, w, cuda)
     scale = 1 / math.sqrt(w.D)
     max_ctx = int(w.lengths.max())
-    assert ops.decode_launches(w.B, w.Hq, max_ctx) == 2
+    assert ops.decode_launches(w.B, w.Hq, w.Hkv, max_ctx) == 2
     err = torch.zeros(1, dtype=torch.int32, device=cuda)
     out = ops.paged_decode(cache, q, bt, lens, max_ctx, scale=scale, out_dtype=torch.float32,
                            err=err)
@@ -190,7 +190,7 @@ def test_config5_full_batch(ops, O, wl, cuda, bench):
         lens = torch.from_numpy(sub.lengths).to(cuda)
         q = _q(wl, sub, cuda)
         max_ctx = int(sub.lengths.max())
-        assert ops.decode_launches(sub.B, sub.Hq, max_ctx) == 1
+        assert ops.decode_launches(sub.B, sub.Hq, sub.Hkv, max_ctx) == 1
         err = torch.zeros(1, dtype=torch.int32, device=cuda)
         out = ops.paged_decode(cache, q, bt, lens, max_ctx, scale=scale,
                                out_dtype=torch.float32, err=err)

@@ -96,7 +96,7 @@ SIGNATURES = {
     "tkv_paged_decode_partials": (_i32, [C.POINTER(TkvCache), _vp, _i32, _vp, _i32, _vp, _vp,
                                          _i32, _i32, _f32, _i32, _i32, _i32, _vp, _vp, _vp,
                                          _vp, _vp]),
-    "tkv_decode_launches": (_i32, [_i32, _i32, _i32]),
+    "tkv_decode_launches": (_i32, [_i32, _i32, _i32, _i32]),
     "tkv_decode_range_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32, _i32]),
     "tkv_paged_decode_range": (_i32, [C.POINTER(TkvCache), _vp, _i32, _vp, _i32, _vp, _vp,
                                       _i32, _i32, _f32, _i32, _i32, _i32, _vp, _vp, _vp, _sz,

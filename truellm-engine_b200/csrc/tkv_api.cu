@@ -229,9 +229,11 @@ size_t tkv_decode_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
   return stream_workspace_bytes(num_seqs, num_q_heads, head_dim);
 }
 
-int tkv_decode_launches(int num_seqs, int num_q_heads, int max_context_len) {
-  if (num_seqs <= 0 || num_q_heads <= 0 || max_context_len < 0) return 0;
-  return stream_decode_launches(num_seqs, num_q_heads);
+int tkv_decode_launches(int num_seqs, int num_q_heads, int num_kv_heads, int max_context_len) {
+  if (num_seqs <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0 ||
+      max_context_len < 0)
+    return 0;
+  return stream_decode_launches(num_seqs, num_kv_heads);
 }
 
 size_t tkv_decode_range_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
@@ -581,7 +583,7 @@ int tkv_paged_decode(const tkv_cache_t* cache, const void* q, int q_dtype, void*
                              seq_slots, num_seqs, num_q_heads, scale, err_flag);
   if (st != TKV_OK) return st;
   a.max_len = max_context_len;  // longer sequences: TKV_ERR_BAD_LENGTH, zero output
-  a.mode = stream_decode_launches(num_seqs, num_q_heads) == 2 ? kStreamPartials : kStreamFused;
+  a.mode = stream_decode_launches(num_seqs, a.n_kv_heads) == 2 ? kStreamPartials : kStreamFused;
   a.out = out;
   a.out_dtype = out_dtype;
   return launch_stream_decode(a, D, cache->fmt.bits, cache->fmt.group_size, workspace,

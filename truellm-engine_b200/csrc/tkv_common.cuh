@@ -444,7 +444,7 @@ int launch_stream_decode(StreamArgs a, int head_dim, int bits, int group, void* 
                          size_t workspace_bytes, float* out_ml, cudaStream_t stream,
                          const ExPub* pub = nullptr);
 // 1 or 2: the launches tkv_paged_decode makes for these sizes.
-int stream_decode_launches(int num_seqs, int num_q_heads);
+int stream_decode_launches(int num_seqs, int num_kv_heads);
 // tkv_exchange.cu: empty partials of a GPU without splits; the wait + merge.
 int launch_ex_publish_empty(const ExPub& pub, int head_dim, cudaStream_t stream);
 int launch_ex_merge(const ExPub& pub, int head_dim, void* out, int out_dtype, int* err,

@@ -969,10 +969,29 @@ size_t stream_workspace_bytes(int num_seqs, int num_q_heads, int head_dim) {
          slot_rows * (static_cast<size_t>(head_dim) + 2) * sizeof(float);
 }
 
-int stream_decode_launches(int num_seqs, int num_q_heads) {
-  // Few pairs spread over many warps each (long contexts): a slot-parallel
-  // merge kernel beats the serial merge of one warp per pair.
-  return static_cast<long long>(num_seqs) * num_q_heads < 1024 ? 2 : 1;
+// The fused merge runs in the warp that finishes a pair's last part and reads
+// the pair's partial slots one after another; with W resident warps and P
+// (sequence, kv head) pairs a pair spans about W / P warps.  Past
+// kMaxFusedSpan slots per pair the slot-parallel merge kernel (a second
+// launch) is faster: measured on config 2's rank shares, 64 pairs take 28.9 us
+// with it and 33.4 us fused, 128 pairs 43.2 us with it and 39.9 us fused.
+constexpr int kMaxFusedSpan = 16;
+
+int stream_decode_launches(int num_seqs, int num_kv_heads) {
+  static std::atomic<int> warps[kMaxDevices];  // SMs x kWarpsPerSM, per device
+  int dev = 0, w = kStreamMaxWarps;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+    w = warps[dev].load(std::memory_order_relaxed);
+    if (w <= 0) {
+      int sms = 0;
+      w = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0
+              ? sms * kWarpsPerSM
+              : kStreamMaxWarps;
+      warps[dev].store(w, std::memory_order_relaxed);
+    }
+  }
+  const long long pairs = static_cast<long long>(num_seqs) * num_kv_heads;
+  return pairs * kMaxFusedSpan < w ? 2 : 1;
 }
 
 int launch_stream_decode(StreamArgs a, int head_dim, int bits, int group, void* workspace,

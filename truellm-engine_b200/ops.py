@@ -184,11 +184,14 @@ def decode_range_workspace_bytes(num_seqs: int, num_q_heads: int, head_dim: int,
                                                         split_lo, split_hi))
 
 
-def decode_launches(num_seqs: int, num_q_heads: int, max_context_len: int) -> int:
-    """Kernel launches one paged_decode call makes: 1 (merge fused into the
-    decode kernel), or 2 when num_seqs * num_q_heads < 1024 (a separate merge
-    kernel spreads the merge of few, long pairs over the GPU)."""
-    return int(L.lib().tkv_decode_launches(num_seqs, num_q_heads, max_context_len))
+def decode_launches(num_seqs: int, num_q_heads: int, num_kv_heads: int,
+                    max_context_len: int) -> int:
+    """Kernel launches one paged_decode call makes on the current device: 1
+    (merge fused into the decode kernel), or 2 when there is less than one
+    (sequence, kv head) pair per 16 resident warps (a separate merge kernel
+    spreads the merge of pairs that span many warps over the GPU)."""
+    return int(L.lib().tkv_decode_launches(num_seqs, num_q_heads, num_kv_heads,
+                                           max_context_len))
 
 
 def decode_num_splits(max_context_len: int) -> int:
