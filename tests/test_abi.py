@@ -51,6 +51,20 @@ def test_host_entry_points():
     assert lib.tkv_kivi_params_supported(64, 65, 16) == 0         # more outliers than channels
 
 
+def test_decode_launch_count_rule():
+    """tkv_decode_launches: 0 for invalid sizes (the q heads must split evenly
+    over the kv heads); a second, slot-parallel merge launch for pairs that
+    each span many warps (one sequence, one kv head), one launch when every
+    pair spans few (8192 pairs)."""
+    lib = L.lib()
+    assert lib.tkv_decode_launches(4, 32, 5, 100) == 0       # 32 q heads over 5 kv heads
+    assert lib.tkv_decode_launches(0, 32, 8, 100) == 0
+    assert lib.tkv_decode_launches(4, 32, 0, 100) == 0
+    assert lib.tkv_decode_launches(4, 32, 8, -1) == 0
+    assert lib.tkv_decode_launches(1, 4, 1, 131072) == 2
+    assert lib.tkv_decode_launches(1024, 32, 8, 8192) == 1
+
+
 def test_manifests():
     m = L.lib().truellm_kernel_init().contents
     assert m.abi_version == 1 and m.category == 0 and (m.min_sm_major, m.min_sm_minor) == (10, 0)
